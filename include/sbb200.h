@@ -1,0 +1,191 @@
+/*
+ * sbb200 -- B200-native routed-expert NVFP4 MoE: the C-ABI boundary.
+ *
+ * Plain C: opaque handles, plain pointers and sizes, no torch types. Device
+ * pointers are CUDA device addresses of the current device; `stream` is a
+ * cudaStream_t passed as void*. Every compute entry point is stream-ordered
+ * and never synchronises the host.
+ *
+ * Return convention (src/phase7/b70_capi.h:10 of the reference):
+ *   0 = ok, >0 = busy, <0 = error. The error text of the calling thread's
+ *   last failing call is available through sbb200_last_error().
+ *
+ * Weight layout is the reference op's (src/QuixiCore-XPU/include/quixicore/
+ * xpu/ops.hpp:269-279): w13 [E, 2I, K/2] packed e2m1 (gate rows [0, I), up
+ * rows [I, 2I), low nibble = even k), w13_scales [E, 2I, K/16] e4m3,
+ * w13_global_scales fp32 [E] (the dequant multiplier), w2 [E, K, I/2],
+ * w2_scales [E, K, I/16], w2_global_scales fp32 [E]. K is the hidden size.
+ */
+#ifndef SBB200_H
+#define SBB200_H
+
+#ifdef __cplusplus
+#include <cstddef>
+#include <cstdint>
+extern "C" {
+#else
+#include <stddef.h>
+#include <stdint.h>
+#endif
+
+#define SBB200_ABI_VERSION 1
+
+/* Activation / output dtypes; the values of the reference's DType
+ * {f32, f16, bf16} (src/QuixiCore-XPU/include/quixicore/xpu/runtime.hpp:21-27). */
+enum sbb200_dtype { SBB200_F32 = 0, SBB200_F16 = 1, SBB200_BF16 = 2 };
+
+enum sbb200_status {
+  SBB200_OK = 0,
+  SBB200_BUSY = 1,
+  SBB200_EINVAL = -1,       /* bad pointer, shape, dtype or id range */
+  SBB200_EWORKSPACE = -2,   /* workspace smaller than the size query */
+  SBB200_ECUDA = -3,        /* a CUDA runtime call failed */
+  SBB200_EUNSUPPORTED = -4, /* shape outside what the kernels implement */
+  SBB200_ENOTLOADED = -5    /* provider layer not registered */
+};
+
+/* Monotonic ABI version (src/phase7/b70_capi.h:47-52). */
+size_t sbb200_abi_version(void);
+
+/* Copy the calling thread's last error message. Returns the length needed
+ * including the NUL; writes a NUL-terminated prefix when buf is too small
+ * (src/phase7/b70_capi.h:159-172 shape). */
+size_t sbb200_last_error(char* buf, size_t size);
+
+/* ---------------------------------------------------------------------------
+ * Stateless operator: the drop-in for ops::nvfp4_moe_grouped and the PyTorch
+ * extension op nvfp4_moe (src/QuixiCore-XPU/include/quixicore/xpu/ops.hpp:
+ * 333-372, src/QuixiCore-XPU/src/dispatch/moe.cpp:80-134,
+ * src/QuixiCore-XPU/bindings/pytorch/tk_xpu_ext.sycl:296-410).
+ * ------------------------------------------------------------------------- */
+
+/* Device workspace bytes sbb200_nvfp4_moe needs for this shape
+ * (ops::nvfp4_moe_grouped_workspace_bytes, ops.hpp:363-366). */
+size_t sbb200_nvfp4_moe_workspace_bytes(size_t M, size_t E, size_t top_k, size_t K, size_t I,
+                                        int act_dt);
+
+/* out[M, K] = sum_k w[m, k] * FFN_{ids[m, k]}(hidden[m]) with
+ * FFN(x) = W2 (silu(W_gate x) * (W_up x)). hidden [M, K] in act_dt (f32, f16
+ * or bf16); topk_ids int32 [M, top_k], ids outside [0, E) are skipped (their
+ * count is kept, see sbb200_nvfp4_moe_bad_ids); topk_weights fp32 [M, top_k]
+ * (ignored when multiply_router_weight is 0). out [M, K] in out_dt (f32 like
+ * the reference op, or bf16/f16 for the model dtype); every element is
+ * written, tokens with no valid route get 0. Requires K % 32 == 0 and
+ * I % 32 == 0 (tk_xpu_ext.sycl:369-370), E <= 512, top_k <= 64.
+ * `workspace` holds >= sbb200_nvfp4_moe_workspace_bytes(...) device bytes,
+ * not preserved between calls; concurrent calls need distinct workspaces. */
+int sbb200_nvfp4_moe(void* stream, const void* hidden, const int32_t* topk_ids,
+                     const float* topk_weights, const void* w13, const void* w13_scales,
+                     const float* w13_global_scales, const void* w2, const void* w2_scales,
+                     const float* w2_global_scales, void* workspace, size_t workspace_bytes,
+                     void* out, int out_dt, size_t M, size_t E, size_t top_k, size_t K,
+                     size_t I, int act_dt, int multiply_router_weight);
+
+/* sbb200_nvfp4_moe with per-stage events, for attributing its cost (the
+ * reference's nvfp4_moe_grouped_profiled_sycl + Nvfp4MoeGroupedStages,
+ * src/QuixiCore-XPU/kernels/moe/nvfp4_moe/nvfp4_moe_kernel.hpp:53-83): the same
+ * launches in the same order, with cudaEvent_t stage_events[i] recorded on
+ * `stream` at the stage boundaries: [0] start, [1] after the route plan,
+ * [2] after gate/up + SwiGLU, [3] after the down projection, [4] after the
+ * combine. n_stage_events must be SBB200_STAGE_EVENTS; NULL entries are
+ * skipped. */
+#define SBB200_STAGE_EVENTS 5
+int sbb200_nvfp4_moe_staged(void* stream, const void* hidden, const int32_t* topk_ids,
+                            const float* topk_weights, const void* w13, const void* w13_scales,
+                            const float* w13_global_scales, const void* w2, const void* w2_scales,
+                            const float* w2_global_scales, void* workspace,
+                            size_t workspace_bytes, void* out, int out_dt, size_t M, size_t E,
+                            size_t top_k, size_t K, size_t I, int act_dt,
+                            int multiply_router_weight, void* const* stage_events,
+                            size_t n_stage_events);
+
+/* Number of ids outside [-1, E) seen by the last call that used `workspace`
+ * (device counter copied to the host; synchronises `stream`). The reference
+ * provider rejects such ids up front (src/phase1/b70_provider.cpp:1559-1566);
+ * on the device path they are dropped and counted instead. */
+int sbb200_nvfp4_moe_bad_ids(void* stream, const void* workspace, uint32_t* count);
+
+/* ---------------------------------------------------------------------------
+ * Building blocks, exported for parity tests and for callers that own the
+ * routing step. All stream-ordered.
+ * ------------------------------------------------------------------------- */
+
+/* Stable route permutation (nvfp4_moe_grouped.sycl.cpp:140-204 with the CPU
+ * tier's order, src/phase7/cpu_expert_capi.cpp:563-599): counts int32 [E],
+ * offsets int32 [E + 1], sorted int32 [M*top_k] (route ids r = m*top_k + k
+ * grouped by expert, r ascending within an expert; entries past offsets[E]
+ * are left untouched), slot_of int32 [M*top_k] (-1 for dropped ids).
+ * `scratch` needs sbb200_route_plan_scratch_bytes(M*top_k, E) bytes;
+ * `bad_ids` (uint32, may be NULL) is incremented by the count of ids outside
+ * [-1, E). */
+size_t sbb200_route_plan_scratch_bytes(size_t routes, size_t E);
+int sbb200_route_plan(void* stream, const int32_t* topk_ids, size_t M, size_t top_k, size_t E,
+                      int32_t* counts, int32_t* offsets, int32_t* sorted, int32_t* slot_of,
+                      void* scratch, uint32_t* bad_ids);
+
+/* Bit-exact NVFP4 dequant: out[r, c] = e2m1 * fp32(e4m3(sf[r, c/16]) * g[r /
+ * rows_per_scale]) (src/phase7/cpu_expert_capi.cpp:301-346). q [rows, cols/2],
+ * sf [rows, cols/16], out fp32 [rows, cols]; cols % 16 == 0. */
+int sbb200_nvfp4_dequant(void* stream, const void* q, const void* sf, const float* g,
+                         size_t rows_per_scale, float* out, size_t rows, size_t cols);
+
+/* NVFP4 quantiser with vLLM ref_nvfp4_quant semantics (the quantiser of the
+ * reference's fixtures, src/phase7/nvfp4_testutil.py): x [rows, cols] in
+ * in_dt, quantisation global gq[r / rows_per_scale] (= 448*6/amax); writes
+ * q [rows, cols/2] and sf [rows, cols/16]. */
+int sbb200_nvfp4_quantize(void* stream, const void* x, int in_dt, const float* gq,
+                          size_t rows_per_scale, void* q, void* sf, size_t rows, size_t cols);
+
+/* ---------------------------------------------------------------------------
+ * Provider: registered layers and an owned workspace, the device-resident
+ * replacement of the reference's B70 provider C-ABI (src/phase7/b70_capi.h:
+ * 44-321, src/phase1/b70_provider.hpp:86-230) without the doorbell/poller
+ * transport. Weights stay caller-owned device memory.
+ * ------------------------------------------------------------------------- */
+
+typedef struct sbb200_provider sbb200_provider_t;
+
+/* 48-byte POD, field for field the reference's sb_b70_health_t
+ * (src/phase7/b70_capi.h:28-41). */
+typedef struct sbb200_health {
+  uint64_t generation;
+  uint64_t dispatches;
+  uint64_t allocations;
+  uint64_t last_error_bytes;
+  uint32_t loaded;
+  uint32_t pending;
+  uint32_t stopped;
+  uint32_t reserved;
+} sbb200_health_t;
+
+/* Create a provider on `device` able to serve batches up to max_tokens tokens
+ * of top_k routes for layers of at most max_E experts, hidden K and
+ * intermediate I. Allocates its workspace once. NULL on failure. */
+sbb200_provider_t* sbb200_create(int device, size_t max_tokens, size_t top_k, size_t max_E,
+                                 size_t K, size_t I);
+void sbb200_destroy(sbb200_provider_t* p);
+
+/* Register layer `layer`'s device weights (pointers are kept, not copied). */
+int sbb200_register_layer(sbb200_provider_t* p, size_t layer, size_t E, const void* w13,
+                          const void* w13_scales, const float* w13_global_scales,
+                          const void* w2, const void* w2_scales,
+                          const float* w2_global_scales);
+
+/* Routed-expert forward of a registered layer on `stream` (the issue step of
+ * src/phase1/b70_provider.cpp:1530-1849 without the host copies). M must be
+ * <= max_tokens; ids outside [-1, E) are dropped and counted in health. */
+int sbb200_moe_forward(sbb200_provider_t* p, size_t layer, void* stream, const void* hidden,
+                       int act_dt, const int32_t* topk_ids, const float* topk_weights,
+                       void* out, int out_dt, size_t M, int multiply_router_weight);
+
+/* Health snapshot + last error copy-out (src/phase7/b70_capi.h:159-172):
+ * 0 ok, -1 invalid arguments, -2 buffer too small (truncated copy written,
+ * last_error_bytes holds the size needed). */
+int sbb200_health(sbb200_provider_t* p, sbb200_health_t* health, char* last_error,
+                  size_t last_error_size);
+
+#ifdef __cplusplus
+}
+#endif
+
+#endif /* SBB200_H */

@@ -1,0 +1,49 @@
+// Host-side launch entry points of the device kernels (internal to the
+// library; the public surface is include/sbb200.h).
+#pragma once
+
+#include <cuda_runtime.h>
+#include <stddef.h>
+#include <stdint.h>
+
+namespace sbb {
+
+constexpr int kRouteChunk = 4096;  // routes per CTA in the route plan
+constexpr int kMaxExperts = 512;   // route-plan shared-memory bound
+constexpr int kMaxTopK = 64;
+
+size_t route_plan_chunks(int64_t R);
+size_t route_scatter_smem(int E);
+
+cudaError_t launch_route_plan(const int32_t* ids, int64_t R, int E, int32_t* chunk_counts,
+                              int32_t* counts, int32_t* offsets, int32_t* sorted,
+                              int32_t* slot_of, uint32_t* status, cudaStream_t stream);
+
+// CUDA-core grouped expert kernels: any K, I that are multiples of 32.
+// h: fp32 [R, I] in sorted-slot order; y: fp32 [R, K] (global scale applied,
+// router weight not applied).
+cudaError_t launch_gateup_simt(const void* hidden, int act_dt, int top_k, const uint8_t* w13,
+                               const uint8_t* s13, const float* g13, const int32_t* counts,
+                               const int32_t* offsets, const int32_t* sorted, float* h, int E,
+                               int K, int I, cudaStream_t stream);
+cudaError_t launch_down_simt(const float* h, const uint8_t* w2, const uint8_t* s2,
+                             const float* g2, const int32_t* counts, const int32_t* offsets,
+                             float* y, int E, int K, int I, cudaStream_t stream);
+
+// out[t, :] = sum over valid k of w[t, k] * y[slot_of[t*top_k + k], :], k ascending.
+cudaError_t launch_combine(const float* y, const int32_t* slot_of, const float* weights,
+                           int multiply_router_weight, void* out, int out_dt, int64_t M,
+                           int top_k, int K, cudaStream_t stream);
+
+// Bit-exact NVFP4 dequant: out[r, c] = e2m1 * fp32(e4m3 * g[r / rows_per_scale]).
+cudaError_t launch_dequant(const uint8_t* q, const uint8_t* sf, const float* g,
+                           int64_t rows_per_scale, float* out, int64_t rows, int64_t cols,
+                           cudaStream_t stream);
+
+// NVFP4 quantiser (vLLM ref_nvfp4_quant semantics) of a [rows, cols] matrix in
+// dtype in_dt with per-group quantisation global gq[r / rows_per_scale].
+cudaError_t launch_quantize(const void* x, int in_dt, const float* gq, int64_t rows_per_scale,
+                            uint8_t* q, uint8_t* sf, int64_t rows, int64_t cols,
+                            cudaStream_t stream);
+
+}  // namespace sbb

@@ -1,0 +1,76 @@
+// Kernel-choice driver: route plan -> gate/up + SwiGLU -> down -> combine.
+#include "moe_driver.h"
+
+#include "kernels.h"
+
+namespace sbb {
+
+namespace {
+inline size_t align_up(size_t v, size_t a) { return (v + a - 1) / a * a; }
+}  // namespace
+
+size_t route_plan_scratch_bytes(size_t routes, size_t E) {
+  return 256 + align_up(route_plan_chunks((int64_t)routes) * E * sizeof(int32_t), 256);
+}
+
+WorkspacePlan plan_workspace(size_t M, size_t E, size_t top_k, size_t K, size_t I) {
+  const size_t R = M * top_k;
+  WorkspacePlan p{};
+  size_t at = 0;
+  auto take = [&](size_t bytes) {
+    const size_t here = at;
+    at = align_up(at + bytes, 256);
+    return here;
+  };
+  p.status = take(256);
+  p.chunk_counts = take(route_plan_chunks((int64_t)R) * E * sizeof(int32_t));
+  p.counts = take(E * sizeof(int32_t));
+  p.offsets = take((E + 1) * sizeof(int32_t));
+  p.sorted = take(R * sizeof(int32_t));
+  p.slot_of = take(R * sizeof(int32_t));
+  p.h = take(R * I * sizeof(float));
+  p.y = take(R * K * sizeof(float));
+  p.total = at;
+  return p;
+}
+
+cudaError_t run_moe(const MoeArgs& a, const WorkspacePlan& plan, void* workspace,
+                    cudaStream_t stream, std::string* why) {
+  char* ws = static_cast<char*>(workspace);
+  auto* status = reinterpret_cast<uint32_t*>(ws + plan.status);
+  auto* chunk_counts = reinterpret_cast<int32_t*>(ws + plan.chunk_counts);
+  auto* counts = reinterpret_cast<int32_t*>(ws + plan.counts);
+  auto* offsets = reinterpret_cast<int32_t*>(ws + plan.offsets);
+  auto* sorted = reinterpret_cast<int32_t*>(ws + plan.sorted);
+  auto* slot_of = reinterpret_cast<int32_t*>(ws + plan.slot_of);
+  auto* h = reinterpret_cast<float*>(ws + plan.h);
+  auto* y = reinterpret_cast<float*>(ws + plan.y);
+  const int64_t R = a.M * a.top_k;
+  auto mark = [&](int i) -> cudaError_t {
+    if (!a.stage_events || !a.stage_events[i]) return cudaSuccess;
+    return cudaEventRecord(static_cast<cudaEvent_t>(a.stage_events[i]), stream);
+  };
+
+  cudaError_t err = mark(0);
+  if (err != cudaSuccess) { *why = "stage event"; return err; }
+  err = cudaMemsetAsync(status, 0, 256, stream);
+  if (err != cudaSuccess) { *why = "status clear"; return err; }
+  err = launch_route_plan(a.ids, R, a.E, chunk_counts, counts, offsets, sorted, slot_of, status,
+                          stream);
+  if (err != cudaSuccess) { *why = "route plan"; return err; }
+  if ((err = mark(1)) != cudaSuccess) { *why = "stage event"; return err; }
+  err = launch_gateup_simt(a.hidden, a.act_dt, a.top_k, a.w13, a.s13, a.g13, counts, offsets,
+                           sorted, h, a.E, a.K, a.I, stream);
+  if (err != cudaSuccess) { *why = "gate/up"; return err; }
+  if ((err = mark(2)) != cudaSuccess) { *why = "stage event"; return err; }
+  err = launch_down_simt(h, a.w2, a.s2, a.g2, counts, offsets, y, a.E, a.K, a.I, stream);
+  if (err != cudaSuccess) { *why = "down"; return err; }
+  if ((err = mark(3)) != cudaSuccess) { *why = "stage event"; return err; }
+  err = launch_combine(y, slot_of, a.weights, a.multiply_router_weight, a.out, a.out_dt, a.M,
+                       a.top_k, a.K, stream);
+  if (err != cudaSuccess) { *why = "combine"; return err; }
+  if ((err = mark(4)) != cudaSuccess) { *why = "stage event"; return err; }
+  return cudaSuccess;
+}
+
+}  // namespace sbb

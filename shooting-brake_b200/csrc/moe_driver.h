@@ -1,0 +1,55 @@
+// Workspace plan and kernel-choice driver for one routed-expert MoE call.
+#pragma once
+
+#include <cuda_runtime.h>
+#include <stddef.h>
+#include <stdint.h>
+
+#include <string>
+
+namespace sbb {
+
+constexpr size_t kStatusOffset = 0;  // uint32 status words at the workspace start
+
+// Byte offsets of each region inside the caller's workspace. The size query
+// and the launcher both derive them from plan_workspace, so they cannot drift
+// (the reference's plan_workspace rule, nvfp4_moe_grouped.sycl.cpp:92-130).
+struct WorkspacePlan {
+  size_t status;        // uint32[64]: [0] ids outside [-1, E)
+  size_t chunk_counts;  // int32[nchunks * E]
+  size_t counts;        // int32[E]
+  size_t offsets;       // int32[E + 1]
+  size_t sorted;        // int32[R]   route id per sorted slot
+  size_t slot_of;       // int32[R]   sorted slot per route, -1 if dropped
+  size_t h;             // fp32[R, I] SwiGLU activations per slot
+  size_t y;             // fp32[R, K] down-projection output per slot
+  size_t total;
+};
+
+WorkspacePlan plan_workspace(size_t M, size_t E, size_t top_k, size_t K, size_t I);
+size_t route_plan_scratch_bytes(size_t routes, size_t E);
+
+struct MoeArgs {
+  const void* hidden;
+  int act_dt;
+  const int32_t* ids;
+  const float* weights;
+  int multiply_router_weight;
+  const uint8_t *w13, *s13, *w2, *s2;
+  const float *g13, *g2;
+  void* out;
+  int out_dt;
+  int64_t M;
+  int E, top_k, K, I;
+  void* const* stage_events;  // optional cudaEvent_t[SBB200_STAGE_EVENTS]
+};
+
+int validate_shape(size_t M, size_t E, size_t top_k, size_t K, size_t I, int act_dt, int out_dt,
+                   std::string* why);
+
+// Enqueue the whole forward on `stream`. On failure returns the CUDA error and
+// names the failing step in *why.
+cudaError_t run_moe(const MoeArgs& a, const WorkspacePlan& plan, void* workspace,
+                    cudaStream_t stream, std::string* why);
+
+}  // namespace sbb

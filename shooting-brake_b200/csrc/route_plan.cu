@@ -1,0 +1,194 @@
+// Route permutation: histogram of routes per expert, exclusive scan, and a
+// STABLE scatter, so the routes of one expert appear in ascending
+// route index r = token * top_k + k.
+//
+// This is the device form of the reference's grouping step
+// (src/QuixiCore-XPU/kernels/moe/nvfp4_moe/variants/xpu_sycl/
+// nvfp4_moe_grouped.sycl.cpp:140-204: histogram -> scan -> scatter) with the
+// order of its CPU tier (src/phase7/cpu_expert_capi.cpp:563-599), where the
+// grouped SYCL kernel's atomics would leave the order nondeterministic.
+// Ids outside [0, E) are dropped (nvfp4_moe.sycl.cpp:139-141); ids outside
+// [-1, E) are also counted into status[0] so the caller can surface them.
+//
+// Layout: routes are split into chunks of kRouteChunk. Pass 1 writes one
+// per-expert count row per chunk. Pass 2 (one CTA per chunk) derives each
+// expert's global offset and the chunk's base within the expert from those
+// rows, then ranks its routes in order with warp match masks. With a single
+// chunk, pass 2 computes the histogram itself and pass 1 is skipped.
+#include "common.cuh"
+#include "kernels.h"
+
+namespace sbb {
+
+namespace {
+
+constexpr int kThreads = 1024;
+constexpr int kWarps = kThreads / 32;
+
+__device__ __forceinline__ bool valid_id(int32_t e, int E) { return e >= 0 && e < E; }
+
+__global__ void __launch_bounds__(kThreads) route_hist_kernel(
+    const int32_t* __restrict__ ids, int64_t R, int E, int32_t* __restrict__ chunk_counts,
+    uint32_t* __restrict__ status) {
+  extern __shared__ int32_t s_hist[];
+  for (int e = threadIdx.x; e < E; e += kThreads) s_hist[e] = 0;
+  __syncthreads();
+  const int64_t begin = (int64_t)blockIdx.x * kRouteChunk;
+  const int64_t end = min(begin + (int64_t)kRouteChunk, R);
+  uint32_t bad = 0;
+  for (int64_t r = begin + threadIdx.x; r < end; r += kThreads) {
+    const int32_t e = ids[r];
+    if (valid_id(e, E)) {
+      atomicAdd(&s_hist[e], 1);
+    } else if (e != -1) {
+      ++bad;
+    }
+  }
+  if (bad) atomicAdd(&status[0], bad);
+  __syncthreads();
+  for (int e = threadIdx.x; e < E; e += kThreads)
+    chunk_counts[(int64_t)blockIdx.x * E + e] = s_hist[e];
+}
+
+// Shared memory: base[E] (chunk base, then running cursor), offs[E + 1],
+// warp_cnt[kWarps * E].
+__global__ void __launch_bounds__(kThreads) route_scatter_kernel(
+    const int32_t* __restrict__ ids, int64_t R, int E, int nchunks,
+    const int32_t* __restrict__ chunk_counts, int32_t* __restrict__ counts,
+    int32_t* __restrict__ offsets, int32_t* __restrict__ sorted,
+    int32_t* __restrict__ slot_of, uint32_t* __restrict__ status) {
+  extern __shared__ int32_t smem[];
+  int32_t* s_base = smem;                // [E]
+  int32_t* s_offs = s_base + E;          // [E + 1]
+  int32_t* s_wcnt = s_offs + (E + 1);    // [kWarps * E]
+  const int tid = threadIdx.x;
+  const int warp = tid >> 5;
+  const int lane = tid & 31;
+  const int c = blockIdx.x;
+  const int64_t begin = (int64_t)c * kRouteChunk;
+  const int64_t end = min(begin + (int64_t)kRouteChunk, R);
+
+  // 1. per-expert totals and this chunk's base.
+  if (nchunks == 1) {
+    for (int e = tid; e < E; e += kThreads) s_base[e] = 0;
+    __syncthreads();
+    uint32_t bad = 0;
+    for (int64_t r = begin + tid; r < end; r += kThreads) {
+      const int32_t e = ids[r];
+      if (valid_id(e, E)) atomicAdd(&s_base[e], 1);
+      else if (e != -1) ++bad;
+    }
+    if (bad) atomicAdd(&status[0], bad);
+    __syncthreads();
+    for (int e = tid; e < E; e += kThreads) {
+      s_offs[e + 1] = s_base[e];  // total
+      s_base[e] = 0;              // chunk base within the expert
+    }
+  } else {
+    for (int e = tid; e < E; e += kThreads) {
+      int32_t before = 0, total = 0;
+      for (int cc = 0; cc < nchunks; ++cc) {
+        const int32_t v = chunk_counts[(int64_t)cc * E + e];
+        before += cc < c ? v : 0;
+        total += v;
+      }
+      s_base[e] = before;
+      s_offs[e + 1] = total;
+    }
+  }
+  __syncthreads();
+  // 2. exclusive scan of totals (E is small: one warp walks it in 32-wide
+  //    steps with a shuffle scan per step).
+  if (warp == 0) {
+    int32_t carry = 0;
+    for (int e0 = 0; e0 < E; e0 += 32) {
+      const int e = e0 + lane;
+      int32_t v = e < E ? s_offs[e + 1] : 0;
+      for (int d = 1; d < 32; d <<= 1) {
+        const int32_t n = __shfl_up_sync(0xffffffffu, v, d);
+        if (lane >= d) v += n;
+      }
+      if (e < E) s_offs[e + 1] = carry + v;
+      carry += __shfl_sync(0xffffffffu, v, 31);
+    }
+    if (lane == 0) s_offs[0] = 0;
+  }
+  __syncthreads();
+  if (c == 0) {
+    for (int e = tid; e < E; e += kThreads) {
+      counts[e] = s_offs[e + 1] - s_offs[e];
+      offsets[e] = s_offs[e];
+    }
+    if (tid == 0) offsets[E] = s_offs[E];
+  }
+  // 3. stable ranks, 1024 routes per step.
+  for (int64_t step = begin; step < end; step += kThreads) {
+    for (int i = tid; i < kWarps * E; i += kThreads) s_wcnt[i] = 0;
+    __syncthreads();
+    const int64_t r = step + tid;
+    const int32_t e = r < end ? ids[r] : -1;
+    const bool ok = r < end && valid_id(e, E);
+    const uint32_t active = __ballot_sync(0xffffffffu, ok);
+    uint32_t peers = __match_any_sync(0xffffffffu, ok ? e : -1);
+    peers &= active;
+    const int rank_in_warp = __popc(peers & lanemask_lt());
+    if (ok && rank_in_warp == 0) s_wcnt[warp * E + e] = __popc(peers);
+    __syncthreads();
+    int32_t slot = -1;
+    if (ok) {
+      int32_t before = 0;
+      for (int w = 0; w < warp; ++w) before += s_wcnt[w * E + e];
+      slot = s_offs[e] + s_base[e] + before + rank_in_warp;
+    }
+    __syncthreads();  // every thread has read s_base before it advances
+    for (int x = tid; x < E; x += kThreads) {
+      int32_t add = 0;
+      for (int w = 0; w < kWarps; ++w) add += s_wcnt[w * E + x];
+      s_base[x] += add;
+    }
+    if (r < end) {
+      slot_of[r] = slot;
+      if (ok) sorted[slot] = (int32_t)r;
+    }
+    __syncthreads();
+  }
+}
+
+}  // namespace
+
+size_t route_plan_chunks(int64_t R) { return (size_t)((R + kRouteChunk - 1) / kRouteChunk); }
+
+size_t route_scatter_smem(int E) { return sizeof(int32_t) * ((size_t)E + (E + 1) + (size_t)kWarps * E); }
+
+cudaError_t launch_route_plan(const int32_t* ids, int64_t R, int E, int32_t* chunk_counts,
+                              int32_t* counts, int32_t* offsets, int32_t* sorted,
+                              int32_t* slot_of, uint32_t* status, cudaStream_t stream) {
+  const int nchunks = (int)route_plan_chunks(R);
+  if (nchunks == 0) {
+    // No routes: counts and offsets are all zero.
+    cudaError_t err = cudaMemsetAsync(counts, 0, sizeof(int32_t) * E, stream);
+    if (err != cudaSuccess) return err;
+    return cudaMemsetAsync(offsets, 0, sizeof(int32_t) * (E + 1), stream);
+  }
+  const size_t smem = route_scatter_smem(E);
+  int dev = 0;
+  cudaError_t err = cudaGetDevice(&dev);
+  if (err != cudaSuccess) return err;
+  static bool attr_set[64] = {};
+  if (dev >= 0 && dev < 64 && !attr_set[dev]) {
+    err = cudaFuncSetAttribute(route_scatter_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                               (int)route_scatter_smem(kMaxExperts));
+    if (err != cudaSuccess) return err;
+    attr_set[dev] = true;
+  }
+  if (nchunks > 1) {
+    route_hist_kernel<<<nchunks, kThreads, sizeof(int32_t) * E, stream>>>(ids, R, E, chunk_counts,
+                                                                          status);
+  }
+  route_scatter_kernel<<<nchunks, kThreads, smem, stream>>>(ids, R, E, nchunks, chunk_counts,
+                                                            counts, offsets, sorted, slot_of,
+                                                            status);
+  return cudaGetLastError();
+}
+
+}  // namespace sbb

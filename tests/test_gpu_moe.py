@@ -1,0 +1,163 @@
+"""Routed-expert forward on the B200 vs the reference's expert path.
+
+Tolerance: max relative error <= 1e-2, measured as
+max|got - want| / max|want|, and cosine >= 0.9999 against the fp32-accumulated
+reference result."""
+
+from __future__ import annotations
+
+import numpy as np
+import pytest
+import torch
+
+from conftest import cosine, golden, rel_err
+from gpu_util import dev, layer_to, run_moe
+
+pytestmark = pytest.mark.gpu
+
+REL_TOL = 1e-2
+COS_TOL = 0.9999
+
+
+def check(got, want):
+    assert rel_err(got, want) <= REL_TOL, rel_err(got, want)
+    assert cosine(got, want) >= COS_TOL, cosine(got, want)
+
+
+@pytest.mark.parametrize("kind", ["moe", "blocks"])
+def test_known_answer_fixture(sbb, oracle, cuda, kind):
+    fx = oracle.kat_fixture(kind)
+    gold = golden(f"kat_{kind}.npz")
+    got = run_moe(sbb, fx["hidden"], fx["ids"], fx["weights"], fx["layer"], cuda)
+    check(got, gold["out_ref"])
+    # the reference device test's own bound on a bf16 path (xpu_ops_smoke.cpp:2383-2385)
+    assert np.abs(got - gold["out_loop"]).max() <= 2.0 ** -8 * np.abs(gold["out_loop"]).max()
+    routed = (fx["ids"] >= 0).any(axis=1)
+    assert np.all(np.abs(got[routed]).max(axis=1) > 0)
+
+
+def test_config0_golden(sbb, oracle, cuda):
+    E, K, I, T, top_k = 16, 1024, 512, 64, 2
+    L = oracle.make_layer(E, K, I, seed=0)
+    hidden = oracle.make_hidden(T, K, seed=1)
+    ids, w = oracle.route_logits(T, E, top_k, seed=2)
+    got = run_moe(sbb, hidden, ids, w, L, cuda)
+    check(got, golden("c0.npz")["out_ref"])
+
+
+@pytest.mark.parametrize("E,K,I,T,top_k", [
+    (8, 256, 64, 1, 1), (8, 256, 96, 13, 3), (32, 512, 256, 40, 4), (16, 1024, 512, 200, 2),
+    (170, 1024, 256, 64, 8), (64, 2048, 768, 100, 6),
+])
+def test_random_shapes_vs_oracle(sbb, oracle, cuda, E, K, I, T, top_k):
+    seed = E * 7 + K + I + T
+    L = oracle.make_layer(E, K, I, seed=seed)
+    hidden = oracle.make_hidden(T, K, seed=seed + 1)
+    ids, w = oracle.route_logits(T, E, top_k, seed=seed + 2)
+    ids[0, 0] = -1
+    got = run_moe(sbb, hidden, ids, w, L, cuda)
+    check(got, oracle.moe_forward(hidden, ids, w, L))
+
+
+@pytest.mark.parametrize("act", [torch.float32, torch.float16, torch.bfloat16])
+@pytest.mark.parametrize("out_dtype", [torch.float32, torch.bfloat16])
+def test_dtypes(sbb, oracle, cuda, act, out_dtype):
+    E, K, I, T, top_k = 12, 512, 128, 24, 3
+    L = oracle.make_layer(E, K, I, seed=21)
+    hidden = oracle.make_hidden(T, K, seed=22)
+    ids, w = oracle.route_logits(T, E, top_k, seed=23)
+    got = run_moe(sbb, hidden, ids, w, L, cuda, act=act, out_dtype=out_dtype)
+    want = oracle.moe_forward(hidden, ids, w, L)
+    check(got, want)
+
+
+def test_multiply_router_weight_off(sbb, oracle, cuda):
+    E, K, I, T, top_k = 8, 256, 64, 10, 2
+    L = oracle.make_layer(E, K, I, seed=31)
+    hidden = oracle.make_hidden(T, K, seed=32)
+    ids, w = oracle.route_logits(T, E, top_k, seed=33)
+    got = run_moe(sbb, hidden, ids, w, L, cuda, multiply_router_weight=False)
+    check(got, oracle.moe_forward(hidden, ids, w, L, multiply_router_weight=False))
+
+
+def test_duplicate_experts_and_empty_tokens(sbb, oracle, cuda):
+    E, K, I, T, top_k = 8, 256, 64, 12, 4
+    L = oracle.make_layer(E, K, I, seed=41)
+    hidden = oracle.make_hidden(T, K, seed=42)
+    ids = np.array([[1, 1, 1, 1]] * 4 + [[-1, -1, -1, -1]] * 4 + [[0, 7, 7, -1]] * 4, np.int32)
+    w = np.full((T, top_k), 0.25, np.float32)
+    got = run_moe(sbb, hidden, ids, w, L, cuda)
+    want = oracle.moe_forward(hidden, ids, w, L)
+    check(got, want)
+    assert np.all(got[4:8] == 0)
+
+
+def test_out_of_range_ids_are_dropped_and_counted(sbb, oracle, cuda):
+    E, K, I, T, top_k = 8, 256, 64, 6, 2
+    L = oracle.make_layer(E, K, I, seed=51)
+    hidden = oracle.make_hidden(T, K, seed=52)
+    ids, w = oracle.route_logits(T, E, top_k, seed=53)
+    ids[1, 0] = E
+    ids[2, 1] = -4
+    got = run_moe(sbb, hidden, ids, w, L, cuda)
+    check(got, oracle.moe_forward(hidden, ids, w, L))
+    assert sbb.nvfp4_moe_bad_ids(cuda) == 2
+
+
+def test_custom_op_and_validation(sbb, oracle, cuda):
+    L = oracle.make_layer(4, 256, 64, seed=61)
+    hidden = dev(oracle.make_hidden(3, 256, seed=62), cuda, torch.bfloat16)
+    ids = torch.zeros((3, 2), dtype=torch.int32, device=cuda)
+    w = torch.full((3, 2), 0.5, device=cuda)
+    tensors = layer_to(L, cuda)
+    out = torch.ops.sbb200.nvfp4_moe(hidden, ids, w, *tensors, True, 0)
+    assert out.shape == (3, 256) and out.dtype == torch.float32
+    with pytest.raises(ValueError, match="topk ids must be int32"):
+        sbb.nvfp4_moe(hidden, ids.long(), w, *tensors)
+    with pytest.raises(ValueError, match="w2 must be byte"):
+        sbb.nvfp4_moe(hidden, ids, w, *tensors[:3], tensors[3][:, :128], *tensors[4:])
+    with pytest.raises(ValueError, match="CUDA tensor"):
+        sbb.nvfp4_moe(hidden.cpu(), ids, w, *tensors)
+
+
+def test_provider_forward_and_health(sbb, oracle, cuda):
+    E, K, I, T, top_k = 16, 512, 128, 20, 4
+    L = oracle.make_layer(E, K, I, seed=71)
+    hidden = oracle.make_hidden(T, K, seed=72)
+    ids, w = oracle.route_logits(T, E, top_k, seed=73)
+    p = sbb.Provider(0, max_tokens=32, top_k=top_k, max_E=E, K=K, I=I)
+    tensors = layer_to(L, cuda)
+    p.register_layer(3, *tensors)
+    out = p.forward(3, dev(hidden, cuda, torch.bfloat16), dev(ids, cuda), dev(w, cuda))
+    torch.cuda.synchronize()
+    check(out.cpu().numpy(), oracle.moe_forward(hidden, ids, w, L))
+    h, err = p.health()
+    assert h["dispatches"] == 1 and h["loaded"] == 1
+    with pytest.raises(sbb.Sbb200Error):
+        p.forward(9, dev(hidden, cuda, torch.bfloat16), dev(ids, cuda), dev(w, cuda))
+    h, err = p.health()
+    assert "not registered" in err
+    p.close()
+
+
+def test_cuda_graph_replay(sbb, oracle, cuda):
+    E, K, I, T, top_k = 16, 512, 128, 8, 4
+    L = oracle.make_layer(E, K, I, seed=81)
+    hidden = oracle.make_hidden(T, K, seed=82)
+    ids, w = oracle.route_logits(T, E, top_k, seed=83)
+    tensors = layer_to(L, cuda)
+    h = dev(hidden, cuda, torch.bfloat16)
+    i = dev(ids, cuda)
+    ww = dev(w, cuda)
+    s = torch.cuda.Stream()
+    with torch.cuda.stream(s):
+        sbb.nvfp4_moe(h, i, ww, *tensors)  # eager call sizes the workspace
+        g = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(g, stream=s):
+            out = sbb.nvfp4_moe(h, i, ww, *tensors)
+    ids2, w2 = oracle.route_logits(T, E, top_k, seed=84)
+    i.copy_(dev(ids2, cuda))
+    ww.copy_(dev(w2, cuda))
+    g.replay()
+    torch.cuda.synchronize()
+    check(out.cpu().numpy(), oracle.moe_forward(hidden, ids2, w2, L))
