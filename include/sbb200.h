@@ -105,6 +105,13 @@ int sbb200_nvfp4_moe_staged(void* stream, const void* hidden, const int32_t* top
  * on the device path they are dropped and counted instead. */
 int sbb200_nvfp4_moe_bad_ids(void* stream, const void* workspace, uint32_t* count);
 
+/* Device-side error word of the last call that used `workspace` (synchronises
+ * `stream`): bit 0 = a pipeline wait inside a tcgen05 kernel passed its
+ * deadline and the kernel abandoned its work (the result is not valid). The
+ * reference's poller counts failed dispatches the same way instead of
+ * hanging (src/phase7/b70_capi.h:189-193). */
+int sbb200_nvfp4_moe_device_errors(void* stream, const void* workspace, uint32_t* errors);
+
 /* ---------------------------------------------------------------------------
  * Building blocks, exported for parity tests and for callers that own the
  * routing step. All stream-ordered.

@@ -71,6 +71,8 @@ def lib() -> ctypes.CDLL:
                                               S, I, I, P, S]
         L.sbb200_nvfp4_moe_bad_ids.restype = I
         L.sbb200_nvfp4_moe_bad_ids.argtypes = [P, P, P]
+        L.sbb200_nvfp4_moe_device_errors.restype = I
+        L.sbb200_nvfp4_moe_device_errors.argtypes = [P, P, P]
         L.sbb200_route_plan_scratch_bytes.restype = S
         L.sbb200_route_plan_scratch_bytes.argtypes = [S, S]
         L.sbb200_route_plan.restype = I
@@ -292,6 +294,19 @@ def nvfp4_moe_bad_ids(device: torch.device | None = None) -> int:
         return 0
     v = ctypes.c_uint32(0)
     _check(lib().sbb200_nvfp4_moe_bad_ids(key[1], _p(ws), ctypes.addressof(v)))
+    return int(v.value)
+
+
+def nvfp4_moe_device_errors(device: torch.device | None = None) -> int:
+    """Device error word of the last nvfp4_moe call on the current stream of
+    ``device`` (bit 0: a kernel wait passed its deadline; synchronises)."""
+    device = device or torch.device("cuda", torch.cuda.current_device())
+    key = (device.index or 0, torch.cuda.current_stream(device).cuda_stream)
+    ws = _workspaces.get(key)
+    if ws is None:
+        return 0
+    v = ctypes.c_uint32(0)
+    _check(lib().sbb200_nvfp4_moe_device_errors(key[1], _p(ws), ctypes.addressof(v)))
     return int(v.value)
 
 

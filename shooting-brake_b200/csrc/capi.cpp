@@ -166,6 +166,18 @@ int sbb200_nvfp4_moe_bad_ids(void* stream, const void* workspace, uint32_t* coun
   return SBB200_OK;
 }
 
+int sbb200_nvfp4_moe_device_errors(void* stream, const void* workspace, uint32_t* errors) {
+  if (!workspace || !errors) return fail(SBB200_EINVAL, "device_errors received a null pointer");
+  const uint32_t* status = reinterpret_cast<const uint32_t*>(
+      static_cast<const char*>(workspace) + sbb::kStatusOffset);
+  cudaStream_t s = static_cast<cudaStream_t>(stream);
+  cudaError_t err =
+      cudaMemcpyAsync(errors, status + 1, sizeof(uint32_t), cudaMemcpyDeviceToHost, s);
+  if (err == cudaSuccess) err = cudaStreamSynchronize(s);
+  if (err != cudaSuccess) return cuda_fail(err, "device_errors");
+  return SBB200_OK;
+}
+
 size_t sbb200_route_plan_scratch_bytes(size_t routes, size_t E) {
   return sbb::route_plan_scratch_bytes(routes, E);
 }

@@ -28,6 +28,8 @@ WorkspacePlan plan_workspace(size_t M, size_t E, size_t top_k, size_t K, size_t 
   p.offsets = take((E + 1) * sizeof(int32_t));
   p.sorted = take(R * sizeof(int32_t));
   p.slot_of = take(R * sizeof(int32_t));
+  p.xperm = take(R * K * 2);
+  p.xscale = take(R * sizeof(float));
   p.h = take(R * I * sizeof(float));
   p.y = take(R * K * sizeof(float));
   p.total = at;
@@ -58,14 +60,53 @@ cudaError_t run_moe(const MoeArgs& a, const WorkspacePlan& plan, void* workspace
   err = launch_route_plan(a.ids, R, a.E, chunk_counts, counts, offsets, sorted, slot_of, status,
                           stream);
   if (err != cudaSuccess) { *why = "route plan"; return err; }
-  if ((err = mark(1)) != cudaSuccess) { *why = "stage event"; return err; }
-  err = launch_gateup_simt(a.hidden, a.act_dt, a.top_k, a.w13, a.s13, a.g13, counts, offsets,
-                           sorted, h, a.E, a.K, a.I, stream);
-  if (err != cudaSuccess) { *why = "gate/up"; return err; }
-  if ((err = mark(2)) != cudaSuccess) { *why = "stage event"; return err; }
-  err = launch_down_simt(h, a.w2, a.s2, a.g2, counts, offsets, y, a.E, a.K, a.I, stream);
-  if (err != cudaSuccess) { *why = "down"; return err; }
-  if ((err = mark(3)) != cudaSuccess) { *why = "stage event"; return err; }
+  if (tc_supported(a.K, a.I, a.act_dt)) {
+    TcLaunch t{};
+    t.hidden = a.hidden;
+    t.act_dt = a.act_dt;
+    t.counts = counts;
+    t.offsets = offsets;
+    t.sorted = sorted;
+    t.w13 = a.w13;
+    t.s13 = a.s13;
+    t.w2 = a.w2;
+    t.s2 = a.s2;
+    t.g13 = a.g13;
+    t.g2 = a.g2;
+    t.xperm = ws + plan.xperm;
+    t.xscale = reinterpret_cast<float*>(ws + plan.xscale);
+    t.h = h;
+    t.y = y;
+    t.status = status;
+    t.R = R;
+    t.E = a.E;
+    t.top_k = a.top_k;
+    t.K = a.K;
+    t.I = a.I;
+    struct Ctx {
+      void* const* ev;
+      cudaStream_t s;
+    } ctx{a.stage_events, stream};
+    if (a.stage_events) {
+      t.stage_mark = [](void* c, int i) {
+        auto* x = static_cast<Ctx*>(c);
+        if (x->ev[i]) cudaEventRecord(static_cast<cudaEvent_t>(x->ev[i]), x->s);
+      };
+      t.stage_ctx = &ctx;
+    }
+    const char* step = "tcgen05 path";
+    err = launch_moe_tc(t, stream, &step);
+    if (err != cudaSuccess) { *why = step; return err; }
+  } else {
+    if ((err = mark(1)) != cudaSuccess) { *why = "stage event"; return err; }
+    err = launch_gateup_simt(a.hidden, a.act_dt, a.top_k, a.w13, a.s13, a.g13, counts, offsets,
+                             sorted, h, a.E, a.K, a.I, stream);
+    if (err != cudaSuccess) { *why = "gate/up"; return err; }
+    if ((err = mark(2)) != cudaSuccess) { *why = "stage event"; return err; }
+    err = launch_down_simt(h, a.w2, a.s2, a.g2, counts, offsets, y, a.E, a.K, a.I, stream);
+    if (err != cudaSuccess) { *why = "down"; return err; }
+    if ((err = mark(3)) != cudaSuccess) { *why = "stage event"; return err; }
+  }
   err = launch_combine(y, slot_of, a.weights, a.multiply_router_weight, a.out, a.out_dt, a.M,
                        a.top_k, a.K, stream);
   if (err != cudaSuccess) { *why = "combine"; return err; }

@@ -54,7 +54,8 @@ def test_random_shapes_vs_oracle(sbb, oracle, cuda, E, K, I, T, top_k):
     L = oracle.make_layer(E, K, I, seed=seed)
     hidden = oracle.make_hidden(T, K, seed=seed + 1)
     ids, w = oracle.route_logits(T, E, top_k, seed=seed + 2)
-    ids[0, 0] = -1
+    if T * top_k > 1:
+        ids[0, 0] = -1
     got = run_moe(sbb, hidden, ids, w, L, cuda)
     check(got, oracle.moe_forward(hidden, ids, w, L))
 
@@ -62,7 +63,7 @@ def test_random_shapes_vs_oracle(sbb, oracle, cuda, E, K, I, T, top_k):
 @pytest.mark.parametrize("act", [torch.float32, torch.float16, torch.bfloat16])
 @pytest.mark.parametrize("out_dtype", [torch.float32, torch.bfloat16])
 def test_dtypes(sbb, oracle, cuda, act, out_dtype):
-    E, K, I, T, top_k = 12, 512, 128, 24, 3
+    E, K, I, T, top_k = 12, 512, 256, 24, 3
     L = oracle.make_layer(E, K, I, seed=21)
     hidden = oracle.make_hidden(T, K, seed=22)
     ids, w = oracle.route_logits(T, E, top_k, seed=23)
@@ -80,8 +81,9 @@ def test_multiply_router_weight_off(sbb, oracle, cuda):
     check(got, oracle.moe_forward(hidden, ids, w, L, multiply_router_weight=False))
 
 
-def test_duplicate_experts_and_empty_tokens(sbb, oracle, cuda):
-    E, K, I, T, top_k = 8, 256, 64, 12, 4
+@pytest.mark.parametrize("K,I", [(256, 64), (512, 256)])
+def test_duplicate_experts_and_empty_tokens(sbb, oracle, cuda, K, I):
+    E, T, top_k = 8, 12, 4
     L = oracle.make_layer(E, K, I, seed=41)
     hidden = oracle.make_hidden(T, K, seed=42)
     ids = np.array([[1, 1, 1, 1]] * 4 + [[-1, -1, -1, -1]] * 4 + [[0, 7, 7, -1]] * 4, np.int32)
@@ -115,13 +117,14 @@ def test_custom_op_and_validation(sbb, oracle, cuda):
     with pytest.raises(ValueError, match="topk ids must be int32"):
         sbb.nvfp4_moe(hidden, ids.long(), w, *tensors)
     with pytest.raises(ValueError, match="w2 must be byte"):
-        sbb.nvfp4_moe(hidden, ids, w, *tensors[:3], tensors[3][:, :128], *tensors[4:])
+        sbb.nvfp4_moe(hidden, ids, w, *tensors[:3], tensors[3][:, :128].contiguous(),
+                      *tensors[4:])
     with pytest.raises(ValueError, match="CUDA tensor"):
         sbb.nvfp4_moe(hidden.cpu(), ids, w, *tensors)
 
 
 def test_provider_forward_and_health(sbb, oracle, cuda):
-    E, K, I, T, top_k = 16, 512, 128, 20, 4
+    E, K, I, T, top_k = 16, 512, 256, 20, 4
     L = oracle.make_layer(E, K, I, seed=71)
     hidden = oracle.make_hidden(T, K, seed=72)
     ids, w = oracle.route_logits(T, E, top_k, seed=73)
@@ -141,7 +144,7 @@ def test_provider_forward_and_health(sbb, oracle, cuda):
 
 
 def test_cuda_graph_replay(sbb, oracle, cuda):
-    E, K, I, T, top_k = 16, 512, 128, 8, 4
+    E, K, I, T, top_k = 16, 512, 256, 8, 4
     L = oracle.make_layer(E, K, I, seed=81)
     hidden = oracle.make_hidden(T, K, seed=82)
     ids, w = oracle.route_logits(T, E, top_k, seed=83)

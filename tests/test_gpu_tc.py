@@ -1,0 +1,143 @@
+"""The tcgen05 path at the BASELINE shapes (E=170, d=4096, I=1280, top-8),
+checked against the CPU oracle on sampled tokens: a token's output depends
+only on its own routes, so a sample checks a full-size batch exactly.
+
+Weights here are random NVFP4 bytes generated on the device (all 16 e2m1
+codes, e4m3 scale exponents 4..10 as in the reference's fixtures,
+src/phase7/nvfp4_testutil.py:33-51). Tolerance: max relative error <= 1e-2
+(max|got-want| / max|want|) and cosine >= 0.9999."""
+
+from __future__ import annotations
+
+import numpy as np
+import pytest
+import torch
+
+from conftest import cosine, rel_err
+from gpu_util import dev
+
+pytestmark = pytest.mark.gpu
+
+REL_TOL = 1e-2
+COS_TOL = 0.9999
+
+
+def random_layer(E, K, I, seed, device):
+    g = torch.Generator(device=device)
+    g.manual_seed(seed)
+
+    def plane(rows, cols):
+        q = torch.randint(0, 256, (E, rows, cols // 2), generator=g, device=device,
+                          dtype=torch.int32).to(torch.uint8)
+        ex = torch.randint(4, 11, (E, rows, cols // 16), generator=g, device=device,
+                           dtype=torch.int32)
+        man = torch.randint(0, 8, (E, rows, cols // 16), generator=g, device=device,
+                            dtype=torch.int32)
+        return q, ((ex << 3) | man).to(torch.uint8)
+
+    w13, s13 = plane(2 * I, K)
+    w2, s2 = plane(K, I)
+    g13 = (torch.rand(E, generator=g, device=device) * 0.002 + 0.001).float()
+    g2 = (torch.rand(E, generator=g, device=device) * 0.002 + 0.001).float()
+    return w13, s13, g13, w2, s2, g2
+
+
+def host_layer(oracle, t, E, K, I):
+    w13, s13, g13, w2, s2, g2 = (x.cpu().numpy() for x in t)
+    return oracle.Layer(E, K, I, w13, s13, g13, w2, s2, g2)
+
+
+def run_and_check(sbb, oracle, cuda, E, K, I, ids, w, hidden_bits, tensors, sample=48, seed=0,
+                  act=torch.bfloat16):
+    T = ids.shape[0]
+    h = dev(hidden_bits, cuda, torch.bfloat16).to(act)
+    out = sbb.nvfp4_moe(h, dev(ids, cuda), dev(w, cuda), *tensors)
+    torch.cuda.synchronize()
+    assert sbb.nvfp4_moe_device_errors(cuda) == 0
+    got = out.cpu().numpy()
+    rng = np.random.default_rng(seed)
+    toks = np.sort(rng.choice(T, size=min(sample, T), replace=False)).astype(np.int32)
+    L = host_layer(oracle, tensors, E, K, I)
+    want = oracle.moe_forward(hidden_bits, ids, w, L, tokens=toks)
+    assert rel_err(got[toks], want) <= REL_TOL, rel_err(got[toks], want)
+    assert cosine(got[toks], want) >= COS_TOL, cosine(got[toks], want)
+    return got
+
+
+@pytest.fixture(scope="module")
+def big_layer(cuda):
+    return random_layer(170, 4096, 1280, seed=5, device=cuda)
+
+
+@pytest.mark.parametrize("T", [1, 8, 64, 200])
+def test_decode_shapes(sbb, oracle, cuda, big_layer, T):
+    ids, w = oracle.route_logits(T, 170, 8, seed=T)
+    hidden = oracle.make_hidden(T, 4096, seed=T + 1)
+    run_and_check(sbb, oracle, cuda, 170, 4096, 1280, ids, w, hidden, big_layer, seed=T)
+
+
+def test_prefill_chunk_8k(sbb, oracle, cuda, big_layer):
+    T = 8192
+    ids, w = oracle.route_logits(T, 170, 8, seed=9, bias_std=0.5)
+    hidden = oracle.make_hidden(T, 4096, seed=10)
+    run_and_check(sbb, oracle, cuda, 170, 4096, 1280, ids, w, hidden, big_layer, sample=24)
+
+
+def test_skewed_zipf_routing(sbb, oracle, cuda, big_layer):
+    T = 1024
+    ids, w = oracle.route_zipf(T, 170, 8, seed=11)
+    hidden = oracle.make_hidden(T, 4096, seed=12)
+    run_and_check(sbb, oracle, cuda, 170, 4096, 1280, ids, w, hidden, big_layer, sample=32)
+
+
+@pytest.mark.parametrize("T,E,top_k", [(40, 16, 2), (90, 8, 4), (300, 8, 8), (2000, 16, 4)])
+def test_token_tile_widths(sbb, oracle, cuda, T, E, top_k):
+    """Routes per expert from ~5 to ~500 select every token-tile width and
+    experts that span several tiles."""
+    K, I = 1024, 512
+    tensors = random_layer(E, K, I, seed=T, device=cuda)
+    ids, w = oracle.route_logits(T, E, top_k, seed=T + 3)
+    ids[::7, 0] = -1
+    hidden = oracle.make_hidden(T, K, seed=T + 4)
+    run_and_check(sbb, oracle, cuda, E, K, I, ids, w, hidden, tensors, sample=40)
+
+
+def test_single_hot_expert(sbb, oracle, cuda):
+    K, I, E, T = 512, 256, 4, 700
+    tensors = random_layer(E, K, I, seed=3, device=cuda)
+    ids = np.full((T, 2), 2, np.int32)
+    ids[:, 1] = -1
+    ids[::3, 1] = 1
+    w = np.full((T, 2), 0.5, np.float32)
+    hidden = oracle.make_hidden(T, K, seed=4)
+    run_and_check(sbb, oracle, cuda, E, K, I, ids, w, hidden, tensors, sample=60)
+
+
+@pytest.mark.parametrize("scale", [1e-4, 1.0, 3000.0])
+def test_activation_range(sbb, oracle, cuda, scale):
+    """Activations far from unit scale: the per-row power-of-two staging keeps
+    the f16 operand exact whatever the magnitude."""
+    K, I, E, T = 512, 256, 8, 33
+    tensors = random_layer(E, K, I, seed=7, device=cuda)
+    ids, w = oracle.route_logits(T, E, 3, seed=8)
+    hidden = oracle.make_hidden(T, K, seed=9, scale=scale)
+    run_and_check(sbb, oracle, cuda, E, K, I, ids, w, hidden, tensors, sample=T)
+
+
+def test_f16_activations_tc(sbb, oracle, cuda):
+    K, I, E, T = 1024, 512, 8, 50
+    tensors = random_layer(E, K, I, seed=21, device=cuda)
+    ids, w = oracle.route_logits(T, E, 4, seed=22)
+    hidden = oracle.make_hidden(T, K, seed=23)
+    run_and_check(sbb, oracle, cuda, E, K, I, ids, w, hidden, tensors, sample=T,
+                  act=torch.float16)
+
+
+def test_deterministic_repeat(sbb, oracle, cuda, big_layer):
+    T = 64
+    ids, w = oracle.route_logits(T, 170, 8, seed=31)
+    hidden = dev(oracle.make_hidden(T, 4096, seed=32), cuda, torch.bfloat16)
+    a = sbb.nvfp4_moe(hidden, dev(ids, cuda), dev(w, cuda), *big_layer)
+    b = sbb.nvfp4_moe(hidden, dev(ids, cuda), dev(w, cuda), *big_layer)
+    torch.cuda.synchronize()
+    assert torch.equal(a, b)
