@@ -67,6 +67,37 @@ struct TcLaunch {
   void* stage_ctx;
 };
 
+// Block-scaled path (moe_bs.cu): activations split into kSplitTerms NVFP4
+// terms, tcgen05.mma kind::mxf4nvf4 on the packed weights.
+constexpr int kSplitTerms = 4;
+
+struct BsLaunch {
+  const void* hidden;
+  int act_dt;
+  const int32_t* counts;
+  const int32_t* offsets;
+  const int32_t* sorted;
+  const uint8_t *w13, *s13, *w2, *s2;
+  const float *g13, *g2;
+  uint8_t* xq;   // [R*NT, K/2]
+  uint8_t* xsf;  // [R*NT, K/16]
+  float* xg;     // [R*NT]
+  float* h;      // fp32 [R, I]
+  uint8_t* hq;   // [R*NT, I/2]
+  uint8_t* hsf;  // [R*NT, I/16]
+  float* hg;     // [R*NT]
+  float* y;      // fp32 [R, K]
+  uint32_t* status;
+  int64_t R;
+  int E, top_k, K, I;
+  void (*stage_mark)(void* ctx, int stage);
+  void* stage_ctx;
+};
+
+bool bs_supported(int K, int I);
+int bs_tile_rows(int64_t routes, int E, int mode);
+cudaError_t launch_moe_bs(const BsLaunch& a, cudaStream_t stream, const char** step);
+
 bool tc_supported(int K, int I, int act_dt);
 int tc_token_tile(int64_t routes, int E, int mode);
 cudaError_t launch_moe_tc(const TcLaunch& a, cudaStream_t stream, const char** step);

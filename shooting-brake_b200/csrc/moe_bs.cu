@@ -1,0 +1,743 @@
+// Block-scaled tcgen05 path for the routed-expert NVFP4 MoE (sm_100a).
+//
+// The weights go to the tensor core as they are stored: packed e2m1 with one
+// e4m3 scale per 16 elements, through tcgen05.mma kind::mxf4nvf4 block16
+// (K = 64 per instruction, scales from tensor memory). Nothing dequantises a
+// weight. A kind::f16 MMA that reads a 16-bit copy of the weights costs a
+// fixed ~50 cycles per 128x16 weight tile whatever the token count, which at
+// decode sizes is as slow as streaming the tile from HBM; the block-scaled
+// instruction covers four times the weights per issue.
+//
+// The activations (bf16 hidden rows, then the fp32 SwiGLU rows) are split
+// into NT NVFP4 terms by residual quantisation,
+//   x = sum_t e2m1_t * e4m3_t * g_t  (+ residual),
+// each term quantised with vLLM ref_nvfp4_quant semantics (the reference's
+// fixture quantiser) under its own per-row global g_t = amax(residual_t) /
+// (448 * 6). Each term shrinks the residual about 11x; with NT = 4 the
+// represented activations are within ~1e-4 (normwise) of the inputs, finer
+// than the bf16 rounding of the inputs themselves. The terms of a row sit in
+// consecutive rows of the N operand, so one MMA covers all terms of BN/NT
+// routed tokens and the epilogue folds them: D[:, slot] = sum_t D[:, slot*NT
+// + t] * g_t.
+//
+// Work unit, persistent grid and warp specialisation as in moe_tc.cu:
+//   warp 0       TMA: packed weights (128-byte swizzle), their linear scale
+//                rows, the packed term rows and their scale rows.
+//   warp 1       TMEM allocation; one thread copies the stage's scale atoms
+//                to tensor memory (tcgen05.cp 32x128b.warpx4) and issues the
+//                MMAs.
+//   warps 4-7    scale warps: rearrange the linear e4m3 scale rows of the
+//                stage into the 32x4x4 atoms the MMA reads (row r = r0 +
+//                32*r1 of a 128-row block, 4 scales per 64-wide K group:
+//                byte r0*16 + r1*4 + kb).
+//   warps 12-15  epilogue: fold terms, global scale, SwiGLU (gate/up) or the
+//                fp32 route output (down).
+// Every wait is bounded (the kernel raises status[1], drains and returns).
+#include <cuda.h>
+#include <cudaTypedefs.h>
+#include <cuda_fp8.h>
+
+#include <mutex>
+
+#include "common.cuh"
+#include "kernels.h"
+#include "tc_ptx.cuh"
+
+namespace sbb {
+
+namespace {
+
+using namespace ptx;
+
+constexpr int kBK = 256;              // K elements per pipeline stage
+constexpr int kRowBytes = kBK / 2;    // packed bytes per row per stage (128)
+constexpr int kRowScales = kBK / 16;  // scale bytes per row per stage (16)
+constexpr int kM = 128;
+constexpr int kThreads = 512;
+constexpr int kTmemCols = 512;
+constexpr uint64_t kTimeoutNs = 2000000000ull;
+constexpr int kAtom = 512;            // one 128-row x 4-scale atom
+
+enum : int { kGateUp = 0, kDown = 1 };
+
+struct BsParams {
+  const int32_t* counts;
+  const int32_t* offsets;
+  const float* gscale;  // per-expert weight global (g13 or g2)
+  const float* bg;      // per (slot, term) activation global
+  float* out;           // gate/up: fp32 h [R, I]; down: fp32 y [R, K]
+  uint32_t* status;
+  int E;
+  int I;
+  int m_tiles;          // I/128 (gate/up) or K/256 (down)
+  int a_stride;         // row offset of the second 128-row block: I (up rows) or 128
+  int k_stages;         // reduction / 256
+  int rows_per_expert;  // 2I or K
+  int out_ld;           // I or K
+};
+
+template <int MODE, int BNR, int NT>
+struct BsCfg {
+  // two 128-row weight blocks per unit: gate and up rows (gate/up) or 256
+  // consecutive rows of w2 (down), each into its own accumulator
+  static constexpr int kNA = 2;
+  static constexpr int kTok = BNR / NT;                    // routed tokens per tile
+  static constexpr int kA = kNA * kM * kRowBytes;          // packed weights
+  static constexpr int kB = BNR * kRowBytes;               // packed term rows
+  static constexpr int kSA = kNA * kM * kRowScales;        // linear weight scales
+  static constexpr int kSB = BNR * kRowScales;             // linear term scales
+  static constexpr int kAtoms = (kNA + 1) * 4 * kAtom;     // rearranged scales
+  static constexpr int kRaw = kA + kB + kSA + kSB + kAtoms;
+  static constexpr int kStageBytes = (kRaw + 1023) / 1024 * 1024;
+  static constexpr int kStagesRaw = (200 * 1024) / kStageBytes;
+  static constexpr int kStages = kStagesRaw > 8 ? 8 : (kStagesRaw < 2 ? 2 : kStagesRaw);
+  static constexpr int kSmem = kStages * kStageBytes + 1024;
+  static constexpr int kOffB = kA;
+  static constexpr int kOffSA = kA + kB;
+  static constexpr int kOffSB = kOffSA + kSA;
+  static constexpr int kOffAtoms = ((kOffSB + kSB + 127) / 128) * 128;
+  // tensor memory: accumulators then two scale buffers
+  static constexpr int kDCols = kNA * BNR;
+  static constexpr int kDBufs = 2 * kDCols + 2 * (kNA + 1) * 16 <= kTmemCols ? 2 : 1;
+  static constexpr int kSfCol0 = kDBufs * kDCols;
+  static constexpr int kSfCols = (kNA + 1) * 16;  // per buffer
+  static constexpr uint32_t kIdesc =
+      (1u << 7) | (1u << 10) | (static_cast<uint32_t>(BNR >> 3) << 17) | ((kM >> 4) << 24);
+  static_assert(kOffAtoms + kAtoms <= kStageBytes, "stage layout");
+  static_assert(kSfCol0 + 2 * kSfCols <= kTmemCols, "tensor memory");
+  static_assert(BNR % 16 == 0 && BNR >= 16 && BNR <= 256 && BNR % NT == 0, "tile");
+};
+
+__device__ __forceinline__ void decode_unit(int u, int m_tiles, const int* prefix, int E, int& e,
+                                            int& nt, int& mt) {
+  const int t = u / m_tiles;
+  mt = u - t * m_tiles;
+  int lo = 0, hi = E;
+  while (hi - lo > 1) {
+    const int mid = (lo + hi) >> 1;
+    if (prefix[mid] <= t) lo = mid;
+    else hi = mid;
+  }
+  e = lo;
+  nt = t - prefix[e];
+}
+
+__device__ __forceinline__ bool warp_wait(uint64_t* bar, uint32_t parity, volatile int* abort,
+                                          uint64_t deadline) {
+  const int lane = threadIdx.x & 31;
+  for (uint32_t i = 0;; ++i) {
+    const bool done = mbar_try_wait(bar, parity);
+    if (__all_sync(0xffffffffu, done)) return true;
+    if ((i & 15) == 15) {
+      int stop = 0;
+      if (lane == 0) {
+        stop = *abort || now_ns() > deadline;
+        if (stop) *abort = 1;
+      }
+      if (__shfl_sync(0xffffffffu, stop, 0)) return false;
+    }
+  }
+}
+
+// no-swizzle descriptor of one 32 x 16-byte scale chunk (8-row core matrices
+// 128 bytes apart) for tcgen05.cp
+__device__ __forceinline__ uint64_t desc_atom(uint32_t saddr) {
+  uint64_t d = 0;
+  d |= static_cast<uint64_t>((saddr >> 4) & 0x3FFFu);
+  d |= static_cast<uint64_t>(128 >> 4) << 32;
+  d |= static_cast<uint64_t>(1) << 46;
+  return d;
+}
+
+__device__ __forceinline__ void tmem_cp_atom(uint32_t taddr, uint64_t desc) {
+  asm volatile("tcgen05.cp.cta_group::1.32x128b.warpx4 [%0], %1;" ::"r"(taddr), "l"(desc)
+               : "memory");
+}
+
+__device__ __forceinline__ void mma_bs(uint32_t d_tmem, uint64_t a_desc, uint64_t b_desc,
+                                       uint32_t idesc, uint32_t sfa, uint32_t sfb,
+                                       uint32_t accumulate) {
+  asm volatile(
+      "{\n .reg .pred p;\n setp.ne.b32 p, %4, 0;\n"
+      " tcgen05.mma.cta_group::1.kind::mxf4nvf4.block_scale.block16 [%0], %1, %2, %3, [%5], [%6], p;\n}"
+      ::"r"(d_tmem), "l"(a_desc), "l"(b_desc), "r"(idesc), "r"(accumulate), "r"(sfa), "r"(sfb)
+      : "memory");
+}
+
+template <int MODE, int BNR, int NT>
+__global__ void __launch_bounds__(kThreads, 1)
+    moe_gemm_bs_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmSA,
+                       const __grid_constant__ CUtensorMap tmB, const __grid_constant__ CUtensorMap tmSB,
+                       const BsParams p) {
+  using C = BsCfg<MODE, BNR, NT>;
+  constexpr int S = C::kStages;
+  constexpr int NB = C::kDBufs;
+  extern __shared__ uint8_t smem_raw[];
+  uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) &
+                                             ~static_cast<uintptr_t>(1023));
+  __shared__ __align__(8) uint64_t full[S], empty[S], sfready[S], dfull[NB], dempty[NB], sffree[2],
+      done_bar;
+  __shared__ uint32_t tmem_base_s;
+  __shared__ int abort_s;
+  __shared__ int prefix[kMaxExperts + 1];
+
+  const int tid = threadIdx.x;
+  const int warp = tid >> 5;
+  const int lane = tid & 31;
+  const uint64_t deadline = now_ns() + kTimeoutNs;
+  volatile int* abort = &abort_s;
+
+  if (tid == 0) {
+    for (int i = 0; i < S; ++i) {
+      mbar_init(&full[i], 1);
+      mbar_init(&empty[i], 1 + 4);  // MMA commit + the four scale warps
+      mbar_init(&sfready[i], 4);
+    }
+    for (int i = 0; i < NB; ++i) {
+      mbar_init(&dfull[i], 1);
+      mbar_init(&dempty[i], 4);
+    }
+    mbar_init(&sffree[0], 1);
+    mbar_init(&sffree[1], 1);
+    mbar_init(&done_bar, 1);
+    abort_s = 0;
+    fence_mbar_init();
+  }
+  if (warp == 0 && lane == 0) {
+    prefetch_tensormap(&tmA);
+    prefetch_tensormap(&tmSA);
+    prefetch_tensormap(&tmB);
+    prefetch_tensormap(&tmSB);
+  }
+  if (warp == 1) {
+    tmem_alloc(&tmem_base_s, kTmemCols);
+    tmem_relinquish();
+  }
+  if (warp == 2) {
+    int carry = 0;
+    for (int e0 = 0; e0 < p.E; e0 += 32) {
+      const int e = e0 + lane;
+      int v = e < p.E ? (p.counts[e] + C::kTok - 1) / C::kTok : 0;
+#pragma unroll
+      for (int d = 1; d < 32; d <<= 1) {
+        const int n = __shfl_up_sync(0xffffffffu, v, d);
+        if (lane >= d) v += n;
+      }
+      if (e < p.E) prefix[e + 1] = carry + v;
+      carry += __shfl_sync(0xffffffffu, v, 31);
+    }
+    if (lane == 0) prefix[0] = 0;
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem = tmem_base_s;
+  const int total_units = prefix[p.E] * p.m_tiles;
+
+  if (warp == 0) {
+    // ---------------- TMA producer ----------------
+    if (lane == 0) {
+      const uint64_t pol_w = policy_evict_first();
+      const uint64_t pol_x = policy_evict_last();
+      int s = 0;
+      uint32_t ph = 0;
+      uint32_t issued_phase[S];
+      bool issued[S];
+#pragma unroll
+      for (int i = 0; i < S; ++i) issued[i] = false;
+      bool ok = true;
+      for (int u = blockIdx.x; u < total_units && ok; u += gridDim.x) {
+        int e, nt, mt;
+        decode_unit(u, p.m_tiles, prefix, p.E, e, nt, mt);
+        const int row_b = (p.offsets[e] + nt * C::kTok) * NT;
+        const int r0 = e * p.rows_per_expert + mt * (MODE == kGateUp ? kM : 2 * kM);
+        for (int kk = 0; kk < p.k_stages; ++kk) {
+          if (!mbar_wait(&empty[s], ph ^ 1u, abort, deadline)) {
+            ok = false;
+            break;
+          }
+          uint8_t* st = smem + s * C::kStageBytes;
+          mbar_expect_tx(&full[s], C::kA + C::kB + C::kSA + C::kSB);
+          const int xa = kk * kRowBytes;
+          const int xs = kk * kRowScales;
+#pragma unroll
+          for (int a = 0; a < C::kNA; ++a) {
+            tma_load_2d_hint(st + a * kM * kRowBytes, &tmA, &full[s], xa, r0 + a * p.a_stride,
+                             pol_w);
+            tma_load_2d_hint(st + C::kOffSA + a * kM * kRowScales, &tmSA, &full[s], xs,
+                             r0 + a * p.a_stride, pol_w);
+          }
+          tma_load_2d_hint(st + C::kOffB, &tmB, &full[s], xa, row_b, pol_x);
+          tma_load_2d_hint(st + C::kOffSB, &tmSB, &full[s], xs, row_b, pol_x);
+          issued[s] = true;
+          issued_phase[s] = ph;
+          if (++s == S) {
+            s = 0;
+            ph ^= 1u;
+          }
+        }
+      }
+      const uint64_t drain_deadline = now_ns() + kTimeoutNs;
+      for (int i = 0; i < S; ++i) {
+        if (!issued[i]) continue;
+        while (!mbar_try_wait(&full[i], issued_phase[i]) && now_ns() < drain_deadline) {
+        }
+      }
+    }
+  } else if (warp == 1) {
+    // ---------------- scale copies + MMA issuer ----------------
+    if (lane == 0) {
+      int s = 0;
+      uint32_t ph = 0;
+      uint32_t it = 0;  // stage sequence number (scale buffer = it & 1)
+      uint32_t ui = 0;
+      bool ok = true;
+      for (int u = blockIdx.x; u < total_units && ok; u += gridDim.x, ++ui) {
+        const int d = ui % NB;
+        if (!mbar_wait(&dempty[d], ((ui / NB) & 1u) ^ 1u, abort, deadline)) break;
+        tc_fence_after();
+        const uint32_t d_tm = tmem + d * C::kDCols;
+        for (int kk = 0; kk < p.k_stages; ++kk) {
+          const int sb = it & 1;
+          // the scale buffer's previous MMAs (two stages ago) are complete
+          if (!mbar_wait(&sffree[sb], ((it >> 1) & 1u) ^ 1u, abort, deadline) ||
+              !mbar_wait(&full[s], ph, abort, deadline) ||
+              !mbar_wait(&sfready[s], ph, abort, deadline)) {
+            ok = false;
+            break;
+          }
+          tc_fence_after();
+          const uint8_t* st = smem + s * C::kStageBytes;
+          const uint32_t atoms = smem_u32(st + C::kOffAtoms);
+          const uint32_t a_sa = smem_u32(st);
+          const uint32_t b_sa = smem_u32(st + C::kOffB);
+          const uint32_t sf0 = tmem + C::kSfCol0 + sb * C::kSfCols;
+#pragma unroll
+          for (int kg = 0; kg < 4; ++kg) {
+#pragma unroll
+            for (int a = 0; a < C::kNA; ++a)
+              tmem_cp_atom(sf0 + (a * 4 + kg) * 4, desc_atom(atoms + (a * 4 + kg) * kAtom));
+            tmem_cp_atom(sf0 + (C::kNA * 4 + kg) * 4, desc_atom(atoms + (C::kNA * 4 + kg) * kAtom));
+          }
+#pragma unroll
+          for (int kg = 0; kg < 4; ++kg) {
+            const uint64_t bd = desc_sw128(b_sa + kg * 32);
+            const uint32_t acc = (kk | kg) != 0;
+#pragma unroll
+            for (int a = 0; a < C::kNA; ++a) {
+              const uint64_t ad = desc_sw128(a_sa + a * kM * kRowBytes + kg * 32);
+              mma_bs(d_tm + a * BNR, ad, bd, C::kIdesc, sf0 + (a * 4 + kg) * 4,
+                     sf0 + (C::kNA * 4 + kg) * 4, acc);
+            }
+          }
+          mma_commit(&empty[s]);
+          mma_commit(&sffree[sb]);
+          ++it;
+          if (++s == S) {
+            s = 0;
+            ph ^= 1u;
+          }
+        }
+        if (!ok) break;
+        mma_commit(&dfull[d]);
+      }
+      mma_commit(&done_bar);
+      const uint64_t drain_deadline = now_ns() + kTimeoutNs;
+      while (!mbar_try_wait(&done_bar, 0) && now_ns() < drain_deadline) {
+      }
+    }
+  } else if (warp >= 4 && warp < 8) {
+    // ---------------- scale rearrangement ----------------
+    const int t = tid - 128;  // 0..127
+    int s = 0;
+    uint32_t ph = 0;
+    bool ok = true;
+    for (int u = blockIdx.x; u < total_units && ok; u += gridDim.x) {
+      for (int kk = 0; kk < p.k_stages; ++kk) {
+        if (!warp_wait(&full[s], ph, abort, deadline)) {
+          ok = false;
+          break;
+        }
+        uint8_t* st = smem + s * C::kStageBytes;
+        uint8_t* atoms = st + C::kOffAtoms;
+        // row t of each weight block and of the term tile: its 16 scale bytes
+        // are 4 K groups x 4 blocks; group kg goes to atom kg at r0*16 + r1*4.
+        const int r0 = t & 31, r1 = t >> 5;
+#pragma unroll
+        for (int a = 0; a < C::kNA; ++a) {
+          const uint4 v = *reinterpret_cast<const uint4*>(st + C::kOffSA + (a * kM + t) * kRowScales);
+          const uint32_t w[4] = {v.x, v.y, v.z, v.w};
+#pragma unroll
+          for (int kg = 0; kg < 4; ++kg)
+            *reinterpret_cast<uint32_t*>(atoms + (a * 4 + kg) * kAtom + r0 * 16 + r1 * 4) = w[kg];
+        }
+        if (t < BNR) {
+          const uint4 v = *reinterpret_cast<const uint4*>(st + C::kOffSB + t * kRowScales);
+          const uint32_t w[4] = {v.x, v.y, v.z, v.w};
+#pragma unroll
+          for (int kg = 0; kg < 4; ++kg)
+            *reinterpret_cast<uint32_t*>(atoms + (C::kNA * 4 + kg) * kAtom + r0 * 16 + r1 * 4) = w[kg];
+        }
+        // make the generic-proxy writes visible to tcgen05.cp (async proxy)
+        asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+        __syncwarp();
+        if (lane == 0) {
+          mbar_arrive(&sfready[s]);
+          mbar_arrive(&empty[s]);
+        }
+        if (++s == S) {
+          s = 0;
+          ph ^= 1u;
+        }
+      }
+    }
+  } else if (warp >= 12) {
+    // ---------------- epilogue ----------------
+    const int q = warp & 3;
+    const int r = q * 32 + lane;
+    const uint32_t lane_base = static_cast<uint32_t>(q * 32) << 16;
+    uint32_t ui = 0;
+    for (int u = blockIdx.x; u < total_units; u += gridDim.x, ++ui) {
+      int e, nt, mt;
+      decode_unit(u, p.m_tiles, prefix, p.E, e, nt, mt);
+      const int d = ui % NB;
+      if (!warp_wait(&dfull[d], (ui / NB) & 1u, abort, deadline)) break;
+      tc_fence_after();
+      const int valid = min(C::kTok, p.counts[e] - nt * C::kTok);
+      const int slot0 = p.offsets[e] + nt * C::kTok;
+      const float gs = p.gscale[e];
+      const uint32_t taddr = tmem + lane_base + d * C::kDCols;
+#pragma unroll 1
+      for (int c0 = 0; c0 < BNR; c0 += 16) {
+        uint32_t t0[16], t1[16];
+        tmem_ld16(taddr + c0, t0);
+        tmem_ld16(taddr + BNR + c0, t1);
+        tmem_wait_ld();
+        constexpr int kTokPerChunk = 16 / NT;
+#pragma unroll
+        for (int jj = 0; jj < kTokPerChunk; ++jj) {
+          const int j = c0 / NT + jj;  // token within the tile
+          if (j < valid) {
+            const int slot = slot0 + j;
+            float v0 = 0.0f, v1 = 0.0f;
+#pragma unroll
+            for (int tt = 0; tt < NT; ++tt) {
+              const float g = p.bg[static_cast<int64_t>(slot) * NT + tt];
+              v0 = fmaf(__uint_as_float(t0[jj * NT + tt]), g, v0);
+              v1 = fmaf(__uint_as_float(t1[jj * NT + tt]), g, v1);
+            }
+            float* orow = p.out + static_cast<int64_t>(slot) * p.out_ld;
+            if (MODE == kGateUp) {
+              const float gv = v0 * gs, uv = v1 * gs;
+              orow[mt * kM + r] = silu(gv) * uv;
+            } else {
+              orow[mt * 2 * kM + r] = v0 * gs;
+              orow[mt * 2 * kM + kM + r] = v1 * gs;
+            }
+          }
+        }
+      }
+      tc_fence_before();
+      __syncwarp();
+      if (lane == 0) mbar_arrive(&dempty[d]);
+    }
+  }
+
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  if (warp == 1) tmem_dealloc(tmem, kTmemCols);
+  if (tid == 0 && abort_s) atomicOr(&p.status[1], 1u);
+}
+
+// ---- activation splitter ----------------------------------------------------
+
+// Two fp32 -> one byte of e2m1 (lo -> low nibble), round to nearest even,
+// saturating: cvt.rn.satfinite.e2m1x2.f32 places its first source operand in
+// the upper nibble.
+__device__ __forceinline__ uint32_t e2m1x2_from_f32(float lo, float hi) {
+  uint32_t r;
+  asm("{\n .reg .b8 b;\n cvt.rn.satfinite.e2m1x2.f32 b, %1, %2;\n cvt.u32.u8 %0, b;\n}"
+      : "=r"(r)
+      : "f"(hi), "f"(lo));
+  return r;
+}
+
+__device__ __forceinline__ float2 e2m1x2_to_float2(uint32_t byte) {
+  uint32_t h;
+  asm("{\n .reg .b8 b;\n cvt.u8.u32 b, %1;\n cvt.rn.f16x2.e2m1x2 %0, b;\n}" : "=r"(h) : "r"(byte));
+  return __half22float2(*reinterpret_cast<const __half2*>(&h));
+}
+
+
+// One CTA of kSplitThreads per output row: row i reads source row src(i) (the
+// token of sorted route i, or row i) and writes NT terms: packed e2m1
+// [i*NT + t, K/2], e4m3 scales [i*NT + t, K/16] and the dequant global
+// g [i*NT + t]. The residual stays in registers: thread T owns element pairs
+// (2T, 2T+1) of every 2*kSplitThreads-wide chunk, so a 16-element block is 8
+// lanes (block maxima and nibble packing are shuffles) and a packed byte is
+// one thread's pair. The row maximum of each term is one CTA reduction.
+constexpr int kSplitThreads = 256;
+constexpr int kSplitMaxPairs = 16384 / (2 * kSplitThreads);  // K <= 16384
+
+template <int PAIRS>
+__global__ void __launch_bounds__(kSplitThreads) split_nvfp4_kernel(
+    const void* __restrict__ src, int src_dt, const int32_t* __restrict__ sorted, int top_k,
+    const int32_t* __restrict__ n_rows_dev, int K, int NT, uint8_t* __restrict__ q,
+    uint8_t* __restrict__ sf, float* __restrict__ gout) {
+  __shared__ float s_max[kSplitThreads / 32];
+  const int64_t row = blockIdx.x;
+  if (row >= static_cast<int64_t>(*n_rows_dev)) return;
+  const int tid = threadIdx.x;
+  const int lane = tid & 31;
+  const int warp = tid >> 5;
+  const int64_t srow = sorted ? static_cast<int64_t>(sorted[row] / top_k) : row;
+  // pairs per thread; with K % 64 == 0 the last partial chunk ends on a warp
+  // boundary, so every validity test below is warp-uniform
+  const int npairs = (K + 2 * kSplitThreads - 1) / (2 * kSplitThreads);
+  float2 v[PAIRS];
+  float amax = 0.0f;
+#pragma unroll
+  for (int i = 0; i < PAIRS; ++i) {
+    const int64_t k = static_cast<int64_t>(i) * 2 * kSplitThreads + 2 * tid;
+    v[i] = make_float2(0.0f, 0.0f);
+    if (i < npairs && k < K) {
+      if (src_dt == kBF16) {
+        const uint32_t w = *reinterpret_cast<const uint32_t*>(
+            static_cast<const uint16_t*>(src) + srow * K + k);
+        v[i] = make_float2(__uint_as_float(w << 16), __uint_as_float(w & 0xFFFF0000u));
+      } else if (src_dt == kF32) {
+        v[i] = *reinterpret_cast<const float2*>(static_cast<const float*>(src) + srow * K + k);
+      } else {
+        v[i] = __half22float2(*reinterpret_cast<const __half2*>(
+            static_cast<const __half*>(src) + srow * K + k));
+      }
+      amax = fmaxf(amax, fmaxf(fabsf(v[i].x), fabsf(v[i].y)));
+    }
+  }
+  for (int t = 0; t < NT; ++t) {
+#pragma unroll
+    for (int d = 16; d > 0; d >>= 1) amax = fmaxf(amax, __shfl_xor_sync(0xffffffffu, amax, d));
+    if (lane == 0) s_max[warp] = amax;
+    __syncthreads();
+    amax = s_max[0];
+#pragma unroll
+    for (int w = 1; w < kSplitThreads / 32; ++w) amax = fmaxf(amax, s_max[w]);
+    __syncthreads();  // s_max is rewritten by the next term
+    const float G = amax > 0.0f ? __fdiv_rn(2688.0f, amax) : 1.0f;
+    const float g = __fdiv_rn(1.0f, G);
+    const int64_t orow = row * NT + t;
+    uint8_t* qrow = q + orow * (K / 2);
+    uint8_t* sfrow = sf + orow * (K / 16);
+    float next_amax = 0.0f;
+#pragma unroll
+    for (int i = 0; i < PAIRS; ++i) {
+      const int k = i * 2 * kSplitThreads + 2 * tid;  // first element of the pair
+      if (i < npairs && k < K) {
+        float bmax = fmaxf(fabsf(v[i].x), fabsf(v[i].y));
+        bmax = fmaxf(bmax, __shfl_xor_sync(0xffffffffu, bmax, 1));
+        bmax = fmaxf(bmax, __shfl_xor_sync(0xffffffffu, bmax, 2));
+        bmax = fmaxf(bmax, __shfl_xor_sync(0xffffffffu, bmax, 4));
+        const float scale = fminf(__fmul_rn(G, __fmul_rn(bmax, 1.0f / 6.0f)), 448.0f);
+        const __nv_fp8_storage_t s8 = __nv_cvt_float_to_fp8(scale, __NV_SATFINITE, __NV_E4M3);
+        const float sg = __fmul_rn(e4m3_to_float(s8), g);  // one e2m1 step of this block
+        const float inv = sg == 0.0f ? 0.0f : __frcp_rn(sg);
+        // nearest e2m1 (ties to even, saturating at 6) of both elements
+        const uint32_t pair = e2m1x2_from_f32(__fmul_rn(v[i].x, inv), __fmul_rn(v[i].y, inv));
+        const float2 dq = e2m1x2_to_float2(pair);
+        const uint32_t c0 = pair & 0xFu, c1 = pair >> 4;
+        // the MMA sees e2m1 * e4m3 * g; the next term quantises what is left
+        v[i].x -= __fmul_rn(dq.x, sg);
+        v[i].y -= __fmul_rn(dq.y, sg);
+        next_amax = fmaxf(next_amax, fmaxf(fabsf(v[i].x), fabsf(v[i].y)));
+        uint32_t w = (c0 | (c1 << 4)) << (8 * (lane & 3));
+        w |= __shfl_xor_sync(0xffffffffu, w, 1);
+        w |= __shfl_xor_sync(0xffffffffu, w, 2);
+        if ((lane & 3) == 0) *reinterpret_cast<uint32_t*>(qrow + k / 2) = w;
+        if ((lane & 7) == 0) sfrow[k / 16] = static_cast<uint8_t>(s8);
+      }
+    }
+    if (tid == 0) gout[orow] = g;
+    amax = next_amax;
+  }
+}
+
+// ---- host ---------------------------------------------------------------------
+
+PFN_cuTensorMapEncodeTiled_v12000 get_encode() {
+  static PFN_cuTensorMapEncodeTiled_v12000 fn = nullptr;
+  static std::once_flag once;
+  std::call_once(once, [] {
+    void* ptr = nullptr;
+    cudaDriverEntryPointQueryResult qr;
+    if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &ptr, cudaEnableDefault, &qr) ==
+            cudaSuccess &&
+        qr == cudaDriverEntryPointSuccess)
+      fn = reinterpret_cast<PFN_cuTensorMapEncodeTiled_v12000>(ptr);
+  });
+  return fn;
+}
+
+bool encode_u8(CUtensorMap* map, const void* base, uint64_t inner, uint64_t rows,
+               uint32_t box_inner, uint32_t box_rows, CUtensorMapSwizzle swz) {
+  auto fn = get_encode();
+  if (!fn) return false;
+  const cuuint64_t dims[2] = {inner, rows};
+  const cuuint64_t strides[1] = {inner};
+  const cuuint32_t box[2] = {box_inner, box_rows};
+  const cuuint32_t estr[2] = {1, 1};
+  return fn(map, CU_TENSOR_MAP_DATA_TYPE_UINT8, 2, const_cast<void*>(base), dims, strides, box,
+            estr, CU_TENSOR_MAP_INTERLEAVE_NONE, swz, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+            CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
+}
+
+template <int MODE, int BNR, int NT>
+cudaError_t launch_gemm(const CUtensorMap& a, const CUtensorMap& sa, const CUtensorMap& b,
+                        const CUtensorMap& sb, const BsParams& p, int grid, cudaStream_t stream) {
+  using C = BsCfg<MODE, BNR, NT>;
+  auto kern = moe_gemm_bs_kernel<MODE, BNR, NT>;
+  int dev = 0;
+  cudaError_t err = cudaGetDevice(&dev);
+  if (err != cudaSuccess) return err;
+  static bool attr[64] = {};
+  if (dev >= 0 && dev < 64 && !attr[dev]) {
+    err = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, C::kSmem);
+    if (err != cudaSuccess) return err;
+    attr[dev] = true;
+  }
+  kern<<<grid, kThreads, C::kSmem, stream>>>(a, sa, b, sb, p);
+  return cudaGetLastError();
+}
+
+template <int MODE>
+cudaError_t launch_bnr(int bnr, const CUtensorMap& a, const CUtensorMap& sa, const CUtensorMap& b,
+                       const CUtensorMap& sb, const BsParams& p, int grid, cudaStream_t stream) {
+  switch (bnr) {
+    case 16: return launch_gemm<MODE, 16, kSplitTerms>(a, sa, b, sb, p, grid, stream);
+    case 32: return launch_gemm<MODE, 32, kSplitTerms>(a, sa, b, sb, p, grid, stream);
+    case 64: return launch_gemm<MODE, 64, kSplitTerms>(a, sa, b, sb, p, grid, stream);
+    case 128: return launch_gemm<MODE, 128, kSplitTerms>(a, sa, b, sb, p, grid, stream);
+    default: return cudaErrorInvalidValue;
+  }
+}
+
+int sm_count() {
+  int dev = 0, n = 148;
+  if (cudaGetDevice(&dev) == cudaSuccess)
+    cudaDeviceGetAttribute(&n, cudaDevAttrMultiProcessorCount, dev);
+  return n;
+}
+
+cudaError_t launch_split(const void* src, int src_dt, const int32_t* sorted, int top_k,
+                         const int32_t* n_rows_dev, int64_t n_rows_max, int K, uint8_t* q,
+                         uint8_t* sf, float* g, cudaStream_t stream) {
+  if (n_rows_max <= 0) return cudaSuccess;
+  const int pairs = (K + 2 * kSplitThreads - 1) / (2 * kSplitThreads);
+  const unsigned grid = static_cast<unsigned>(n_rows_max);
+  if (pairs <= 1)
+    split_nvfp4_kernel<1><<<grid, kSplitThreads, 0, stream>>>(src, src_dt, sorted, top_k,
+                                                              n_rows_dev, K, kSplitTerms, q, sf, g);
+  else if (pairs <= 4)
+    split_nvfp4_kernel<4><<<grid, kSplitThreads, 0, stream>>>(src, src_dt, sorted, top_k,
+                                                              n_rows_dev, K, kSplitTerms, q, sf, g);
+  else if (pairs <= 8)
+    split_nvfp4_kernel<8><<<grid, kSplitThreads, 0, stream>>>(src, src_dt, sorted, top_k,
+                                                              n_rows_dev, K, kSplitTerms, q, sf, g);
+  else
+    split_nvfp4_kernel<kSplitMaxPairs><<<grid, kSplitThreads, 0, stream>>>(
+        src, src_dt, sorted, top_k, n_rows_dev, K, kSplitTerms, q, sf, g);
+  return cudaGetLastError();
+}
+
+}  // namespace
+
+bool bs_supported(int K, int I) {
+  return K % kBK == 0 && I % kBK == 0 && K <= 16384 && I <= 16384 && get_encode() != nullptr;
+}
+
+// term rows per MMA tile: enough for ~1.5x the mean routes per expert
+int bs_tile_rows(int64_t routes, int E, int mode) {
+  const double per = static_cast<double>(routes) / E * 1.5;
+  int tok = 4;
+  (void)mode;
+  while (tok < per && tok * kSplitTerms < 64) tok *= 2;
+  return tok * kSplitTerms;
+}
+
+cudaError_t launch_moe_bs(const BsLaunch& a, cudaStream_t stream, const char** step) {
+  const int64_t R = a.R;
+  const int NT = kSplitTerms;
+  const int grid = sm_count();
+  *step = "activation split";
+  cudaError_t err = launch_split(a.hidden, a.act_dt, a.sorted, a.top_k, a.offsets + a.E, R, a.K,
+                                 a.xq, a.xsf, a.xg, stream);
+  if (err != cudaSuccess) return err;
+  if (a.stage_mark) a.stage_mark(a.stage_ctx, 1);
+  const uint64_t brows = static_cast<uint64_t>(R > 0 ? R : 1) * NT;
+  {
+    *step = "gate/up tensor maps";
+    CUtensorMap ta, tsa, tb, tsb;
+    const int bnr = bs_tile_rows(R, a.E, kGateUp);
+    if (!encode_u8(&ta, a.w13, a.K / 2, (uint64_t)a.E * 2 * a.I, kRowBytes, kM,
+                   CU_TENSOR_MAP_SWIZZLE_128B) ||
+        !encode_u8(&tsa, a.s13, a.K / 16, (uint64_t)a.E * 2 * a.I, kRowScales, kM,
+                   CU_TENSOR_MAP_SWIZZLE_NONE) ||
+        !encode_u8(&tb, a.xq, a.K / 2, brows, kRowBytes, bnr, CU_TENSOR_MAP_SWIZZLE_128B) ||
+        !encode_u8(&tsb, a.xsf, a.K / 16, brows, kRowScales, bnr, CU_TENSOR_MAP_SWIZZLE_NONE))
+      return cudaErrorInvalidValue;
+    BsParams p{};
+    p.counts = a.counts;
+    p.offsets = a.offsets;
+    p.gscale = a.g13;
+    p.bg = a.xg;
+    p.out = a.h;
+    p.status = a.status;
+    p.E = a.E;
+    p.I = a.I;
+    p.m_tiles = a.I / kM;
+    p.a_stride = a.I;
+    p.k_stages = a.K / kBK;
+    p.rows_per_expert = 2 * a.I;
+    p.out_ld = a.I;
+    *step = "gate/up";
+    err = launch_bnr<kGateUp>(bnr, ta, tsa, tb, tsb, p, grid, stream);
+    if (err != cudaSuccess) return err;
+  }
+  *step = "h split";
+  err = launch_split(a.h, kF32, nullptr, 1, a.offsets + a.E, R, a.I, a.hq, a.hsf, a.hg, stream);
+  if (err != cudaSuccess) return err;
+  if (a.stage_mark) a.stage_mark(a.stage_ctx, 2);
+  {
+    *step = "down tensor maps";
+    CUtensorMap ta, tsa, tb, tsb;
+    const int bnr = bs_tile_rows(R, a.E, kDown);
+    if (!encode_u8(&ta, a.w2, a.I / 2, (uint64_t)a.E * a.K, kRowBytes, kM,
+                   CU_TENSOR_MAP_SWIZZLE_128B) ||
+        !encode_u8(&tsa, a.s2, a.I / 16, (uint64_t)a.E * a.K, kRowScales, kM,
+                   CU_TENSOR_MAP_SWIZZLE_NONE) ||
+        !encode_u8(&tb, a.hq, a.I / 2, brows, kRowBytes, bnr, CU_TENSOR_MAP_SWIZZLE_128B) ||
+        !encode_u8(&tsb, a.hsf, a.I / 16, brows, kRowScales, bnr, CU_TENSOR_MAP_SWIZZLE_NONE))
+      return cudaErrorInvalidValue;
+    BsParams p{};
+    p.counts = a.counts;
+    p.offsets = a.offsets;
+    p.gscale = a.g2;
+    p.bg = a.hg;
+    p.out = a.y;
+    p.status = a.status;
+    p.E = a.E;
+    p.I = a.I;
+    p.m_tiles = a.K / (2 * kM);
+    p.a_stride = kM;
+    p.k_stages = a.I / kBK;
+    p.rows_per_expert = a.K;
+    p.out_ld = a.K;
+    *step = "down";
+    err = launch_bnr<kDown>(bnr, ta, tsa, tb, tsb, p, grid, stream);
+    if (err != cudaSuccess) return err;
+  }
+  if (a.stage_mark) a.stage_mark(a.stage_ctx, 3);
+  return cudaSuccess;
+}
+
+}  // namespace sbb

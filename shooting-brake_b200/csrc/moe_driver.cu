@@ -31,6 +31,13 @@ WorkspacePlan plan_workspace(size_t M, size_t E, size_t top_k, size_t K, size_t 
   p.xperm = take(R * K * 2);
   p.xscale = take(R * sizeof(float));
   p.h = take(R * I * sizeof(float));
+  const size_t RT = R * kSplitTerms;
+  p.xq = take(RT * K / 2);
+  p.xsf = take(RT * K / 16);
+  p.xg = take(RT * sizeof(float));
+  p.hq = take(RT * I / 2);
+  p.hsf = take(RT * I / 16);
+  p.hg = take(RT * sizeof(float));
   p.y = take(R * K * sizeof(float));
   p.total = at;
   return p;
@@ -60,7 +67,48 @@ cudaError_t run_moe(const MoeArgs& a, const WorkspacePlan& plan, void* workspace
   err = launch_route_plan(a.ids, R, a.E, chunk_counts, counts, offsets, sorted, slot_of, status,
                           stream);
   if (err != cudaSuccess) { *why = "route plan"; return err; }
-  if (tc_supported(a.K, a.I, a.act_dt)) {
+  if (bs_supported(a.K, a.I)) {
+    BsLaunch t{};
+    t.hidden = a.hidden;
+    t.act_dt = a.act_dt;
+    t.counts = counts;
+    t.offsets = offsets;
+    t.sorted = sorted;
+    t.w13 = a.w13;
+    t.s13 = a.s13;
+    t.w2 = a.w2;
+    t.s2 = a.s2;
+    t.g13 = a.g13;
+    t.g2 = a.g2;
+    t.xq = reinterpret_cast<uint8_t*>(ws + plan.xq);
+    t.xsf = reinterpret_cast<uint8_t*>(ws + plan.xsf);
+    t.xg = reinterpret_cast<float*>(ws + plan.xg);
+    t.h = h;
+    t.hq = reinterpret_cast<uint8_t*>(ws + plan.hq);
+    t.hsf = reinterpret_cast<uint8_t*>(ws + plan.hsf);
+    t.hg = reinterpret_cast<float*>(ws + plan.hg);
+    t.y = y;
+    t.status = status;
+    t.R = R;
+    t.E = a.E;
+    t.top_k = a.top_k;
+    t.K = a.K;
+    t.I = a.I;
+    struct Ctx {
+      void* const* ev;
+      cudaStream_t s;
+    } ctx{a.stage_events, stream};
+    if (a.stage_events) {
+      t.stage_mark = [](void* c, int i) {
+        auto* x = static_cast<Ctx*>(c);
+        if (x->ev[i]) cudaEventRecord(static_cast<cudaEvent_t>(x->ev[i]), x->s);
+      };
+      t.stage_ctx = &ctx;
+    }
+    const char* step = "block-scaled path";
+    err = launch_moe_bs(t, stream, &step);
+    if (err != cudaSuccess) { *why = step; return err; }
+  } else if (tc_supported(a.K, a.I, a.act_dt)) {
     TcLaunch t{};
     t.hidden = a.hidden;
     t.act_dt = a.act_dt;

@@ -23,7 +23,9 @@ struct WorkspacePlan {
   size_t slot_of;       // int32[R]   sorted slot per route, -1 if dropped
   size_t xperm;         // f16[R, K]  scaled activation rows per slot (tcgen05 path)
   size_t xscale;        // fp32[R]    their power-of-two scales
-  size_t h;             // fp32[R, I] SwiGLU activations per slot (bf16 on the tcgen05 path)
+  size_t h;             // fp32[R, I] SwiGLU activations per slot
+  size_t xq, xsf, xg;   // activation split terms: [R*NT, K/2], [R*NT, K/16], fp32 [R*NT]
+  size_t hq, hsf, hg;   // SwiGLU split terms:     [R*NT, I/2], [R*NT, I/16], fp32 [R*NT]
   size_t y;             // fp32[R, K] down-projection output per slot
   size_t total;
 };

@@ -36,8 +36,13 @@
 // (exact for bf16/f16 inputs) and the epilogue multiplies it back. Down uses
 // bf16 operands because h has no a-priori range bound.
 //
-// Tensor memory (512 columns): two A slots of 128 columns at [0, 256), the
-// double-buffered accumulators at [256, 512).
+// Tensor memory (512 columns): a ring of four A slots of 64 columns (one
+// 128-row block x 128 K elements) at [0, 256) and two accumulator buffers of
+// 128 columns at [256, 512). MMAs that accumulate into the same tile
+// serialise on the tensor-core pipeline latency, which at N = 16 costs far
+// more than the MMA itself, so consecutive K steps rotate over P independent
+// partial accumulators (P = 64/BN for gate/up, whose gate and up chains also
+// interleave, and 128/BN for down) that the epilogue sums.
 //
 // Every wait is an mbarrier try-wait loop with a deadline; on timeout the
 // kernel raises status[1], drains its own in-flight copies and MMAs, frees
@@ -62,8 +67,7 @@ constexpr int kRowBytes = kBK / 2;   // packed bytes per weight row per stage (1
 constexpr int kRowScales = kBK / 16; // scale bytes per weight row per stage (16)
 constexpr int kM = 128;              // MMA M
 constexpr int kThreads = 512;
-constexpr int kSlotCols = 128;       // TMEM columns of one A slot
-constexpr int kDCol0 = 256;          // first accumulator column
+constexpr int kSlotCols = 64;        // TMEM columns of one A slot (128 K elements)
 constexpr int kTmemCols = 512;
 constexpr uint64_t kTimeoutNs = 2000000000ull;  // 2 s per wait
 constexpr int kMaxUnitsE = kMaxExperts;
@@ -95,11 +99,21 @@ struct Cfg {
   static constexpr int kStagesRaw = (200 * 1024) / kStageBytes;
   static constexpr int kStages = kStagesRaw > 8 ? 8 : (kStagesRaw < 2 ? 2 : kStagesRaw);
   static constexpr int kSmem = kStages * kStageBytes + 1024;
-  static constexpr int kSlotsPerStage = MODE == kGateUp ? 2 : 1;
-  static constexpr int kDCols = MODE == kGateUp ? 2 * BN : BN;  // one accumulator buffer
+  // A-slot uses per stage: (128-row block, K half) pairs. Even uses belong to
+  // dequant warpgroup 0, odd ones to warpgroup 1.
+  static constexpr int kUsesPerStage = 2 * kNA;
+  // Partial accumulators per output and accumulator buffers; what they leave
+  // of tensor memory forms the A ring (at most 8 slots).
+  static constexpr int kP = MODE == kGateUp ? (BN <= 16 ? 2 : 1) : (BN <= 16 ? 4 : (BN <= 32 ? 2 : 1));
+  static constexpr int kDBufs = 2;
+  static constexpr int kOutCols = kP * BN;                             // one output (gate, up or y)
+  static constexpr int kDCols = (MODE == kGateUp ? 2 : 1) * kOutCols;  // one buffer
+  static constexpr int kDCol0 = kTmemCols - kDBufs * kDCols;
+  static constexpr int kSlotsRaw = kDCol0 / kSlotCols;
+  static constexpr int kSlots = kSlotsRaw > 8 ? 8 : kSlotsRaw;
   static constexpr uint32_t kIdesc = idesc_f16(MODE == kGateUp ? 0u : 1u, kM, BN);
   static_assert(kStageBytes % 1024 == 0, "stages must keep 1024-byte alignment");
-  static_assert(kDCol0 + 2 * kDCols <= kTmemCols, "accumulators exceed tensor memory");
+  static_assert(kSlots >= 2, "accumulators leave no room for an A ring");
   static_assert(kStageBytes * 2 + 1024 <= 227 * 1024, "two stages must fit");
 };
 
@@ -198,8 +212,9 @@ __global__ void __launch_bounds__(kThreads, 1)
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) &
                                              ~static_cast<uintptr_t>(1023));
-  __shared__ __align__(8) uint64_t full[S], empty[S], afull[2], aempty[2], dfull[2], dempty[2],
-      done_bar;
+  constexpr int NS = C::kSlots;
+  __shared__ __align__(8) uint64_t full[S], empty[S], afull[NS], aempty[NS], dfull[C::kDBufs],
+      dempty[C::kDBufs], done_bar;
   __shared__ uint32_t tmem_base_s;
   __shared__ int abort_s;
   __shared__ int prefix[kMaxUnitsE + 1];
@@ -215,9 +230,11 @@ __global__ void __launch_bounds__(kThreads, 1)
       mbar_init(&full[i], 1);
       mbar_init(&empty[i], 8 + 1);
     }
-    for (int i = 0; i < 2; ++i) {
-      mbar_init(&afull[i], 8);
+    for (int i = 0; i < NS; ++i) {
+      mbar_init(&afull[i], 4);
       mbar_init(&aempty[i], 1);
+    }
+    for (int i = 0; i < C::kDBufs; ++i) {
       mbar_init(&dfull[i], 1);
       mbar_init(&dempty[i], 4);
     }
@@ -317,14 +334,15 @@ __global__ void __launch_bounds__(kThreads, 1)
     if (lane == 0) {
       int s = 0;
       uint32_t ph = 0;
-      uint32_t it = 0;  // A slot sequence number
+      int slot = 0;         // A ring position
+      uint32_t sph = 0;     // A ring phase
       uint32_t ui = 0;
       bool ok = true;
       for (int u = blockIdx.x; u < total_units && ok; u += gridDim.x, ++ui) {
-        const int d = ui & 1;
-        if (!mbar_wait(&dempty[d], ((ui >> 1) & 1u) ^ 1u, abort, deadline)) break;
+        const int d = ui % C::kDBufs;
+        if (!mbar_wait(&dempty[d], ((ui / C::kDBufs) & 1u) ^ 1u, abort, deadline)) break;
         tc_fence_after();
-        const uint32_t d_tm = tmem + kDCol0 + d * C::kDCols;
+        const uint32_t d_tm = tmem + C::kDCol0 + d * C::kDCols;
         for (int kk = 0; kk < p.k_stages && ok; ++kk) {
           if (!mbar_wait(&full[s], ph, abort, deadline)) {
             ok = false;
@@ -332,37 +350,49 @@ __global__ void __launch_bounds__(kThreads, 1)
           }
           const uint32_t b_saddr = smem_u32(smem + s * C::kStageBytes + C::kAStage);
 #pragma unroll
-          for (int h = 0; h < C::kSlotsPerStage; ++h) {
-            const int slot = it & 1;
-            if (!mbar_wait(&afull[slot], (it >> 1) & 1u, abort, deadline)) {
+          for (int khalf = 0; khalf < 2; ++khalf) {
+            // gate/up: uses (gate, khalf) and (up, khalf) sit at consecutive
+            // ring positions; down: one use per K half.
+            int slot2 = slot;
+            uint32_t sph2 = sph;
+            if (MODE == kGateUp) {
+              slot2 = slot + 1;
+              if (slot2 == NS) {
+                slot2 = 0;
+                sph2 ^= 1u;
+              }
+            }
+            if (!mbar_wait(&afull[slot], sph, abort, deadline) ||
+                (MODE == kGateUp && !mbar_wait(&afull[slot2], sph2, abort, deadline))) {
               ok = false;
               break;
             }
             tc_fence_after();
-            const uint32_t a_tm = tmem + slot * kSlotCols;
-            if (MODE == kGateUp) {
-              // slot = [gate K-half: 64 cols | up K-half: 64 cols]
+            const uint32_t a0 = tmem + slot * kSlotCols;
+            const uint32_t a1 = tmem + slot2 * kSlotCols;
 #pragma unroll
-              for (int j = 0; j < 8; ++j) {
-                const int kel = h * 128 + j * 16;
-                const uint64_t bd =
-                    desc_sw128(b_saddr + (kel >> 6) * (BN * 128) + (kel & 63) * 2);
-                const uint32_t acc = (kk | h | j) != 0;
-                mma_f16_ts(d_tm, a_tm + j * 8, bd, C::kIdesc, acc);
-                mma_f16_ts(d_tm + BN, a_tm + 64 + j * 8, bd, C::kIdesc, acc);
-              }
-            } else {
-              // slot = one full K stage: 16 steps of K=16
-#pragma unroll
-              for (int j = 0; j < 16; ++j) {
-                const int kel = j * 16;
-                const uint64_t bd =
-                    desc_sw128(b_saddr + (kel >> 6) * (BN * 128) + (kel & 63) * 2);
-                mma_f16_ts(d_tm, a_tm + j * 8, bd, C::kIdesc, (kk | j) != 0);
-              }
+            for (int m = 0; m < 8; ++m) {
+              const int kel = khalf * 128 + m * 16;
+              const uint64_t bd = desc_sw128(b_saddr + (kel >> 6) * (BN * 128) + (kel & 63) * 2);
+              const int step = (MODE == kGateUp ? 0 : khalf * 8) + m;  // step within K half pair
+              const int part = step % C::kP;
+              // a partial's first MMA of the unit overwrites it
+              const uint32_t acc = (kk != 0 || khalf != 0 || step >= C::kP) ? 1u : 0u;
+              const uint32_t accg = MODE == kGateUp ? ((kk != 0 || khalf != 0 || m >= C::kP) ? 1u : 0u) : acc;
+              mma_f16_ts(d_tm + part * BN, a0 + m * 8, bd, C::kIdesc, accg);
+              if (MODE == kGateUp)
+                mma_f16_ts(d_tm + C::kOutCols + part * BN, a1 + m * 8, bd, C::kIdesc, accg);
             }
             mma_commit(&aempty[slot]);
-            ++it;
+            if (MODE == kGateUp) mma_commit(&aempty[slot2]);
+            const int adv = MODE == kGateUp ? 2 : 1;
+#pragma unroll
+            for (int a = 0; a < adv; ++a) {
+              if (++slot == NS) {
+                slot = 0;
+                sph ^= 1u;
+              }
+            }
           }
           if (!ok) break;
           mma_commit(&empty[s]);
@@ -388,7 +418,8 @@ __global__ void __launch_bounds__(kThreads, 1)
     const uint32_t lane_base = static_cast<uint32_t>(q * 32) << 16;
     int s = 0;
     uint32_t ph = 0;
-    uint32_t it = 0;
+    int slot = wg;         // this warpgroup's position in the A ring
+    uint32_t sph = 0;
     bool ok = true;
     for (int u = blockIdx.x; u < total_units && ok; u += gridDim.x) {
       for (int kk = 0; kk < p.k_stages && ok; ++kk) {
@@ -399,36 +430,41 @@ __global__ void __launch_bounds__(kThreads, 1)
         const uint8_t* st = smem + s * C::kStageBytes;
         const uint8_t* ss = st + C::kAStage + C::kBStage;
 #pragma unroll
-        for (int h = 0; h < C::kSlotsPerStage; ++h) {
-          const int slot = it & 1;
-          if (!warp_wait(&aempty[slot], ((it >> 1) & 1u) ^ 1u, abort, deadline)) {
+        for (int j = wg; j < C::kUsesPerStage; j += 2) {
+          if (!warp_wait(&aempty[slot], sph ^ 1u, abort, deadline)) {
             ok = false;
             break;
           }
-          // gate/up: warpgroup wg owns the gate (0) or up (1) rows, h selects
-          // the K half; down: warpgroup wg owns K half wg of the stage.
+          // gate/up: warpgroup wg owns the gate (0) or up (1) rows and use j
+          // selects the K half; down: warpgroup wg owns K half wg.
           const int arow = MODE == kGateUp ? wg * kM + row : row;
-          const int khalf = MODE == kGateUp ? h : wg;
+          const int khalf = MODE == kGateUp ? (j >> 1) : wg;
           const uint8_t* ap = st + arow * kRowBytes;
           uint4 qv[4];
 #pragma unroll
           for (int c = 0; c < 4; ++c) {
-            const int j = khalf * 4 + c;
-            qv[c] = *reinterpret_cast<const uint4*>(ap + ((j ^ (arow & 7)) << 4));
+            const int jj = khalf * 4 + c;
+            qv[c] = *reinterpret_cast<const uint4*>(ap + ((jj ^ (arow & 7)) << 4));
           }
           const uint2 sc = *reinterpret_cast<const uint2*>(ss + arow * kRowScales + khalf * 8);
           uint32_t r[64];
           if (MODE == kGateUp) dequant_f16(qv, sc, r);
           else dequant_bf16(qv, sc, r);
-          const uint32_t col = slot * kSlotCols + (MODE == kGateUp ? wg * 64 : wg * 64);
-          const uint32_t taddr = tmem + lane_base + col;
+          const uint32_t taddr = tmem + lane_base + slot * kSlotCols;
           tmem_st32(taddr, r);
           tmem_st32(taddr + 32, r + 32);
           tmem_wait_st();
           tc_fence_before();
           __syncwarp();
           if (lane == 0) mbar_arrive(&afull[slot]);
-          ++it;
+          // advance two ring positions: the other warpgroup takes the one between
+#pragma unroll
+          for (int step = 0; step < 2; ++step) {
+            if (++slot == NS) {
+              slot = 0;
+              sph ^= 1u;
+            }
+          }
         }
         if (!ok) break;
         if (lane == 0) mbar_arrive(&empty[s]);
@@ -447,41 +483,64 @@ __global__ void __launch_bounds__(kThreads, 1)
     for (int u = blockIdx.x; u < total_units; u += gridDim.x, ++ui) {
       int e, nt, mt;
       decode_unit(u, p.m_tiles, prefix, p.E, e, nt, mt);
-      const int d = ui & 1;
-      if (!warp_wait(&dfull[d], (ui >> 1) & 1u, abort, deadline)) break;
+      const int d = ui % C::kDBufs;
+      if (!warp_wait(&dfull[d], (ui / C::kDBufs) & 1u, abort, deadline)) break;
       tc_fence_after();
       const int valid = min(BN, p.counts[e] - nt * BN);
       const int slot0 = p.offsets[e] + nt * BN;
       const float gs = p.gscale[e];
-      const uint32_t taddr = tmem + lane_base + kDCol0 + d * C::kDCols;
+      const uint32_t taddr = tmem + lane_base + C::kDCol0 + d * C::kDCols;
 #pragma unroll 1
       for (int c0 = 0; c0 < BN; c0 += 16) {
-        uint32_t v[16];
-        tmem_ld16(taddr + c0, v);
-        if (MODE == kGateUp) {
-          uint32_t w[16];
-          tmem_ld16(taddr + BN + c0, w);
+        float v[16];
+        {
+          uint32_t t[16];
+          tmem_ld16(taddr + c0, t);
           tmem_wait_ld();
+#pragma unroll
+          for (int j = 0; j < 16; ++j) v[j] = __uint_as_float(t[j]);
+#pragma unroll
+          for (int pp = 1; pp < C::kP; ++pp) {
+            tmem_ld16(taddr + pp * BN + c0, t);
+            tmem_wait_ld();
+#pragma unroll
+            for (int j = 0; j < 16; ++j) v[j] += __uint_as_float(t[j]);
+          }
+        }
+        if (MODE == kGateUp) {
+          float w[16];
+          {
+            uint32_t t[16];
+            tmem_ld16(taddr + C::kOutCols + c0, t);
+            tmem_wait_ld();
+#pragma unroll
+            for (int j = 0; j < 16; ++j) w[j] = __uint_as_float(t[j]);
+#pragma unroll
+            for (int pp = 1; pp < C::kP; ++pp) {
+              tmem_ld16(taddr + C::kOutCols + pp * BN + c0, t);
+              tmem_wait_ld();
+#pragma unroll
+              for (int j = 0; j < 16; ++j) w[j] += __uint_as_float(t[j]);
+            }
+          }
           __nv_bfloat16* h = static_cast<__nv_bfloat16*>(p.out);
           const int f = mt * kM + r;
 #pragma unroll
           for (int j = 0; j < 16; ++j) {
             if (c0 + j < valid) {
               const float sc = gs * p.xscale[slot0 + c0 + j];
-              const float gv = __uint_as_float(v[j]) * sc;
-              const float uv = __uint_as_float(w[j]) * sc;
+              const float gv = v[j] * sc;
+              const float uv = w[j] * sc;
               h[static_cast<int64_t>(slot0 + c0 + j) * p.out_ld + f] =
                   __float2bfloat16_rn(silu(gv) * uv);
             }
           }
         } else {
-          tmem_wait_ld();
           float* y = static_cast<float*>(p.out);
 #pragma unroll
           for (int j = 0; j < 16; ++j) {
             if (c0 + j < valid)
-              y[static_cast<int64_t>(slot0 + c0 + j) * p.out_ld + mt * kM + r] =
-                  __uint_as_float(v[j]) * gs;
+              y[static_cast<int64_t>(slot0 + c0 + j) * p.out_ld + mt * kM + r] = v[j] * gs;
           }
         }
       }
