@@ -130,6 +130,22 @@ int sbb200_route_plan(void* stream, const int32_t* topk_ids, size_t M, size_t to
                       int32_t* counts, int32_t* offsets, int32_t* sorted, int32_t* slot_of,
                       void* scratch, uint32_t* bad_ids);
 
+/* sbb200_route_plan without allocation, for callers that cannot give the
+ * library device memory: code inside a CUDA stream capture, engines whose
+ * device memory is owned by a pooling allocator, FFI bindings without a
+ * device allocator. Same arguments and results as sbb200_route_plan minus
+ * the scratch: its scratch is a fixed 128 KB array in the library's device
+ * image (held on every device that loads the library until exit), so it
+ * handles at most 262144 routes (M * top_k) and E <= 512; larger calls fail
+ * with SBB200_EUNSUPPORTED. The first call on a device resolves that array's
+ * device address (cudaGetSymbolAddress), so make the first call on each
+ * device before any stream capture. All calls share the array: calls that
+ * overlap on the GPU (different streams, or several host threads) race and
+ * must be serialised by the caller. Has no counterpart in the reference. */
+int sbb200_route_plan_static(void* stream, const int32_t* topk_ids, size_t M, size_t top_k,
+                             size_t E, int32_t* counts, int32_t* offsets, int32_t* sorted,
+                             int32_t* slot_of, uint32_t* bad_ids);
+
 /* Bit-exact NVFP4 dequant: out[r, c] = e2m1 * fp32(e4m3(sf[r, c/16]) * g[r /
  * rows_per_scale]) (src/phase7/cpu_expert_capi.cpp:301-346). q [rows, cols/2],
  * sf [rows, cols/16], out fp32 [rows, cols]; cols % 16 == 0. */

@@ -38,6 +38,8 @@ bool dtype_ok(int dt) { return dt == SBB200_F32 || dt == SBB200_F16 || dt == SBB
 
 namespace sbb {
 
+void set_last_error(const std::string& msg) { t_last_error = msg; }
+
 int validate_shape(size_t M, size_t E, size_t top_k, size_t K, size_t I, int act_dt, int out_dt,
                    std::string* why) {
   if (M == 0 || E == 0 || top_k == 0 || K == 0 || I == 0) {

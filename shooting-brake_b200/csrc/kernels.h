@@ -6,9 +6,14 @@
 #include <stddef.h>
 #include <stdint.h>
 
+#include <string>
+
 namespace sbb {
 
 constexpr int kRouteChunk = 4096;  // routes per CTA in the route plan
+
+// Sets the calling thread's message returned by sbb200_last_error.
+void set_last_error(const std::string& msg);
 constexpr int kMaxExperts = 512;   // route-plan shared-memory bound
 constexpr int kMaxTopK = 64;
 

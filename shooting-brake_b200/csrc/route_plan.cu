@@ -192,3 +192,103 @@ cudaError_t launch_route_plan(const int32_t* ids, int64_t R, int E, int32_t* chu
 }
 
 }  // namespace sbb
+
+// ---------------------------------------------------------------------------
+// Route plan without any allocation.
+//
+// Some callers cannot hand the library a workspace: code running inside a
+// CUDA stream capture (a cudaMalloc there is not part of the graph and can
+// stall the device), engines whose device memory belongs to a pooling
+// allocator that forbids allocations outside the pool, and thin FFI bindings
+// that have no device allocator at all. sbb200_route_plan_static serves them
+// with scratch that the library owns: the per-chunk expert counts live in the
+// file-scope array below, so a call allocates nothing.
+// ---------------------------------------------------------------------------
+#include <mutex>
+#include <string>
+
+#include "sbb200.h"
+
+namespace sbb {
+namespace {
+
+constexpr int64_t kStaticMaxRoutes = 262144;                      // M * top_k
+constexpr int kStaticChunks = static_cast<int>(kStaticMaxRoutes / kRouteChunk);  // 64
+constexpr int kStaticWords = kStaticChunks * kMaxExperts + 64;     // counts + status
+
+// 128 KB + 256 B on every device that loads the library, held until exit.
+// Every call shares it: [0, kStaticChunks * kMaxExperts) per-chunk counts
+// (fully rewritten by each multi-chunk call before it is read), then the
+// status word that counts out-of-range ids when the caller passes no counter
+// (cleared by each such call).
+static __device__ __align__(256) int32_t g_route_scratch[kStaticWords];
+
+std::mutex g_route_scratch_mu;
+int32_t* g_route_scratch_dev[64] = {};  // device address per device, from set-up
+
+}  // namespace
+}  // namespace sbb
+
+extern "C" int sbb200_route_plan_static(void* stream, const int32_t* topk_ids, size_t M,
+                                        size_t top_k, size_t E, int32_t* counts,
+                                        int32_t* offsets, int32_t* sorted, int32_t* slot_of,
+                                        uint32_t* bad_ids) {
+  using namespace sbb;
+  const size_t R = M * top_k;
+  if (E == 0 || E > static_cast<size_t>(kMaxExperts)) {
+    set_last_error("route_plan_static: E must be in [1, 512]");
+    return SBB200_EINVAL;
+  }
+  if (R > static_cast<size_t>(kStaticMaxRoutes)) {
+    set_last_error("route_plan_static: " + std::to_string(R) +
+                   " routes (M*top_k) exceed its static scratch limit of 262144; use "
+                   "sbb200_route_plan with a caller workspace");
+    return SBB200_EUNSUPPORTED;
+  }
+  if (!counts || !offsets || (R != 0 && (!topk_ids || !sorted || !slot_of))) {
+    set_last_error("route_plan_static received a null pointer");
+    return SBB200_EINVAL;
+  }
+  int dev = 0;
+  cudaError_t err = cudaGetDevice(&dev);
+  if (err != cudaSuccess || dev < 0 || dev >= 64) {
+    set_last_error(std::string("route_plan_static: no usable current device: ") +
+                   cudaGetErrorString(err));
+    return SBB200_ECUDA;
+  }
+  int32_t* scratch = nullptr;
+  {
+    // Set-up, once per device, with that device current: the array's name in
+    // host code is only a host-side stand-in, its device address comes from
+    // the runtime.
+    std::lock_guard<std::mutex> lock(g_route_scratch_mu);
+    if (!g_route_scratch_dev[dev]) {
+      void* p = nullptr;
+      err = cudaGetSymbolAddress(&p, g_route_scratch);
+      if (err != cudaSuccess || !p) {
+        set_last_error(std::string("route_plan_static: cudaGetSymbolAddress failed: ") +
+                       cudaGetErrorString(err));
+        return SBB200_ECUDA;
+      }
+      g_route_scratch_dev[dev] = static_cast<int32_t*>(p);
+    }
+    scratch = g_route_scratch_dev[dev];
+  }
+  cudaStream_t s = static_cast<cudaStream_t>(stream);
+  uint32_t* status = bad_ids;
+  if (!status) {
+    status = reinterpret_cast<uint32_t*>(scratch + kStaticChunks * kMaxExperts);
+    err = cudaMemsetAsync(status, 0, sizeof(uint32_t), s);
+    if (err != cudaSuccess) {
+      set_last_error(std::string("route_plan_static: ") + cudaGetErrorString(err));
+      return SBB200_ECUDA;
+    }
+  }
+  err = launch_route_plan(topk_ids, static_cast<int64_t>(R), static_cast<int>(E), scratch, counts,
+                          offsets, sorted, slot_of, status, s);
+  if (err != cudaSuccess) {
+    set_last_error(std::string("route_plan_static: ") + cudaGetErrorString(err));
+    return SBB200_ECUDA;
+  }
+  return SBB200_OK;
+}
