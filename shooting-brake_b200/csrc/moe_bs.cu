@@ -23,13 +23,14 @@
 // Work unit, persistent grid and warp specialisation as in moe_tc.cu:
 //   warp 0       TMA: packed weights (128-byte swizzle), their linear scale
 //                rows, the packed term rows and their scale rows.
-//   warp 1       TMEM allocation; one thread copies the stage's scale atoms
-//                to tensor memory (tcgen05.cp 32x128b.warpx4) and issues the
-//                MMAs.
-//   warps 4-7    scale warps: rearrange the linear e4m3 scale rows of the
-//                stage into the 32x4x4 atoms the MMA reads (row r = r0 +
-//                32*r1 of a 128-row block, 4 scales per 64-wide K group:
-//                byte r0*16 + r1*4 + kb).
+//   warp 1       TMEM allocation; one thread issues the MMAs.
+//   warps 4-7    scale warps: write the stage's e4m3 scales into tensor
+//                memory with tcgen05.st in the layout the block-scaled MMA
+//                reads: for a 128-row operand block and a 64-wide K group the
+//                4 scales of row r0 + 32*r1 sit in column c + r1 of lane r0
+//                of every 32-lane quarter. Writing them from registers keeps
+//                the tensor core's queue for MMAs only (a tcgen05.cp costs as
+//                much as an MMA there, and mixing the two serialises).
 //   warps 12-15  epilogue: fold terms, global scale, SwiGLU (gate/up) or the
 //                fp32 route output (down).
 // Every wait is bounded (the kernel raises status[1], drains and returns).
@@ -56,7 +57,6 @@ constexpr int kM = 128;
 constexpr int kThreads = 512;
 constexpr int kTmemCols = 512;
 constexpr uint64_t kTimeoutNs = 2000000000ull;
-constexpr int kAtom = 512;            // one 128-row x 4-scale atom
 
 enum : int { kGateUp = 0, kDown = 1 };
 
@@ -86,24 +86,29 @@ struct BsCfg {
   static constexpr int kB = BNR * kRowBytes;               // packed term rows
   static constexpr int kSA = kNA * kM * kRowScales;        // linear weight scales
   static constexpr int kSB = BNR * kRowScales;             // linear term scales
-  static constexpr int kAtoms = (kNA + 1) * 4 * kAtom;     // rearranged scales
-  static constexpr int kRaw = kA + kB + kSA + kSB + kAtoms;
+  static constexpr int kRaw = kA + kB + kSA + kSB;
   static constexpr int kStageBytes = (kRaw + 1023) / 1024 * 1024;
-  static constexpr int kStagesRaw = (200 * 1024) / kStageBytes;
+  static constexpr int kStagesRaw = (224 * 1024 - 1024) / kStageBytes;
   static constexpr int kStages = kStagesRaw > 8 ? 8 : (kStagesRaw < 2 ? 2 : kStagesRaw);
   static constexpr int kSmem = kStages * kStageBytes + 1024;
   static constexpr int kOffB = kA;
   static constexpr int kOffSA = kA + kB;
   static constexpr int kOffSB = kOffSA + kSA;
-  static constexpr int kOffAtoms = ((kOffSB + kSB + 127) / 128) * 128;
-  // tensor memory: accumulators then two scale buffers
+  // tensor memory: accumulators, then two scale buffers. Each operand gets 4
+  // columns per K group (the 4 row quarters of a 128-row block), so every
+  // scale address handed to the MMA is 4-column aligned; B fills the first
+  // ceil(rows / 32) of its 4.
   static constexpr int kDCols = kNA * BNR;
-  static constexpr int kDBufs = 2 * kDCols + 2 * (kNA + 1) * 16 <= kTmemCols ? 2 : 1;
+  static constexpr int kBQ = (BNR + 31) / 32;  // B row quarters in use
+  // per buffer, a multiple of 16 so every tcgen05.st (x4/x8/x16) starts on a
+  // column aligned to its width
+  static constexpr int kSfCols = (kNA + 1) * 16;
+  static constexpr int kDBufs = 2 * kDCols + 2 * kSfCols <= kTmemCols ? 2 : 1;
   static constexpr int kSfCol0 = kDBufs * kDCols;
-  static constexpr int kSfCols = (kNA + 1) * 16;  // per buffer
   static constexpr uint32_t kIdesc =
       (1u << 7) | (1u << 10) | (static_cast<uint32_t>(BNR >> 3) << 17) | ((kM >> 4) << 24);
-  static_assert(kOffAtoms + kAtoms <= kStageBytes, "stage layout");
+  static_assert(kSmem <= 227 * 1024, "shared memory");
+  static_assert(kSfCol0 % 16 == 0 && kSfCols % 16 == 0, "tensor-memory store alignment");
   static_assert(kSfCol0 + 2 * kSfCols <= kTmemCols, "tensor memory");
   static_assert(BNR % 16 == 0 && BNR >= 16 && BNR <= 256 && BNR % NT == 0, "tile");
 };
@@ -139,20 +144,6 @@ __device__ __forceinline__ bool warp_wait(uint64_t* bar, uint32_t parity, volati
   }
 }
 
-// no-swizzle descriptor of one 32 x 16-byte scale chunk (8-row core matrices
-// 128 bytes apart) for tcgen05.cp
-__device__ __forceinline__ uint64_t desc_atom(uint32_t saddr) {
-  uint64_t d = 0;
-  d |= static_cast<uint64_t>((saddr >> 4) & 0x3FFFu);
-  d |= static_cast<uint64_t>(128 >> 4) << 32;
-  d |= static_cast<uint64_t>(1) << 46;
-  return d;
-}
-
-__device__ __forceinline__ void tmem_cp_atom(uint32_t taddr, uint64_t desc) {
-  asm volatile("tcgen05.cp.cta_group::1.32x128b.warpx4 [%0], %1;" ::"r"(taddr), "l"(desc)
-               : "memory");
-}
 
 __device__ __forceinline__ void mma_bs(uint32_t d_tmem, uint64_t a_desc, uint64_t b_desc,
                                        uint32_t idesc, uint32_t sfa, uint32_t sfb,
@@ -175,8 +166,8 @@ __global__ void __launch_bounds__(kThreads, 1)
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) &
                                              ~static_cast<uintptr_t>(1023));
-  __shared__ __align__(8) uint64_t full[S], empty[S], sfready[S], dfull[NB], dempty[NB], sffree[2],
-      done_bar;
+  __shared__ __align__(8) uint64_t full[S], empty[S], sfready[2], dfull[NB], dempty[NB],
+      sffree[2], done_bar;
   __shared__ uint32_t tmem_base_s;
   __shared__ int abort_s;
   __shared__ int prefix[kMaxExperts + 1];
@@ -191,8 +182,8 @@ __global__ void __launch_bounds__(kThreads, 1)
     for (int i = 0; i < S; ++i) {
       mbar_init(&full[i], 1);
       mbar_init(&empty[i], 1 + 4);  // MMA commit + the four scale warps
-      mbar_init(&sfready[i], 4);
     }
+    for (int i = 0; i < 2; ++i) mbar_init(&sfready[i], 4);
     for (int i = 0; i < NB; ++i) {
       mbar_init(&dfull[i], 1);
       mbar_init(&dempty[i], 4);
@@ -300,25 +291,16 @@ __global__ void __launch_bounds__(kThreads, 1)
         for (int kk = 0; kk < p.k_stages; ++kk) {
           const int sb = it & 1;
           // the scale buffer's previous MMAs (two stages ago) are complete
-          if (!mbar_wait(&sffree[sb], ((it >> 1) & 1u) ^ 1u, abort, deadline) ||
-              !mbar_wait(&full[s], ph, abort, deadline) ||
-              !mbar_wait(&sfready[s], ph, abort, deadline)) {
+          if (!mbar_wait(&full[s], ph, abort, deadline) ||
+              !mbar_wait(&sfready[sb], (it >> 1) & 1u, abort, deadline)) {
             ok = false;
             break;
           }
           tc_fence_after();
           const uint8_t* st = smem + s * C::kStageBytes;
-          const uint32_t atoms = smem_u32(st + C::kOffAtoms);
           const uint32_t a_sa = smem_u32(st);
           const uint32_t b_sa = smem_u32(st + C::kOffB);
           const uint32_t sf0 = tmem + C::kSfCol0 + sb * C::kSfCols;
-#pragma unroll
-          for (int kg = 0; kg < 4; ++kg) {
-#pragma unroll
-            for (int a = 0; a < C::kNA; ++a)
-              tmem_cp_atom(sf0 + (a * 4 + kg) * 4, desc_atom(atoms + (a * 4 + kg) * kAtom));
-            tmem_cp_atom(sf0 + (C::kNA * 4 + kg) * 4, desc_atom(atoms + (C::kNA * 4 + kg) * kAtom));
-          }
 #pragma unroll
           for (int kg = 0; kg < 4; ++kg) {
             const uint64_t bd = desc_sw128(b_sa + kg * 32);
@@ -326,8 +308,8 @@ __global__ void __launch_bounds__(kThreads, 1)
 #pragma unroll
             for (int a = 0; a < C::kNA; ++a) {
               const uint64_t ad = desc_sw128(a_sa + a * kM * kRowBytes + kg * 32);
-              mma_bs(d_tm + a * BNR, ad, bd, C::kIdesc, sf0 + (a * 4 + kg) * 4,
-                     sf0 + (C::kNA * 4 + kg) * 4, acc);
+              mma_bs(d_tm + a * BNR, ad, bd, C::kIdesc, sf0 + a * 16 + kg * 4,
+                     sf0 + C::kNA * 16 + kg * 4, acc);
             }
           }
           mma_commit(&empty[s]);
@@ -347,44 +329,60 @@ __global__ void __launch_bounds__(kThreads, 1)
       }
     }
   } else if (warp >= 4 && warp < 8) {
-    // ---------------- scale rearrangement ----------------
-    const int t = tid - 128;  // 0..127
+    // ---------------- scales into tensor memory ----------------
+    const int q = warp & 3;  // this warp's 32-lane quarter of tensor memory
+    const uint32_t lane_base = static_cast<uint32_t>(q * 32) << 16;
     int s = 0;
     uint32_t ph = 0;
+    uint32_t it = 0;  // stage sequence number (scale buffer = it & 1)
     bool ok = true;
     for (int u = blockIdx.x; u < total_units && ok; u += gridDim.x) {
       for (int kk = 0; kk < p.k_stages; ++kk) {
-        if (!warp_wait(&full[s], ph, abort, deadline)) {
+        const int sb = it & 1;
+        // the buffer's previous MMAs (two stages ago) are complete
+        if (!warp_wait(&full[s], ph, abort, deadline) ||
+            !warp_wait(&sffree[sb], ((it >> 1) & 1u) ^ 1u, abort, deadline)) {
           ok = false;
           break;
         }
-        uint8_t* st = smem + s * C::kStageBytes;
-        uint8_t* atoms = st + C::kOffAtoms;
-        // row t of each weight block and of the term tile: its 16 scale bytes
-        // are 4 K groups x 4 blocks; group kg goes to atom kg at r0*16 + r1*4.
-        const int r0 = t & 31, r1 = t >> 5;
+        const uint8_t* st = smem + s * C::kStageBytes;
+        const uint32_t sf0 = tmem + lane_base + C::kSfCol0 + sb * C::kSfCols;
+        // column kg*4 + r1 of lane r0: word kg (4 scales) of row r0 + 32*r1
+        uint32_t ra[16];
 #pragma unroll
         for (int a = 0; a < C::kNA; ++a) {
-          const uint4 v = *reinterpret_cast<const uint4*>(st + C::kOffSA + (a * kM + t) * kRowScales);
-          const uint32_t w[4] = {v.x, v.y, v.z, v.w};
 #pragma unroll
-          for (int kg = 0; kg < 4; ++kg)
-            *reinterpret_cast<uint32_t*>(atoms + (a * 4 + kg) * kAtom + r0 * 16 + r1 * 4) = w[kg];
+          for (int r1 = 0; r1 < 4; ++r1) {
+            const uint4 v = *reinterpret_cast<const uint4*>(
+                st + C::kOffSA + (a * kM + r1 * 32 + lane) * kRowScales);
+            ra[0 * 4 + r1] = v.x;
+            ra[1 * 4 + r1] = v.y;
+            ra[2 * 4 + r1] = v.z;
+            ra[3 * 4 + r1] = v.w;
+          }
+          tmem_st16(sf0 + a * 16, ra);
         }
-        if (t < BNR) {
-          const uint4 v = *reinterpret_cast<const uint4*>(st + C::kOffSB + t * kRowScales);
-          const uint32_t w[4] = {v.x, v.y, v.z, v.w};
+        uint32_t rb[16];
 #pragma unroll
-          for (int kg = 0; kg < 4; ++kg)
-            *reinterpret_cast<uint32_t*>(atoms + (C::kNA * 4 + kg) * kAtom + r0 * 16 + r1 * 4) = w[kg];
+        for (int r1 = 0; r1 < 4; ++r1) {
+          const int n = r1 * 32 + lane;
+          uint4 v = make_uint4(0, 0, 0, 0);
+          if (r1 < C::kBQ && n < BNR)
+            v = *reinterpret_cast<const uint4*>(st + C::kOffSB + n * kRowScales);
+          rb[0 * 4 + r1] = v.x;
+          rb[1 * 4 + r1] = v.y;
+          rb[2 * 4 + r1] = v.z;
+          rb[3 * 4 + r1] = v.w;
         }
-        // make the generic-proxy writes visible to tcgen05.cp (async proxy)
-        asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+        tmem_st16(sf0 + C::kNA * 16, rb);
+        tmem_wait_st();
+        tc_fence_before();
         __syncwarp();
         if (lane == 0) {
-          mbar_arrive(&sfready[s]);
+          mbar_arrive(&sfready[sb]);
           mbar_arrive(&empty[s]);
         }
+        ++it;
         if (++s == S) {
           s = 0;
           ph ^= 1u;
