@@ -82,6 +82,7 @@ struct BsLaunch {
   const int32_t* counts;
   const int32_t* offsets;
   const int32_t* sorted;
+  const int32_t* slot_of;  // [M*top_k] sorted slot of each route, -1 if dropped
   const uint8_t *w13, *s13, *w2, *s2;
   const float *g13, *g2;
   uint8_t* xq;   // [R*NT, K/2]
@@ -93,7 +94,7 @@ struct BsLaunch {
   float* hg;     // [R*NT]
   float* y;      // fp32 [R, K]
   uint32_t* status;
-  int64_t R;
+  int64_t M, R;
   int E, top_k, K, I;
   void (*stage_mark)(void* ctx, int stage);
   void* stage_ctx;

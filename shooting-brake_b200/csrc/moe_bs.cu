@@ -11,11 +11,14 @@
 // The activations (bf16 hidden rows, then the fp32 SwiGLU rows) are split
 // into NT NVFP4 terms by residual quantisation,
 //   x = sum_t e2m1_t * e4m3_t * g_t  (+ residual),
-// each term quantised with vLLM ref_nvfp4_quant semantics (the reference's
-// fixture quantiser) under its own per-row global g_t = amax(residual_t) /
-// (448 * 6). Each term shrinks the residual about 11x; with NT = 4 the
-// represented activations are within ~1e-4 (normwise) of the inputs, finer
-// than the bf16 rounding of the inputs themselves. The terms of a row sit in
+// each 16-element block quantised with vLLM ref_nvfp4_quant semantics (the
+// reference's fixture quantiser) under the per-row global g_t = g_0 / 4^t,
+// g_0 = amax(x) / (448 * 6). A term shrinks a block's residual at least ~6x
+// (about 11x typically), so the 4x step keeps every term's block scales in
+// e4m3 range without a new row reduction per term, and each block runs its
+// NT terms on its own. With NT = 4 the represented activations are within
+// ~1e-4 (normwise) of the inputs, finer than the bf16 rounding of the inputs
+// themselves. The terms of a row sit in
 // consecutive rows of the N operand, so one MMA covers all terms of BN/NT
 // routed tokens and the epilogue folds them: D[:, slot] = sum_t D[:, slot*NT
 // + t] * g_t.
@@ -461,6 +464,12 @@ __device__ __forceinline__ uint32_t e2m1x2_from_f32(float lo, float hi) {
   return r;
 }
 
+__device__ __forceinline__ float e4m3_to_f32_hw(uint32_t byte) {
+  uint32_t h;
+  asm("cvt.rn.f16x2.e4m3x2 %0, %1;" : "=r"(h) : "h"(static_cast<uint16_t>(byte & 0xFFu)));
+  return __low2float(*reinterpret_cast<const __half2*>(&h));
+}
+
 __device__ __forceinline__ float2 e2m1x2_to_float2(uint32_t byte) {
   uint32_t h;
   asm("{\n .reg .b8 b;\n cvt.u8.u32 b, %1;\n cvt.rn.f16x2.e2m1x2 %0, b;\n}" : "=r"(h) : "r"(byte));
@@ -468,28 +477,37 @@ __device__ __forceinline__ float2 e2m1x2_to_float2(uint32_t byte) {
 }
 
 
-// One CTA of kSplitThreads per output row: row i reads source row src(i) (the
-// token of sorted route i, or row i) and writes NT terms: packed e2m1
-// [i*NT + t, K/2], e4m3 scales [i*NT + t, K/16] and the dequant global
-// g [i*NT + t]. The residual stays in registers: thread T owns element pairs
-// (2T, 2T+1) of every 2*kSplitThreads-wide chunk, so a 16-element block is 8
-// lanes (block maxima and nibble packing are shuffles) and a packed byte is
-// one thread's pair. The row maximum of each term is one CTA reduction.
+// One CTA of kSplitThreads per source row. Without slot_of, row i is written
+// to output rows i*NT + t; with slot_of (token mode) source row i is token i
+// and its terms go to every route slot the token feeds (slot_of[i*top_k + k],
+// -1 skipped), so the token is split once however many experts it visits.
+// Outputs: packed e2m1 [row*NT + t, K/2], e4m3 scales [row*NT + t, K/16] and
+// the dequant global g [row*NT + t]. Thread T owns element pairs (2T, 2T+1)
+// of every 2*kSplitThreads-wide chunk, so a 16-element block is 8 lanes
+// (block maxima and nibble packing are shuffles) and a packed byte is one
+// thread's pair. One CTA reduction gives the row maximum; after that every
+// block runs its NT terms in registers.
 constexpr int kSplitThreads = 256;
 constexpr int kSplitMaxPairs = 16384 / (2 * kSplitThreads);  // K <= 16384
 
 template <int PAIRS>
 __global__ void __launch_bounds__(kSplitThreads) split_nvfp4_kernel(
-    const void* __restrict__ src, int src_dt, const int32_t* __restrict__ sorted, int top_k,
+    const void* __restrict__ src, int src_dt, const int32_t* __restrict__ slot_of, int top_k,
     const int32_t* __restrict__ n_rows_dev, int K, int NT, uint8_t* __restrict__ q,
     uint8_t* __restrict__ sf, float* __restrict__ gout) {
   __shared__ float s_max[kSplitThreads / 32];
+  __shared__ int32_t s_dst[kMaxTopK];
   const int64_t row = blockIdx.x;
-  if (row >= static_cast<int64_t>(*n_rows_dev)) return;
+  if (n_rows_dev && row >= static_cast<int64_t>(*n_rows_dev)) return;
   const int tid = threadIdx.x;
   const int lane = tid & 31;
   const int warp = tid >> 5;
-  const int64_t srow = sorted ? static_cast<int64_t>(sorted[row] / top_k) : row;
+  // destination rows of this source row's terms
+  int ndst = 1;
+  if (slot_of) {
+    if (tid < top_k) s_dst[tid] = slot_of[row * top_k + tid];
+    ndst = top_k;
+  }
   // pairs per thread; with K % 64 == 0 the last partial chunk ends on a warp
   // boundary, so every validity test below is warp-uniform
   const int npairs = (K + 2 * kSplitThreads - 1) / (2 * kSplitThreads);
@@ -502,61 +520,65 @@ __global__ void __launch_bounds__(kSplitThreads) split_nvfp4_kernel(
     if (i < npairs && k < K) {
       if (src_dt == kBF16) {
         const uint32_t w = *reinterpret_cast<const uint32_t*>(
-            static_cast<const uint16_t*>(src) + srow * K + k);
+            static_cast<const uint16_t*>(src) + row * K + k);
         v[i] = make_float2(__uint_as_float(w << 16), __uint_as_float(w & 0xFFFF0000u));
       } else if (src_dt == kF32) {
-        v[i] = *reinterpret_cast<const float2*>(static_cast<const float*>(src) + srow * K + k);
+        v[i] = *reinterpret_cast<const float2*>(static_cast<const float*>(src) + row * K + k);
       } else {
         v[i] = __half22float2(*reinterpret_cast<const __half2*>(
-            static_cast<const __half*>(src) + srow * K + k));
+            static_cast<const __half*>(src) + row * K + k));
       }
       amax = fmaxf(amax, fmaxf(fabsf(v[i].x), fabsf(v[i].y)));
     }
   }
-  for (int t = 0; t < NT; ++t) {
 #pragma unroll
-    for (int d = 16; d > 0; d >>= 1) amax = fmaxf(amax, __shfl_xor_sync(0xffffffffu, amax, d));
-    if (lane == 0) s_max[warp] = amax;
-    __syncthreads();
-    amax = s_max[0];
+  for (int d = 16; d > 0; d >>= 1) amax = fmaxf(amax, __shfl_xor_sync(0xffffffffu, amax, d));
+  if (lane == 0) s_max[warp] = amax;
+  __syncthreads();
+  amax = s_max[0];
 #pragma unroll
-    for (int w = 1; w < kSplitThreads / 32; ++w) amax = fmaxf(amax, s_max[w]);
-    __syncthreads();  // s_max is rewritten by the next term
-    const float G = amax > 0.0f ? __fdiv_rn(2688.0f, amax) : 1.0f;
-    const float g = __fdiv_rn(1.0f, G);
-    const int64_t orow = row * NT + t;
-    uint8_t* qrow = q + orow * (K / 2);
-    uint8_t* sfrow = sf + orow * (K / 16);
-    float next_amax = 0.0f;
+  for (int w = 1; w < kSplitThreads / 32; ++w) amax = fmaxf(amax, s_max[w]);
+  const float G0 = amax > 0.0f ? __fdiv_rn(2688.0f, amax) : 1.0f;
+  const float g0 = __fdiv_rn(1.0f, G0);
+  if (tid < ndst) {
+    const int64_t dst = slot_of ? static_cast<int64_t>(s_dst[tid]) : row;
+    if (dst >= 0)
+      for (int t = 0; t < NT; ++t) gout[dst * NT + t] = ldexpf(g0, -2 * t);
+  }
 #pragma unroll
-    for (int i = 0; i < PAIRS; ++i) {
-      const int k = i * 2 * kSplitThreads + 2 * tid;  // first element of the pair
-      if (i < npairs && k < K) {
+  for (int i = 0; i < PAIRS; ++i) {
+    const int k = i * 2 * kSplitThreads + 2 * tid;  // first element of the pair
+    if (i < npairs && k < K) {
+      float G = G0, g = g0;
+      for (int t = 0; t < NT; ++t) {
         float bmax = fmaxf(fabsf(v[i].x), fabsf(v[i].y));
         bmax = fmaxf(bmax, __shfl_xor_sync(0xffffffffu, bmax, 1));
         bmax = fmaxf(bmax, __shfl_xor_sync(0xffffffffu, bmax, 2));
         bmax = fmaxf(bmax, __shfl_xor_sync(0xffffffffu, bmax, 4));
         const float scale = fminf(__fmul_rn(G, __fmul_rn(bmax, 1.0f / 6.0f)), 448.0f);
         const __nv_fp8_storage_t s8 = __nv_cvt_float_to_fp8(scale, __NV_SATFINITE, __NV_E4M3);
-        const float sg = __fmul_rn(e4m3_to_float(s8), g);  // one e2m1 step of this block
+        const float sg = __fmul_rn(e4m3_to_f32_hw(s8), g);  // one e2m1 step of this block
         const float inv = sg == 0.0f ? 0.0f : __frcp_rn(sg);
         // nearest e2m1 (ties to even, saturating at 6) of both elements
         const uint32_t pair = e2m1x2_from_f32(__fmul_rn(v[i].x, inv), __fmul_rn(v[i].y, inv));
         const float2 dq = e2m1x2_to_float2(pair);
-        const uint32_t c0 = pair & 0xFu, c1 = pair >> 4;
         // the MMA sees e2m1 * e4m3 * g; the next term quantises what is left
         v[i].x -= __fmul_rn(dq.x, sg);
         v[i].y -= __fmul_rn(dq.y, sg);
-        next_amax = fmaxf(next_amax, fmaxf(fabsf(v[i].x), fabsf(v[i].y)));
-        uint32_t w = (c0 | (c1 << 4)) << (8 * (lane & 3));
+        uint32_t w = pair << (8 * (lane & 3));
         w |= __shfl_xor_sync(0xffffffffu, w, 1);
         w |= __shfl_xor_sync(0xffffffffu, w, 2);
-        if ((lane & 3) == 0) *reinterpret_cast<uint32_t*>(qrow + k / 2) = w;
-        if ((lane & 7) == 0) sfrow[k / 16] = static_cast<uint8_t>(s8);
+        for (int d = 0; d < ndst; ++d) {
+          const int64_t dst = slot_of ? static_cast<int64_t>(s_dst[d]) : row;
+          if (dst < 0) continue;
+          const int64_t orow = dst * NT + t;
+          if ((lane & 3) == 0) *reinterpret_cast<uint32_t*>(q + orow * (K / 2) + k / 2) = w;
+          if ((lane & 7) == 0) sf[orow * (K / 16) + k / 16] = static_cast<uint8_t>(s8);
+        }
+        G = __fmul_rn(G, 4.0f);
+        g = __fmul_rn(g, 0.25f);
       }
     }
-    if (tid == 0) gout[orow] = g;
-    amax = next_amax;
   }
 }
 
@@ -626,24 +648,23 @@ int sm_count() {
   return n;
 }
 
-cudaError_t launch_split(const void* src, int src_dt, const int32_t* sorted, int top_k,
-                         const int32_t* n_rows_dev, int64_t n_rows_max, int K, uint8_t* q,
+// slot_of != nullptr: token mode (n_rows source tokens, terms scattered to
+// their route slots); otherwise n_rows rows (device count n_rows_dev when
+// given, n_rows an upper bound).
+cudaError_t launch_split(const void* src, int src_dt, const int32_t* slot_of, int top_k,
+                         const int32_t* n_rows_dev, int64_t n_rows, int K, uint8_t* q,
                          uint8_t* sf, float* g, cudaStream_t stream) {
-  if (n_rows_max <= 0) return cudaSuccess;
+  if (n_rows <= 0) return cudaSuccess;
   const int pairs = (K + 2 * kSplitThreads - 1) / (2 * kSplitThreads);
-  const unsigned grid = static_cast<unsigned>(n_rows_max);
-  if (pairs <= 1)
-    split_nvfp4_kernel<1><<<grid, kSplitThreads, 0, stream>>>(src, src_dt, sorted, top_k,
-                                                              n_rows_dev, K, kSplitTerms, q, sf, g);
-  else if (pairs <= 4)
-    split_nvfp4_kernel<4><<<grid, kSplitThreads, 0, stream>>>(src, src_dt, sorted, top_k,
-                                                              n_rows_dev, K, kSplitTerms, q, sf, g);
-  else if (pairs <= 8)
-    split_nvfp4_kernel<8><<<grid, kSplitThreads, 0, stream>>>(src, src_dt, sorted, top_k,
-                                                              n_rows_dev, K, kSplitTerms, q, sf, g);
-  else
-    split_nvfp4_kernel<kSplitMaxPairs><<<grid, kSplitThreads, 0, stream>>>(
-        src, src_dt, sorted, top_k, n_rows_dev, K, kSplitTerms, q, sf, g);
+  const unsigned grid = static_cast<unsigned>(n_rows);
+#define SBB_SPLIT(P)                                                                         \
+  split_nvfp4_kernel<P><<<grid, kSplitThreads, 0, stream>>>(src, src_dt, slot_of, top_k,     \
+                                                            n_rows_dev, K, kSplitTerms, q, sf, g)
+  if (pairs <= 1) SBB_SPLIT(1);
+  else if (pairs <= 4) SBB_SPLIT(4);
+  else if (pairs <= 8) SBB_SPLIT(8);
+  else SBB_SPLIT(kSplitMaxPairs);
+#undef SBB_SPLIT
   return cudaGetLastError();
 }
 
@@ -653,12 +674,14 @@ bool bs_supported(int K, int I) {
   return K % kBK == 0 && I % kBK == 0 && K <= 16384 && I <= 16384 && get_encode() != nullptr;
 }
 
-// term rows per MMA tile: enough for ~1.5x the mean routes per expert
+// Term rows per MMA tile: enough for ~1.5x the mean routes per expert, up to
+// 128 (32 tokens). From N = 128 the block-scaled MMA runs at full rate; below
+// N = 64 it costs a fixed ~46 cycles per instruction.
 int bs_tile_rows(int64_t routes, int E, int mode) {
   const double per = static_cast<double>(routes) / E * 1.5;
   int tok = 4;
   (void)mode;
-  while (tok < per && tok * kSplitTerms < 64) tok *= 2;
+  while (tok < per && tok * kSplitTerms < 128) tok *= 2;
   return tok * kSplitTerms;
 }
 
@@ -667,8 +690,10 @@ cudaError_t launch_moe_bs(const BsLaunch& a, cudaStream_t stream, const char** s
   const int NT = kSplitTerms;
   const int grid = sm_count();
   *step = "activation split";
-  cudaError_t err = launch_split(a.hidden, a.act_dt, a.sorted, a.top_k, a.offsets + a.E, R, a.K,
-                                 a.xq, a.xsf, a.xg, stream);
+  cudaError_t err;
+  // split each token once; its terms go to all of its route slots
+  err = launch_split(a.hidden, a.act_dt, a.slot_of, a.top_k, nullptr, a.M, a.K, a.xq, a.xsf,
+                     a.xg, stream);
   if (err != cudaSuccess) return err;
   if (a.stage_mark) a.stage_mark(a.stage_ctx, 1);
   const uint64_t brows = static_cast<uint64_t>(R > 0 ? R : 1) * NT;

@@ -74,6 +74,7 @@ cudaError_t run_moe(const MoeArgs& a, const WorkspacePlan& plan, void* workspace
     t.counts = counts;
     t.offsets = offsets;
     t.sorted = sorted;
+    t.slot_of = slot_of;
     t.w13 = a.w13;
     t.s13 = a.s13;
     t.w2 = a.w2;
@@ -89,6 +90,7 @@ cudaError_t run_moe(const MoeArgs& a, const WorkspacePlan& plan, void* workspace
     t.hg = reinterpret_cast<float*>(ws + plan.hg);
     t.y = y;
     t.status = status;
+    t.M = a.M;
     t.R = R;
     t.E = a.E;
     t.top_k = a.top_k;
