@@ -64,6 +64,12 @@ size_t sbb200_last_error(char* buf, size_t size);
 size_t sbb200_nvfp4_moe_workspace_bytes(size_t M, size_t E, size_t top_k, size_t K, size_t I,
                                         int act_dt);
 
+/* Number of kernels one sbb200_nvfp4_moe call of this shape launches on
+ * its stream (the status clear, a memset, is not counted). No counterpart in
+ * the reference; it lets a benchmark or a graph builder account for launches. */
+int sbb200_nvfp4_moe_launches(size_t M, size_t E, size_t top_k, size_t K, size_t I,
+                              int act_dt);
+
 /* out[M, K] = sum_k w[m, k] * FFN_{ids[m, k]}(hidden[m]) with
  * FFN(x) = W2 (silu(W_gate x) * (W_up x)). hidden [M, K] in act_dt (f32, f16
  * or bf16); topk_ids int32 [M, top_k], ids outside [0, E) are skipped (their
@@ -85,9 +91,9 @@ int sbb200_nvfp4_moe(void* stream, const void* hidden, const int32_t* topk_ids,
  * reference's nvfp4_moe_grouped_profiled_sycl + Nvfp4MoeGroupedStages,
  * src/QuixiCore-XPU/kernels/moe/nvfp4_moe/nvfp4_moe_kernel.hpp:53-83): the same
  * launches in the same order, with cudaEvent_t stage_events[i] recorded on
- * `stream` at the stage boundaries: [0] start, [1] after the route plan,
- * [2] after gate/up + SwiGLU, [3] after the down projection, [4] after the
- * combine. n_stage_events must be SBB200_STAGE_EVENTS; NULL entries are
+ * `stream` at the stage boundaries: [0] start, [1] after the route plan
+ * (and the activation split), [2] after the gate/up + SwiGLU GEMM, [3] after
+ * the down projection (and the split of its input), [4] after the combine. n_stage_events must be SBB200_STAGE_EVENTS; NULL entries are
  * skipped. */
 #define SBB200_STAGE_EVENTS 5
 int sbb200_nvfp4_moe_staged(void* stream, const void* hidden, const int32_t* topk_ids,

@@ -64,6 +64,8 @@ def lib() -> ctypes.CDLL:
         L.sbb200_last_error.argtypes = [ctypes.c_char_p, S]
         L.sbb200_nvfp4_moe_workspace_bytes.restype = S
         L.sbb200_nvfp4_moe_workspace_bytes.argtypes = [S, S, S, S, S, I]
+        L.sbb200_nvfp4_moe_launches.restype = I
+        L.sbb200_nvfp4_moe_launches.argtypes = [S, S, S, S, S, I]
         L.sbb200_nvfp4_moe.restype = I
         L.sbb200_nvfp4_moe.argtypes = [P, P, P, P, P, P, P, P, P, P, P, S, P, I, S, S, S, S, S, I, I]
         L.sbb200_nvfp4_moe_staged.restype = I
@@ -224,14 +226,16 @@ def _nvfp4_moe_impl(hidden: torch.Tensor, topk_ids: torch.Tensor, topk_weights: 
     return out
 
 
-def kernels_per_call(routes: int) -> int:
-    """Kernels of this library one nvfp4_moe call launches: the route plan (a
-    histogram pass only above 4096 routes), gate/up, down, combine."""
-    return (2 if routes > 4096 else 1) + 3
+def kernels_per_call(M: int, E: int, top_k: int, K: int, I: int,
+                     act_dtype: torch.dtype = torch.bfloat16) -> int:
+    """Kernels of this library one nvfp4_moe call of this shape launches (the
+    driver's own count: route plan, activation split, gate/up, SwiGLU split,
+    down, combine on the block-scaled path)."""
+    return int(lib().sbb200_nvfp4_moe_launches(M, E, top_k, K, I, DTYPE_CODE[act_dtype]))
 
 
 STAGE_EVENTS = 5
-STAGE_NAMES = ("route_plan", "gate_up", "down", "combine")
+STAGE_NAMES = ("route_plan+x_split", "gate_up", "h_split+down", "combine")
 
 
 def stage_events(stream: torch.cuda.Stream | None = None) -> list:

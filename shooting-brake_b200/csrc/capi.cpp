@@ -91,6 +91,14 @@ size_t sbb200_nvfp4_moe_workspace_bytes(size_t M, size_t E, size_t top_k, size_t
   return sbb::plan_workspace(M, E, top_k, K, I).total;
 }
 
+int sbb200_nvfp4_moe_launches(size_t M, size_t E, size_t top_k, size_t K, size_t I,
+                              int act_dt) {
+  (void)E;
+  (void)act_dt;
+  return sbb::count_launches(static_cast<int64_t>(M), static_cast<int>(top_k),
+                             static_cast<int>(K), static_cast<int>(I));
+}
+
 int sbb200_nvfp4_moe(void* stream, const void* hidden, const int32_t* topk_ids,
                      const float* topk_weights, const void* w13, const void* w13_scales,
                      const float* w13_global_scales, const void* w2, const void* w2_scales,

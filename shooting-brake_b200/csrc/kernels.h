@@ -51,27 +51,6 @@ cudaError_t launch_quantize(const void* x, int in_dt, const float* gq, int64_t r
                             uint8_t* q, uint8_t* sf, int64_t rows, int64_t cols,
                             cudaStream_t stream);
 
-// tcgen05 grouped GEMM path (moe_tc.cu): gather + f16 scaling of the sorted
-// activation rows, gate/up + SwiGLU into h, down projection into y.
-struct TcLaunch {
-  const void* hidden;
-  int act_dt;
-  const int32_t* counts;
-  const int32_t* offsets;
-  const int32_t* sorted;
-  const uint8_t *w13, *s13, *w2, *s2;
-  const float *g13, *g2;
-  void* xperm;      // f16 [R, K]
-  float* xscale;    // fp32 [R]
-  void* h;          // bf16 [R, I]
-  float* y;         // fp32 [R, K]
-  uint32_t* status;
-  int64_t R;
-  int E, top_k, K, I;
-  void (*stage_mark)(void* ctx, int stage);  // optional
-  void* stage_ctx;
-};
-
 // Block-scaled path (moe_bs.cu): activations split into kSplitTerms NVFP4
 // terms, tcgen05.mma kind::mxf4nvf4 on the packed weights.
 constexpr int kSplitTerms = 4;
@@ -103,9 +82,5 @@ struct BsLaunch {
 bool bs_supported(int K, int I);
 int bs_tile_rows(int64_t routes, int E, int mode);
 cudaError_t launch_moe_bs(const BsLaunch& a, cudaStream_t stream, const char** step);
-
-bool tc_supported(int K, int I, int act_dt);
-int tc_token_tile(int64_t routes, int E, int mode);
-cudaError_t launch_moe_tc(const TcLaunch& a, cudaStream_t stream, const char** step);
 
 }  // namespace sbb

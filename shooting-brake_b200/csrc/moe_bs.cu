@@ -23,7 +23,10 @@
 // routed tokens and the epilogue folds them: D[:, slot] = sum_t D[:, slot*NT
 // + t] * g_t.
 //
-// Work unit, persistent grid and warp specialisation as in moe_tc.cu:
+// A work unit is (expert, weight-row tile, token tile): 128 gate rows plus
+// the matching 128 up rows (gate/up), or 256 consecutive w2 rows (down),
+// against BN term rows of that expert's routed tokens. A persistent grid of
+// one CTA per SM walks the units; within a CTA the warps specialise:
 //   warp 0       TMA: packed weights (128-byte swizzle), their linear scale
 //                rows, the packed term rows and their scale rows.
 //   warp 1       TMEM allocation; one thread issues the MMAs.
@@ -689,76 +692,68 @@ cudaError_t launch_moe_bs(const BsLaunch& a, cudaStream_t stream, const char** s
   const int64_t R = a.R;
   const int NT = kSplitTerms;
   const int grid = sm_count();
+  const uint64_t brows = static_cast<uint64_t>(R > 0 ? R : 1) * NT;
+  // All tensor maps are encoded before the first launch, so the host never
+  // holds the stream up between kernels.
+  *step = "tensor maps";
+  const int bnr1 = bs_tile_rows(R, a.E, kGateUp);
+  const int bnr2 = bs_tile_rows(R, a.E, kDown);
+  CUtensorMap m1a, m1sa, m1b, m1sb, m2a, m2sa, m2b, m2sb;
+  if (!encode_u8(&m1a, a.w13, a.K / 2, (uint64_t)a.E * 2 * a.I, kRowBytes, kM,
+                 CU_TENSOR_MAP_SWIZZLE_128B) ||
+      !encode_u8(&m1sa, a.s13, a.K / 16, (uint64_t)a.E * 2 * a.I, kRowScales, kM,
+                 CU_TENSOR_MAP_SWIZZLE_NONE) ||
+      !encode_u8(&m1b, a.xq, a.K / 2, brows, kRowBytes, bnr1, CU_TENSOR_MAP_SWIZZLE_128B) ||
+      !encode_u8(&m1sb, a.xsf, a.K / 16, brows, kRowScales, bnr1, CU_TENSOR_MAP_SWIZZLE_NONE) ||
+      !encode_u8(&m2a, a.w2, a.I / 2, (uint64_t)a.E * a.K, kRowBytes, kM,
+                 CU_TENSOR_MAP_SWIZZLE_128B) ||
+      !encode_u8(&m2sa, a.s2, a.I / 16, (uint64_t)a.E * a.K, kRowScales, kM,
+                 CU_TENSOR_MAP_SWIZZLE_NONE) ||
+      !encode_u8(&m2b, a.hq, a.I / 2, brows, kRowBytes, bnr2, CU_TENSOR_MAP_SWIZZLE_128B) ||
+      !encode_u8(&m2sb, a.hsf, a.I / 16, brows, kRowScales, bnr2, CU_TENSOR_MAP_SWIZZLE_NONE))
+    return cudaErrorInvalidValue;
+  BsParams p1{};
+  p1.counts = a.counts;
+  p1.offsets = a.offsets;
+  p1.gscale = a.g13;
+  p1.bg = a.xg;
+  p1.out = a.h;
+  p1.status = a.status;
+  p1.E = a.E;
+  p1.I = a.I;
+  p1.m_tiles = a.I / kM;
+  p1.a_stride = a.I;
+  p1.k_stages = a.K / kBK;
+  p1.rows_per_expert = 2 * a.I;
+  p1.out_ld = a.I;
+  BsParams p2 = p1;
+  p2.gscale = a.g2;
+  p2.bg = a.hg;
+  p2.out = a.y;
+  p2.m_tiles = a.K / (2 * kM);
+  p2.a_stride = kM;
+  p2.k_stages = a.I / kBK;
+  p2.rows_per_expert = a.K;
+  p2.out_ld = a.K;
+
+  // 1. split each token once; its terms go to all of its route slots
   *step = "activation split";
-  cudaError_t err;
-  // split each token once; its terms go to all of its route slots
-  err = launch_split(a.hidden, a.act_dt, a.slot_of, a.top_k, nullptr, a.M, a.K, a.xq, a.xsf,
-                     a.xg, stream);
+  cudaError_t err = launch_split(a.hidden, a.act_dt, a.slot_of, a.top_k, nullptr, a.M, a.K,
+                                 a.xq, a.xsf, a.xg, stream);
   if (err != cudaSuccess) return err;
   if (a.stage_mark) a.stage_mark(a.stage_ctx, 1);
-  const uint64_t brows = static_cast<uint64_t>(R > 0 ? R : 1) * NT;
-  {
-    *step = "gate/up tensor maps";
-    CUtensorMap ta, tsa, tb, tsb;
-    const int bnr = bs_tile_rows(R, a.E, kGateUp);
-    if (!encode_u8(&ta, a.w13, a.K / 2, (uint64_t)a.E * 2 * a.I, kRowBytes, kM,
-                   CU_TENSOR_MAP_SWIZZLE_128B) ||
-        !encode_u8(&tsa, a.s13, a.K / 16, (uint64_t)a.E * 2 * a.I, kRowScales, kM,
-                   CU_TENSOR_MAP_SWIZZLE_NONE) ||
-        !encode_u8(&tb, a.xq, a.K / 2, brows, kRowBytes, bnr, CU_TENSOR_MAP_SWIZZLE_128B) ||
-        !encode_u8(&tsb, a.xsf, a.K / 16, brows, kRowScales, bnr, CU_TENSOR_MAP_SWIZZLE_NONE))
-      return cudaErrorInvalidValue;
-    BsParams p{};
-    p.counts = a.counts;
-    p.offsets = a.offsets;
-    p.gscale = a.g13;
-    p.bg = a.xg;
-    p.out = a.h;
-    p.status = a.status;
-    p.E = a.E;
-    p.I = a.I;
-    p.m_tiles = a.I / kM;
-    p.a_stride = a.I;
-    p.k_stages = a.K / kBK;
-    p.rows_per_expert = 2 * a.I;
-    p.out_ld = a.I;
-    *step = "gate/up";
-    err = launch_bnr<kGateUp>(bnr, ta, tsa, tb, tsb, p, grid, stream);
-    if (err != cudaSuccess) return err;
-  }
+  // 2. gate/up + SwiGLU
+  *step = "gate/up";
+  err = launch_bnr<kGateUp>(bnr1, m1a, m1sa, m1b, m1sb, p1, grid, stream);
+  if (err != cudaSuccess) return err;
+  if (a.stage_mark) a.stage_mark(a.stage_ctx, 2);
+  // 3. split the SwiGLU rows, down projection
   *step = "h split";
   err = launch_split(a.h, kF32, nullptr, 1, a.offsets + a.E, R, a.I, a.hq, a.hsf, a.hg, stream);
   if (err != cudaSuccess) return err;
-  if (a.stage_mark) a.stage_mark(a.stage_ctx, 2);
-  {
-    *step = "down tensor maps";
-    CUtensorMap ta, tsa, tb, tsb;
-    const int bnr = bs_tile_rows(R, a.E, kDown);
-    if (!encode_u8(&ta, a.w2, a.I / 2, (uint64_t)a.E * a.K, kRowBytes, kM,
-                   CU_TENSOR_MAP_SWIZZLE_128B) ||
-        !encode_u8(&tsa, a.s2, a.I / 16, (uint64_t)a.E * a.K, kRowScales, kM,
-                   CU_TENSOR_MAP_SWIZZLE_NONE) ||
-        !encode_u8(&tb, a.hq, a.I / 2, brows, kRowBytes, bnr, CU_TENSOR_MAP_SWIZZLE_128B) ||
-        !encode_u8(&tsb, a.hsf, a.I / 16, brows, kRowScales, bnr, CU_TENSOR_MAP_SWIZZLE_NONE))
-      return cudaErrorInvalidValue;
-    BsParams p{};
-    p.counts = a.counts;
-    p.offsets = a.offsets;
-    p.gscale = a.g2;
-    p.bg = a.hg;
-    p.out = a.y;
-    p.status = a.status;
-    p.E = a.E;
-    p.I = a.I;
-    p.m_tiles = a.K / (2 * kM);
-    p.a_stride = kM;
-    p.k_stages = a.I / kBK;
-    p.rows_per_expert = a.K;
-    p.out_ld = a.K;
-    *step = "down";
-    err = launch_bnr<kDown>(bnr, ta, tsa, tb, tsb, p, grid, stream);
-    if (err != cudaSuccess) return err;
-  }
+  *step = "down";
+  err = launch_bnr<kDown>(bnr2, m2a, m2sa, m2b, m2sb, p2, grid, stream);
+  if (err != cudaSuccess) return err;
   if (a.stage_mark) a.stage_mark(a.stage_ctx, 3);
   return cudaSuccess;
 }

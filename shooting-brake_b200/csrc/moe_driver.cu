@@ -28,8 +28,6 @@ WorkspacePlan plan_workspace(size_t M, size_t E, size_t top_k, size_t K, size_t 
   p.offsets = take((E + 1) * sizeof(int32_t));
   p.sorted = take(R * sizeof(int32_t));
   p.slot_of = take(R * sizeof(int32_t));
-  p.xperm = take(R * K * 2);
-  p.xscale = take(R * sizeof(float));
   p.h = take(R * I * sizeof(float));
   const size_t RT = R * kSplitTerms;
   p.xq = take(RT * K / 2);
@@ -41,6 +39,15 @@ WorkspacePlan plan_workspace(size_t M, size_t E, size_t top_k, size_t K, size_t 
   p.y = take(R * K * sizeof(float));
   p.total = at;
   return p;
+}
+
+int count_launches(int64_t M, int top_k, int K, int I) {
+  const int64_t R = M * top_k;
+  const int plan = route_plan_chunks(R) > 1 ? 2 : 1;
+  // block-scaled path: activation split, gate/up, SwiGLU split, down;
+  // CUDA-core path: gate/up, down. Both end with the combine.
+  const int body = bs_supported(K, I) ? 4 : 2;
+  return plan + body + 1;
 }
 
 cudaError_t run_moe(const MoeArgs& a, const WorkspacePlan& plan, void* workspace,
@@ -109,43 +116,6 @@ cudaError_t run_moe(const MoeArgs& a, const WorkspacePlan& plan, void* workspace
     }
     const char* step = "block-scaled path";
     err = launch_moe_bs(t, stream, &step);
-    if (err != cudaSuccess) { *why = step; return err; }
-  } else if (tc_supported(a.K, a.I, a.act_dt)) {
-    TcLaunch t{};
-    t.hidden = a.hidden;
-    t.act_dt = a.act_dt;
-    t.counts = counts;
-    t.offsets = offsets;
-    t.sorted = sorted;
-    t.w13 = a.w13;
-    t.s13 = a.s13;
-    t.w2 = a.w2;
-    t.s2 = a.s2;
-    t.g13 = a.g13;
-    t.g2 = a.g2;
-    t.xperm = ws + plan.xperm;
-    t.xscale = reinterpret_cast<float*>(ws + plan.xscale);
-    t.h = h;
-    t.y = y;
-    t.status = status;
-    t.R = R;
-    t.E = a.E;
-    t.top_k = a.top_k;
-    t.K = a.K;
-    t.I = a.I;
-    struct Ctx {
-      void* const* ev;
-      cudaStream_t s;
-    } ctx{a.stage_events, stream};
-    if (a.stage_events) {
-      t.stage_mark = [](void* c, int i) {
-        auto* x = static_cast<Ctx*>(c);
-        if (x->ev[i]) cudaEventRecord(static_cast<cudaEvent_t>(x->ev[i]), x->s);
-      };
-      t.stage_ctx = &ctx;
-    }
-    const char* step = "tcgen05 path";
-    err = launch_moe_tc(t, stream, &step);
     if (err != cudaSuccess) { *why = step; return err; }
   } else {
     if ((err = mark(1)) != cudaSuccess) { *why = "stage event"; return err; }

@@ -21,8 +21,6 @@ struct WorkspacePlan {
   size_t offsets;       // int32[E + 1]
   size_t sorted;        // int32[R]   route id per sorted slot
   size_t slot_of;       // int32[R]   sorted slot per route, -1 if dropped
-  size_t xperm;         // f16[R, K]  scaled activation rows per slot (tcgen05 path)
-  size_t xscale;        // fp32[R]    their power-of-two scales
   size_t h;             // fp32[R, I] SwiGLU activations per slot
   size_t xq, xsf, xg;   // activation split terms: [R*NT, K/2], [R*NT, K/16], fp32 [R*NT]
   size_t hq, hsf, hg;   // SwiGLU split terms:     [R*NT, I/2], [R*NT, I/16], fp32 [R*NT]
@@ -50,6 +48,9 @@ struct MoeArgs {
 
 int validate_shape(size_t M, size_t E, size_t top_k, size_t K, size_t I, int act_dt, int out_dt,
                    std::string* why);
+
+// Kernels (excluding the status memset) one run_moe call enqueues.
+int count_launches(int64_t M, int top_k, int K, int I);
 
 // Enqueue the whole forward on `stream`. On failure returns the CUDA error and
 // names the failing step in *why.
