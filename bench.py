@@ -8,7 +8,10 @@ renormalised weights. Synthetic seeded data; the weights are random-init.
 
 A "step" is one routed-expert layer forward over one batch of T tokens. Four
 independent layers (4 x 1.5 GB) rotate across steps so consecutive steps
-never find their weights in the 126 MB L2.
+never find their weights in the 126 MB L2. The device-resident number replays
+one captured CUDA graph per (layer, batch), as a serving engine replays its
+decode step; the eager time of the same calls is reported beside it, and the
+end-to-end number goes through the public op with host buffers.
 
     python bench.py [--gpus N] [--steps K] [--warmup W] [--tokens T]
     python bench.py --impl reference ...   # the reference's CPU expert tier
@@ -31,7 +34,6 @@ ROOT = Path(__file__).resolve().parent
 sys.path.insert(0, str(ROOT))
 
 E, D, I, TOP_K = 170, 4096, 1280, 8
-N_LAYERS = 4
 EXPERT_BYTES = 2 * I * D // 2 + 2 * I * D // 16 + D * I // 2 + D * I // 16 + 8
 METRIC = "routed-expert tokens/s"
 
@@ -39,12 +41,16 @@ METRIC = "routed-expert tokens/s"
 def parse():
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
-    ap.add_argument("--steps", type=int, default=50)
+    ap.add_argument("--steps", type=int, default=400)
     ap.add_argument("--warmup", type=int, default=5)
     ap.add_argument("--tokens", type=int, default=64)
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--cpu-seconds", type=float, default=12.0)
+    ap.add_argument("--eager", action="store_true",
+                    help="time eager calls instead of CUDA-graph replay")
+    ap.add_argument("--layers", type=int, default=4,
+                    help="independent layers rotated across steps (>= 2 keeps weights out of L2)")
     return ap.parse_args()
 
 
@@ -91,11 +97,14 @@ _E2M1_THRESH = None
 
 def quantize_plane_torch(w, G):
     """NVFP4 quantisation of a [rows, cols] plane with plain torch ops (vLLM
-    ref_nvfp4_quant semantics): data generation shared by both bench arms, so
-    they see identical bytes; the library's own quantiser is not used here."""
+    ref_nvfp4_quant semantics); G is a scalar or a [rows, 1] column of
+    per-row quantisation globals. Data generation shared by both bench arms,
+    so they see identical bytes; the library's own quantiser is not used."""
     import torch
     rows, cols = w.shape
     x = w.float().reshape(rows, cols // 16, 16)
+    if isinstance(G, torch.Tensor) and G.dim() == 2:
+        G = G[:, :, None]
     vmax = x.abs().amax(dim=-1, keepdim=True)
     scale = (G * (vmax * (1.0 / 6.0))).clamp(-448.0, 448.0)
     sf = scale.to(torch.float8_e4m3fn)
@@ -132,15 +141,20 @@ def make_layers(device, n_layers, seed=0):
         s2 = torch.empty((E, D, I // 16), dtype=torch.uint8, device=device)
         g13 = torch.empty(E, dtype=torch.float32, device=device)
         g2 = torch.empty(E, dtype=torch.float32, device=device)
-        for e in range(E):
+        chunk = 16  # experts generated and quantised per batch of torch ops
+        for e0 in range(0, E, chunk):
+            e1 = min(E, e0 + chunk)
             for (q, sf, g, shape) in ((w13, s13, g13, (2 * I, D)), (w2, s2, g2, (D, I))):
-                w = (torch.randn(shape, generator=gen, device=device) * 0.02).to(torch.bfloat16)
-                amax = w.float().abs().max()
+                w = (torch.randn((e1 - e0,) + shape, generator=gen, device=device) * 0.02).to(
+                    torch.bfloat16)
+                amax = w.float().abs().amax(dim=(1, 2))
                 G = torch.tensor(2688.0, device=device) / amax
-                g[e] = amax / 2688.0
-                qe, se = quantize_plane_torch(w, G)
-                q[e].copy_(qe)
-                sf[e].copy_(se)
+                g[e0:e1] = amax / 2688.0
+                qe, se = quantize_plane_torch(w.reshape(-1, shape[1]),
+                                              G.repeat_interleave(shape[0])[:, None])
+                q[e0:e1].copy_(qe.reshape(e1 - e0, shape[0], -1))
+                sf[e0:e1].copy_(se.reshape(e1 - e0, shape[0], -1))
+                del w
         layers.append((w13, s13, g13, w2, s2, g2))
     return layers
 
@@ -190,11 +204,21 @@ class ClockSampler:
         try:
             self.proc = subprocess.Popen(
                 ["nvidia-smi", "-i", str(self.gpu), f"--query-gpu={self.FIELDS}",
-                 "--format=csv,noheader,nounits", "-lms", "100"],
+                 "--format=csv,noheader,nounits", "-lms", "50"],
                 stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True)
         except (FileNotFoundError, OSError):
             self.proc = None
         return self
+
+    def wait_first_sample(self, timeout=3.0):
+        """Block until nvidia-smi has printed its first line, so the samples
+        that follow cover the timed region."""
+        if self.proc is None or self.proc.stdout is None:
+            return
+        import select
+        r, _, _ = select.select([self.proc.stdout], [], [], timeout)
+        if r:
+            self.proc.stdout.readline()
 
     def __exit__(self, *exc):
         self.lines = []
@@ -232,27 +256,40 @@ class ClockSampler:
 # CPU baselines (reference CPU expert tier, compiled from its source)
 # --------------------------------------------------------------------------
 
-def cpu_reference_run(layer_host, hidden_bits, ids, w, seconds):
+def cpu_reference_run(layer_host, hidden_bits, ids, w, seconds, max_calls=500, warmup=1):
     """Time the reference's CPU expert tier (sb_cpu_moe_forward, compiled from
     its source) on one 170-expert layer of the headline workload with all host
-    threads. Returns (tokens/s, sample description, threads, seconds/call)."""
+    threads: `warmup` untimed calls, then whole-batch calls until `seconds`
+    have passed or `max_calls` were timed (at least 3). Returns (tokens/s,
+    sample description, threads, seconds/call, calls timed)."""
     from oracle import nvfp4 as O
     threads = os.cpu_count() or 1
     T = hidden_bits.shape[0]
     tier = O.ReferenceCpuTier(layer_host, threads=threads)
-    tier.forward(hidden_bits, ids, w)  # warm-up: first touch of the arena
+    for _ in range(max(1, warmup)):  # the first call also touches the arena
+        tier.forward(hidden_bits, ids, w)
     times = []
     t_end = time.perf_counter() + seconds
-    while time.perf_counter() < t_end or len(times) < 3:
+    while (time.perf_counter() < t_end or len(times) < 3) and len(times) < max(3, max_calls):
         t0 = time.perf_counter()
         tier.forward(hidden_bits, ids, w)
         times.append(time.perf_counter() - t0)
-        if len(times) >= 500:
-            break
     tier.close()
-    per_call = statistics.median(times)
-    return T / per_call, (f"median of {len(times)} sb_cpu_moe_forward calls on one 170-expert "
-                          f"layer, T={T}"), threads, per_call
+    per_call = sum(times) / len(times)
+    return T / per_call, (f"mean of {len(times)} timed sb_cpu_moe_forward calls (whole T={T} "
+                          f"batch each) on one 170-expert layer"), threads, per_call, len(times)
+
+
+def profiled_traffic(T):
+    """dram__bytes_read.sum + dram__bytes_write.sum of one gate/up launch,
+    from the committed ncu summary of this workload, or None."""
+    import re
+    f = ROOT / "profiles" / f"moe_gemm_bs_gateup_decode_T{T}.md"
+    try:
+        m = re.search(r"traffic_bytes_per_launch:\s*([0-9]+)", f.read_text())
+    except OSError:
+        return None
+    return int(m.group(1)) if m else None
 
 
 def host_batch(batch):
@@ -287,10 +324,13 @@ def run_reference_arm(args):
     # the same seeded layer 0 and batch 0 as the B200 arm
     layer_host = layer_to_host(make_layers(device, 1, seed=1000)[0])
     hb, ids, w = host_batch(make_batch(device, T, seed=2000))
-    tps, sample, threads, per_call = cpu_reference_run(layer_host, hb, ids, w, args.cpu_seconds)
+    # K timed whole-batch calls after W warm-up calls, bounded to a few
+    # minutes of host time (the step count actually timed is reported).
+    tps, sample, threads, per_call, n = cpu_reference_run(
+        layer_host, hb, ids, w, seconds=150.0, max_calls=args.steps, warmup=args.warmup)
     line = {
         "impl": "reference", "metric": METRIC, "value": tps, "unit": "tokens/s",
-        "n_gpus": args.gpus, "steps": args.steps, "warmup": args.warmup,
+        "n_gpus": args.gpus, "steps": n, "steps_requested": args.steps, "warmup": args.warmup,
         "ms_per_step": per_call * 1e3, "higher_is_better": True, "scaling": "weak",
         "vs_baseline": None, "dtype": "f32", "data": "synthetic",
         "config": {"workload": f"config1-decode E={E} d={D} I={I} top{TOP_K} T={T}",
@@ -318,6 +358,7 @@ def main():
     sbb = g.load_package()
     T = args.tokens
 
+    N_LAYERS = args.layers
     layers = make_layers(device, N_LAYERS, seed=1000 + rank)
     batches = [make_batch(device, T, seed=2000 + 17 * i + rank) for i in range(N_LAYERS)]
     out = torch.empty((T, D), dtype=torch.bfloat16, device=device)
@@ -328,22 +369,52 @@ def main():
         h, ids, w = batches[i % N_LAYERS]
         sbb._nvfp4_moe_impl(h, ids, w, *lw, True, torch.bfloat16, out=out)
 
-    # ---- device-resident timing ------------------------------------------
-    for i in range(max(args.warmup, 3)):
-        step(i)
-    torch.cuda.synchronize()
-    barrier(world)
-    torch.cuda.synchronize()
-    ev0 = torch.cuda.Event(enable_timing=True)
-    ev1 = torch.cuda.Event(enable_timing=True)
-    with ClockSampler(local) as clk:
+    def timed(run_one, use_clocks):
+        """Per-step ms of args.steps calls, bracketed by barrier + synchronize,
+        max over ranks; optionally with nvidia-smi clocks sampled throughout."""
+        torch.cuda.synchronize()
+        barrier(world)
+        torch.cuda.synchronize()
+        ev0 = torch.cuda.Event(enable_timing=True)
+        ev1 = torch.cuda.Event(enable_timing=True)
+        clk = ClockSampler(local) if use_clocks else None
+        if clk is not None:
+            clk.__enter__()
+            clk.wait_first_sample()
         ev0.record(stream)
         for i in range(args.steps):
-            step(i)
+            run_one(i)
         ev1.record(stream)
         torch.cuda.synchronize()
-    barrier(world)
-    ms = max_over_ranks(ev0.elapsed_time(ev1), world) / args.steps
+        if clk is not None:
+            clk.__exit__(None, None, None)
+        barrier(world)
+        return max_over_ranks(ev0.elapsed_time(ev1), world) / args.steps, clk
+
+    # ---- device-resident timing: one CUDA graph per (layer, batch) holding
+    # the same kernel launches an eager call makes -------------------------
+    for i in range(max(args.warmup, 3)):
+        step(i)
+    graphs = []
+    if not args.eager:
+        cap = torch.cuda.Stream(device)
+        cap.wait_stream(stream)
+        with torch.cuda.stream(cap):
+            for i in range(N_LAYERS):
+                step(i)  # the capture stream's workspace exists before capture
+        torch.cuda.synchronize()
+        for i in range(N_LAYERS):
+            gr = torch.cuda.CUDAGraph()
+            with torch.cuda.graph(gr, stream=cap):
+                step(i)
+            graphs.append(gr)
+        for i in range(max(args.warmup, 3)):
+            graphs[i % N_LAYERS].replay()
+        ms, clk = timed(lambda i: graphs[i % N_LAYERS].replay(), True)
+        eager_ms, _ = timed(step, False)
+    else:
+        ms, clk = timed(step, True)
+        eager_ms = ms
     clocks = clk.summary()
 
     # ---- per-stage timing for the roofline: the same calls with the C-ABI's
@@ -408,10 +479,17 @@ def main():
     distinct_bytes_w13 = avg_distinct * (2 * I * D // 2 + 2 * I * D // 16 + 4) + T * D * 2
     distinct_bytes_w2 = avg_distinct * (D * I // 2 + D * I // 16 + 4)
     gu_gbs = distinct_bytes_w13 / (stage_ms["gate_up"] * 1e-3) / 1e9
-    dn_gbs = distinct_bytes_w2 / (stage_ms["down"] * 1e-3) / 1e9
+    dn_gbs = distinct_bytes_w2 / (stage_ms["h_split+down"] * 1e-3) / 1e9
+    # DRAM traffic of one gate/up launch on batch 0 from the committed ncu
+    # summary (same seeds, T and layer shape), beside that launch's own
+    # algorithmic bytes.
+    traffic, traffic_alg = profiled_traffic(T), None
+    if traffic is not None:
+        traffic_alg = byts[0][1] * (2 * I * D // 2 + 2 * I * D // 16 + 4) + T * D * 2
     roofline = {"bound": "hbm", "achieved": gu_gbs, "peak": hbm_peak, "unit": "GB/s",
-                "frac": gu_gbs / hbm_peak, "traffic": None,
-                "kernel": "gate/up + SwiGLU (w13 weight stream)",
+                "frac": gu_gbs / hbm_peak, "traffic": traffic,
+                "traffic_launch_algorithmic_bytes": traffic_alg,
+                "kernel": "moe_gemm_bs_kernel<gate/up> (w13 weight stream + SwiGLU)",
                 "algorithmic_bytes_per_launch": distinct_bytes_w13,
                 "launch_ms": stage_ms["gate_up"], "peak_source": f"{peak_src} hbm_gbs",
                 "stages_ms": stage_ms, "down_gbs": dn_gbs,
@@ -425,26 +503,29 @@ def main():
                 O.build(ref=True)
             if O.reference_available():
                 hb, hids, hw = host_batch(batches[0])
-                tps, sample, threads, _ = cpu_reference_run(layer_to_host(layers[0]), hb, hids,
-                                                            hw, args.cpu_seconds)
+                tps, sample, threads, _, _ = cpu_reference_run(
+                    layer_to_host(layers[0]), hb, hids, hw, args.cpu_seconds)
                 cpu_baseline = {"value": tps, "unit": "tokens/s", "cores": threads,
                                 "kind": "reference", "sample": sample}
         except Exception as exc:  # the baseline is reported, never required
             cpu_baseline = {"error": str(exc)[:200]}
 
-    launches_per_step = sbb.kernels_per_call(T * TOP_K)
+    launches_per_step = sbb.kernels_per_call(T, E, TOP_K, D, I)
     if rank == 0:
         line = {
             "metric": METRIC, "value": world * T / (ms * 1e-3), "unit": "tokens/s",
             "n_gpus": world, "steps": args.steps, "warmup": args.warmup, "ms_per_step": ms,
-            "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "f16/bf16 MMA operands, fp32 accumulate (NVFP4 W4A16)",
+            "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "nvfp4 W4A16: e2m1 weights x 4-term e2m1 activation split, mxf4nvf4 MMA, fp32 accumulate",
             "data": "synthetic",
             "config": {"workload": f"config1-decode E={E} d={D} I={I} top{TOP_K} T={T}",
                        "global_batch": world * T, "tokens_per_gpu": T,
                        "parallelism": f"replicas x{world}" if world > 1 else "single",
-                       "l2": f"{N_LAYERS} rotating layers of {E * EXPERT_BYTES / 1e9:.2f} GB",
+                       "l2": f"inputs larger than L2: {N_LAYERS} rotating layers of "
+                             f"{E * EXPERT_BYTES / 1e9:.2f} GB",
                        "distinct_experts_avg": avg_distinct,
                        "algorithmic_bytes_per_step": avg_bytes},
+            "timing": "CUDA graph replay" if graphs else "eager calls",
+            "eager_ms_per_step": eager_ms,
             "weight_stream_gbs": achieved_step,
             "roofline": roofline,
             "cpu_baseline": cpu_baseline,
