@@ -41,7 +41,7 @@ METRIC = "routed-expert tokens/s"
 def parse():
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
-    ap.add_argument("--steps", type=int, default=400)
+    ap.add_argument("--steps", type=int, default=2000)
     ap.add_argument("--warmup", type=int, default=5)
     ap.add_argument("--tokens", type=int, default=64)
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])

@@ -1,0 +1,149 @@
+"""vLLM routed-experts hook adapter for the B200 path.
+
+The reference reaches its expert kernels from vLLM through
+``HybridRoutedExperts(RoutedExperts).forward_modular(x, topk_weights,
+topk_ids, shared_experts=None, shared_experts_input=None)``
+(``src/phase4/src/shooting_brake_vllm/routed_experts.py:2312-2397``),
+registered out of tree as ``RoutedExperts`` through the
+``vllm.general_plugins`` entry point (``src/phase4/src/shooting_brake_vllm/
+__init__.py:318-344``, ``pyproject.toml:45-46``).
+
+:class:`RoutedExpertsB200` keeps that call shape. Its forward is the custom op
+``torch.ops.sbb200.nvfp4_moe`` on device-resident weights, stream-ordered
+with no host synchronisation, so a vLLM decode step that holds it can be
+captured and replayed as a CUDA graph. Weights are taken in the bank layout
+(w13 rows ``[gate; up]``, linear e4m3 scales, per-expert fp32 dequant
+multiplier); a layer whose w13 halves are stored ``[up; gate]`` (the
+FlashInfer ordering the reference checks at ``routed_experts.py:1757-1760``)
+is reordered once at construction.
+
+:func:`register` installs the adapter into vLLM when vLLM provides the
+``RoutedExperts`` pluggable layer with a ``forward_modular`` method (the
+reference pins vLLM 0.26, ``pyproject.toml:36``); releases without
+it (0.22 aliases ``RoutedExperts`` to ``FusedMoE``) return False.
+"""
+
+from __future__ import annotations
+
+import torch
+
+from . import nvfp4_moe
+
+
+class RoutedExpertsB200:
+    """One MoE layer's routed experts on a B200.
+
+    Args (E experts, d hidden, I intermediate):
+      w13: uint8 [E, 2I, d/2] packed e2m1, rows [gate; up] (or [up; gate] with
+        ``w13_is_up_gate=True``).
+      w13_scale: uint8 [E, 2I, d/16] e4m3 block scales, linear layout.
+      w13_global: float32 [E] dequant multiplier (W = e2m1 * e4m3 * g).
+      w2, w2_scale, w2_global: the down projection, [E, d, I/2], [E, d, I/16], [E].
+      expert_map: optional int32 [n_global] mapping a global expert id to its
+        local row here, -1 where the expert lives elsewhere (the reference's
+        per-card slot map, ``routed_experts.py:354-382``); routes mapped to -1
+        contribute nothing.
+      multiply_router_weight: scale each route by its router weight.
+    """
+
+    def __init__(self, w13: torch.Tensor, w13_scale: torch.Tensor, w13_global: torch.Tensor,
+                 w2: torch.Tensor, w2_scale: torch.Tensor, w2_global: torch.Tensor, *,
+                 w13_is_up_gate: bool = False, expert_map: torch.Tensor | None = None,
+                 multiply_router_weight: bool = True):
+        if w13.dim() != 3 or w13.size(1) % 2:
+            raise ValueError("sbb200: w13 must be uint8 [E,2I,d/2]")
+        if w13_is_up_gate:
+            half = w13.size(1) // 2
+            w13 = torch.cat([w13[:, half:], w13[:, :half]], dim=1).contiguous()
+            w13_scale = torch.cat([w13_scale[:, half:], w13_scale[:, :half]], dim=1).contiguous()
+        self.w13, self.w13_scale = w13.contiguous(), w13_scale.contiguous()
+        self.w13_global = w13_global.float().contiguous()
+        self.w2, self.w2_scale = w2.contiguous(), w2_scale.contiguous()
+        self.w2_global = w2_global.float().contiguous()
+        if expert_map is not None:
+            expert_map = expert_map.to(device=w13.device, dtype=torch.int32).contiguous()
+            if expert_map.dim() != 1:
+                raise ValueError("sbb200: expert map must be int32 [n_global]")
+        self.expert_map = expert_map
+        self.multiply_router_weight = multiply_router_weight
+
+    @classmethod
+    def from_layer(cls, layer, **kw) -> "RoutedExpertsB200":
+        """Build from a vLLM-style layer object holding ``w13_weight``,
+        ``w13_weight_scale``, ``w13_weight_scale_2`` and the ``w2_*``
+        counterparts (``routed_experts.py:1529-1552, 1744-1753``). The scales
+        must be linear (unswizzled); a ``_w13_is_reordered()`` method, when
+        present, says whether the w13 halves are ``[up; gate]``."""
+        reordered = getattr(layer, "_w13_is_reordered", None)
+        kw.setdefault("w13_is_up_gate", bool(reordered()) if callable(reordered) else False)
+
+        def t(name):
+            v = getattr(layer, name)
+            return v.data if hasattr(v, "data") else v
+
+        return cls(t("w13_weight"), t("w13_weight_scale"), t("w13_weight_scale_2"),
+                   t("w2_weight"), t("w2_weight_scale"), t("w2_weight_scale_2"), **kw)
+
+    @property
+    def num_experts(self) -> int:
+        return self.w13.size(0)
+
+    def forward_modular(self, x: torch.Tensor, topk_weights: torch.Tensor,
+                        topk_ids: torch.Tensor, shared_experts=None,
+                        shared_experts_input: torch.Tensor | None = None) -> torch.Tensor:
+        """Routed-expert output [M, d] in x's dtype, plus the shared experts'
+        output when a shared-expert module is given (the hook's
+        ``Y_local + Y_routed`` sum, ``routed_experts.py:2517-2531``)."""
+        ids = topk_ids if topk_ids.dtype == torch.int32 else topk_ids.to(torch.int32)
+        if self.expert_map is not None:
+            valid = (ids >= 0) & (ids < self.expert_map.numel())
+            ids = torch.where(valid, self.expert_map[ids.clamp(0, self.expert_map.numel() - 1)],
+                              torch.full_like(ids, -1))
+        w = topk_weights if topk_weights.dtype == torch.float32 else topk_weights.float()
+        y = nvfp4_moe(x, ids.contiguous(), w.contiguous(), self.w13, self.w13_scale,
+                      self.w13_global, self.w2, self.w2_scale, self.w2_global,
+                      multiply_router_weight=self.multiply_router_weight, out_dtype=x.dtype)
+        if shared_experts is not None:
+            y = y + shared_experts(shared_experts_input if shared_experts_input is not None
+                                   else x)
+        return y
+
+    __call__ = forward_modular
+
+
+_registered = None
+
+
+def register() -> bool:
+    """Register a vLLM ``RoutedExperts`` subclass whose ``forward_modular``
+    runs this path, when the installed vLLM has that pluggable layer. Returns
+    False (and changes nothing) when it does not. Calling it again is a no-op."""
+    global _registered
+    try:
+        from vllm.model_executor.custom_op import PluggableLayer, op_registry_oot
+        from vllm.model_executor.layers.fused_moe import RoutedExperts  # type: ignore
+    except ImportError:
+        return False
+    if not hasattr(RoutedExperts, "forward_modular"):
+        # older vLLM (e.g. 0.22): RoutedExperts is FusedMoE without the
+        # modular forward the hook overrides
+        return False
+
+    if _registered is None:
+        class B200RoutedExperts(RoutedExperts):  # pragma: no cover - needs that vLLM layer
+            def forward_modular(self, x, topk_weights, topk_ids, shared_experts=None,
+                                shared_experts_input=None):
+                impl = getattr(self, "_sbb200", None)
+                if impl is None:
+                    impl = self._sbb200 = RoutedExpertsB200.from_layer(self)
+                return impl.forward_modular(x, topk_weights, topk_ids, shared_experts,
+                                            shared_experts_input)
+
+        _registered = B200RoutedExperts
+
+    existing = op_registry_oot.get("RoutedExperts")
+    if existing is None:
+        PluggableLayer.register_oot(_registered, name="RoutedExperts")
+    elif existing is not _registered:
+        raise RuntimeError("cannot install the B200 adapter: RoutedExperts is already replaced")
+    return True

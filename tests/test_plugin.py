@@ -1,0 +1,124 @@
+"""The vLLM hook adapter (shooting_brake_b200.plugin): host-side behaviour on
+the CPU, forward parity on the B200.
+
+The adapter mirrors HybridRoutedExperts.forward_modular
+(src/phase4/src/shooting_brake_vllm/routed_experts.py:2312-2397 of the
+reference): x bf16 [M, d], topk_weights fp32 [M, top_k], topk_ids [M, top_k]
+in, x-dtype [M, d] out, plus the shared experts' output when given."""
+
+from __future__ import annotations
+
+import importlib
+
+import numpy as np
+import pytest
+import torch
+
+from conftest import cosine, rel_err
+
+REL_TOL = 1e-2
+COS_TOL = 0.9999
+
+
+@pytest.fixture(scope="module")
+def plugin(sbb):
+    return importlib.import_module(sbb.__name__ + ".plugin")
+
+
+def _layer_tensors(oracle, device, E=8, K=256, I=256, seed=3):
+    L = oracle.make_layer(E, K, I, seed=seed)
+    ts = [torch.from_numpy(np.ascontiguousarray(x)).to(device)
+          for x in (L.w13, L.s13, L.g13, L.w2, L.s2, L.g2)]
+    return L, ts
+
+
+def test_up_gate_layout_is_reordered_once(plugin, oracle):
+    L, ts = _layer_tensors(oracle, "cpu")
+    I = L.I
+    swapped = [torch.cat([ts[0][:, I:], ts[0][:, :I]], 1), torch.cat([ts[1][:, I:], ts[1][:, :I]], 1)]
+    ex = plugin.RoutedExpertsB200(swapped[0], swapped[1], ts[2], ts[3], ts[4], ts[5],
+                                  w13_is_up_gate=True)
+    assert torch.equal(ex.w13, ts[0]) and torch.equal(ex.w13_scale, ts[1])
+
+
+def test_from_layer_reads_vllm_attribute_names(plugin, oracle):
+    L, ts = _layer_tensors(oracle, "cpu")
+
+    class FakeLayer:
+        pass
+
+    layer = FakeLayer()
+    for name, t in zip(("w13_weight", "w13_weight_scale", "w13_weight_scale_2", "w2_weight",
+                        "w2_weight_scale", "w2_weight_scale_2"), ts):
+        setattr(layer, name, torch.nn.Parameter(t, requires_grad=False))
+    layer._w13_is_reordered = lambda: False
+    ex = plugin.RoutedExpertsB200.from_layer(layer)
+    assert ex.num_experts == L.E and torch.equal(ex.w2, ts[3])
+
+
+def test_forward_on_cpu_tensors_raises(plugin, oracle):
+    """No CPU fallback: host tensors are rejected by the op."""
+    L, ts = _layer_tensors(oracle, "cpu")
+    ex = plugin.RoutedExpertsB200(*ts)
+    x = torch.zeros((2, L.K), dtype=torch.bfloat16)
+    ids = torch.zeros((2, 2), dtype=torch.int32)
+    w = torch.ones((2, 2), dtype=torch.float32)
+    with pytest.raises(Exception):
+        ex.forward_modular(x, w, ids)
+
+
+def test_register_without_modular_routed_experts(plugin):
+    """vLLM releases whose RoutedExperts has no forward_modular leave the
+    registry untouched."""
+    try:
+        from vllm.model_executor.layers.fused_moe import RoutedExperts
+    except Exception:
+        pytest.skip("vLLM not importable")
+    if hasattr(RoutedExperts, "forward_modular"):
+        pytest.skip("this vLLM has the modular hook")
+    assert plugin.register() is False
+
+
+# ---------------------------------------------------------------- GPU parity
+
+def _check(got, want):
+    assert rel_err(got, want) <= REL_TOL, rel_err(got, want)
+    assert cosine(got, want) >= COS_TOL, cosine(got, want)
+
+
+@pytest.mark.gpu
+def test_forward_modular_matches_oracle(plugin, oracle, cuda):
+    E, K, I, T, top_k = 16, 512, 256, 24, 4
+    L, ts = _layer_tensors(oracle, cuda, E, K, I, seed=11)
+    hidden = oracle.make_hidden(T, K, seed=12)
+    ids, w = oracle.route_logits(T, E, top_k, seed=13)
+    ex = plugin.RoutedExpertsB200(*ts)
+    x = torch.from_numpy(hidden).to(cuda).view(torch.bfloat16)
+    y = ex.forward_modular(x, torch.from_numpy(w).to(cuda), torch.from_numpy(ids).long().to(cuda))
+    assert y.dtype == torch.bfloat16 and y.shape == (T, K)
+    _check(y.float().cpu().numpy(), oracle.moe_forward(hidden, ids, w, L))
+
+
+@pytest.mark.gpu
+def test_expert_map_shard_and_shared_experts(plugin, oracle, cuda):
+    """A shard holding global experts [4, 12) of 16: routes to other experts
+    contribute nothing; the shared-expert output is added."""
+    E_glob, K, I, T, top_k = 16, 256, 256, 20, 4
+    L, _ = _layer_tensors(oracle, "cpu", E_glob, K, I, seed=21)
+    lo, hi = 4, 12
+    shard = oracle.Layer(hi - lo, K, I, L.w13[lo:hi], L.s13[lo:hi], L.g13[lo:hi],
+                         L.w2[lo:hi], L.s2[lo:hi], L.g2[lo:hi])
+    ts = [torch.from_numpy(np.ascontiguousarray(x)).to(cuda)
+          for x in (shard.w13, shard.s13, shard.g13, shard.w2, shard.s2, shard.g2)]
+    emap = torch.full((E_glob,), -1, dtype=torch.int32)
+    emap[lo:hi] = torch.arange(hi - lo, dtype=torch.int32)
+    hidden = oracle.make_hidden(T, K, seed=22)
+    ids, w = oracle.route_logits(T, E_glob, top_k, seed=23)
+    ex = plugin.RoutedExpertsB200(*ts, expert_map=emap)
+    x = torch.from_numpy(hidden).to(cuda).view(torch.bfloat16)
+    shared = lambda inp: torch.full_like(inp, 0.25)  # noqa: E731
+    y = ex.forward_modular(x, torch.from_numpy(w).to(cuda), torch.from_numpy(ids).to(cuda),
+                           shared_experts=shared)
+    local = np.where((ids >= lo) & (ids < hi), ids - lo, -1).astype(np.int32)
+    want = oracle.moe_forward(hidden, local, w, shard) + 0.25
+    _check(y.float().cpu().numpy(), want)
