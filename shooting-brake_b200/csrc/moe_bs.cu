@@ -480,20 +480,42 @@ __device__ __forceinline__ float2 e2m1x2_to_float2(uint32_t byte) {
 }
 
 
-// One CTA of kSplitThreads per source row. Without slot_of, row i is written
-// to output rows i*NT + t; with slot_of (token mode) source row i is token i
-// and its terms go to every route slot the token feeds (slot_of[i*top_k + k],
-// -1 skipped), so the token is split once however many experts it visits.
+// Splits rows into NT NVFP4 terms. Grid (rows, ceil(K / kSplitChunk)): each
+// CTA takes kSplitChunk elements of one source row, one 16-element block per
+// thread, so block maxima need no shuffles and a thread's packed block is one
+// 8-byte store. Every CTA of a row reduces the whole row for the row maximum
+// (at most 64 KB, read again from L2). Without slot_of, row i is written to
+// output rows i*NT + t; with slot_of (token mode) source row i is token i and
+// its terms go to every route slot the token feeds (slot_of[i*top_k + k], -1
+// skipped), so a token is split once however many experts it visits.
 // Outputs: packed e2m1 [row*NT + t, K/2], e4m3 scales [row*NT + t, K/16] and
-// the dequant global g [row*NT + t]. Thread T owns element pairs (2T, 2T+1)
-// of every 2*kSplitThreads-wide chunk, so a 16-element block is 8 lanes
-// (block maxima and nibble packing are shuffles) and a packed byte is one
-// thread's pair. One CTA reduction gives the row maximum; after that every
-// block runs its NT terms in registers.
-constexpr int kSplitThreads = 256;
-constexpr int kSplitMaxPairs = 16384 / (2 * kSplitThreads);  // K <= 16384
+// the dequant global g [row*NT + t].
+constexpr int kSplitThreads = 64;
+constexpr int kSplitChunk = 16 * kSplitThreads;
 
-template <int PAIRS>
+__device__ __forceinline__ void load8(const void* src, int src_dt, int64_t at, float* v) {
+  if (src_dt == kF32) {
+    const float4 a = *reinterpret_cast<const float4*>(static_cast<const float*>(src) + at);
+    const float4 b = *reinterpret_cast<const float4*>(static_cast<const float*>(src) + at + 4);
+    v[0] = a.x; v[1] = a.y; v[2] = a.z; v[3] = a.w;
+    v[4] = b.x; v[5] = b.y; v[6] = b.z; v[7] = b.w;
+  } else {
+    const uint4 w = *reinterpret_cast<const uint4*>(static_cast<const uint16_t*>(src) + at);
+    const uint32_t u[4] = {w.x, w.y, w.z, w.w};
+#pragma unroll
+    for (int i = 0; i < 4; ++i) {
+      if (src_dt == kBF16) {
+        v[2 * i] = __uint_as_float(u[i] << 16);
+        v[2 * i + 1] = __uint_as_float(u[i] & 0xFFFF0000u);
+      } else {
+        const float2 f = __half22float2(*reinterpret_cast<const __half2*>(&u[i]));
+        v[2 * i] = f.x;
+        v[2 * i + 1] = f.y;
+      }
+    }
+  }
+}
+
 __global__ void __launch_bounds__(kSplitThreads) split_nvfp4_kernel(
     const void* __restrict__ src, int src_dt, const int32_t* __restrict__ slot_of, int top_k,
     const int32_t* __restrict__ n_rows_dev, int K, int NT, uint8_t* __restrict__ q,
@@ -503,85 +525,67 @@ __global__ void __launch_bounds__(kSplitThreads) split_nvfp4_kernel(
   const int64_t row = blockIdx.x;
   if (n_rows_dev && row >= static_cast<int64_t>(*n_rows_dev)) return;
   const int tid = threadIdx.x;
-  const int lane = tid & 31;
-  const int warp = tid >> 5;
-  // destination rows of this source row's terms
   int ndst = 1;
   if (slot_of) {
-    if (tid < top_k) s_dst[tid] = slot_of[row * top_k + tid];
+    for (int i = tid; i < top_k; i += kSplitThreads) s_dst[i] = slot_of[row * top_k + i];
     ndst = top_k;
   }
-  // pairs per thread; with K % 64 == 0 the last partial chunk ends on a warp
-  // boundary, so every validity test below is warp-uniform
-  const int npairs = (K + 2 * kSplitThreads - 1) / (2 * kSplitThreads);
-  float2 v[PAIRS];
+  // row maximum
   float amax = 0.0f;
+  for (int k = tid * 8; k < K; k += kSplitThreads * 8) {
+    float v8[8];
+    load8(src, src_dt, row * K + k, v8);
 #pragma unroll
-  for (int i = 0; i < PAIRS; ++i) {
-    const int64_t k = static_cast<int64_t>(i) * 2 * kSplitThreads + 2 * tid;
-    v[i] = make_float2(0.0f, 0.0f);
-    if (i < npairs && k < K) {
-      if (src_dt == kBF16) {
-        const uint32_t w = *reinterpret_cast<const uint32_t*>(
-            static_cast<const uint16_t*>(src) + row * K + k);
-        v[i] = make_float2(__uint_as_float(w << 16), __uint_as_float(w & 0xFFFF0000u));
-      } else if (src_dt == kF32) {
-        v[i] = *reinterpret_cast<const float2*>(static_cast<const float*>(src) + row * K + k);
-      } else {
-        v[i] = __half22float2(*reinterpret_cast<const __half2*>(
-            static_cast<const __half*>(src) + row * K + k));
-      }
-      amax = fmaxf(amax, fmaxf(fabsf(v[i].x), fabsf(v[i].y)));
-    }
+    for (int i = 0; i < 8; ++i) amax = fmaxf(amax, fabsf(v8[i]));
   }
 #pragma unroll
   for (int d = 16; d > 0; d >>= 1) amax = fmaxf(amax, __shfl_xor_sync(0xffffffffu, amax, d));
-  if (lane == 0) s_max[warp] = amax;
+  if ((tid & 31) == 0) s_max[tid >> 5] = amax;
   __syncthreads();
   amax = s_max[0];
 #pragma unroll
   for (int w = 1; w < kSplitThreads / 32; ++w) amax = fmaxf(amax, s_max[w]);
   const float G0 = amax > 0.0f ? __fdiv_rn(2688.0f, amax) : 1.0f;
   const float g0 = __fdiv_rn(1.0f, G0);
-  if (tid < ndst) {
+  if (blockIdx.y == 0 && tid < ndst) {
     const int64_t dst = slot_of ? static_cast<int64_t>(s_dst[tid]) : row;
     if (dst >= 0)
       for (int t = 0; t < NT; ++t) gout[dst * NT + t] = ldexpf(g0, -2 * t);
   }
+  const int blk = blockIdx.y * kSplitThreads + tid;  // this thread's 16-element block
+  if (blk * 16 >= K) return;
+  float v[16];
+  load8(src, src_dt, row * K + blk * 16, v);
+  load8(src, src_dt, row * K + blk * 16 + 8, v + 8);
+  float G = G0, g = g0;
+  for (int t = 0; t < NT; ++t) {
+    float bmax = 0.0f;
 #pragma unroll
-  for (int i = 0; i < PAIRS; ++i) {
-    const int k = i * 2 * kSplitThreads + 2 * tid;  // first element of the pair
-    if (i < npairs && k < K) {
-      float G = G0, g = g0;
-      for (int t = 0; t < NT; ++t) {
-        float bmax = fmaxf(fabsf(v[i].x), fabsf(v[i].y));
-        bmax = fmaxf(bmax, __shfl_xor_sync(0xffffffffu, bmax, 1));
-        bmax = fmaxf(bmax, __shfl_xor_sync(0xffffffffu, bmax, 2));
-        bmax = fmaxf(bmax, __shfl_xor_sync(0xffffffffu, bmax, 4));
-        const float scale = fminf(__fmul_rn(G, __fmul_rn(bmax, 1.0f / 6.0f)), 448.0f);
-        const __nv_fp8_storage_t s8 = __nv_cvt_float_to_fp8(scale, __NV_SATFINITE, __NV_E4M3);
-        const float sg = __fmul_rn(e4m3_to_f32_hw(s8), g);  // one e2m1 step of this block
-        const float inv = sg == 0.0f ? 0.0f : __frcp_rn(sg);
-        // nearest e2m1 (ties to even, saturating at 6) of both elements
-        const uint32_t pair = e2m1x2_from_f32(__fmul_rn(v[i].x, inv), __fmul_rn(v[i].y, inv));
-        const float2 dq = e2m1x2_to_float2(pair);
-        // the MMA sees e2m1 * e4m3 * g; the next term quantises what is left
-        v[i].x -= __fmul_rn(dq.x, sg);
-        v[i].y -= __fmul_rn(dq.y, sg);
-        uint32_t w = pair << (8 * (lane & 3));
-        w |= __shfl_xor_sync(0xffffffffu, w, 1);
-        w |= __shfl_xor_sync(0xffffffffu, w, 2);
-        for (int d = 0; d < ndst; ++d) {
-          const int64_t dst = slot_of ? static_cast<int64_t>(s_dst[d]) : row;
-          if (dst < 0) continue;
-          const int64_t orow = dst * NT + t;
-          if ((lane & 3) == 0) *reinterpret_cast<uint32_t*>(q + orow * (K / 2) + k / 2) = w;
-          if ((lane & 7) == 0) sf[orow * (K / 16) + k / 16] = static_cast<uint8_t>(s8);
-        }
-        G = __fmul_rn(G, 4.0f);
-        g = __fmul_rn(g, 0.25f);
-      }
+    for (int i = 0; i < 16; ++i) bmax = fmaxf(bmax, fabsf(v[i]));
+    const float scale = fminf(__fmul_rn(G, __fmul_rn(bmax, 1.0f / 6.0f)), 448.0f);
+    const __nv_fp8_storage_t s8 = __nv_cvt_float_to_fp8(scale, __NV_SATFINITE, __NV_E4M3);
+    const float sg = __fmul_rn(e4m3_to_f32_hw(s8), g);  // one e2m1 step of this block
+    const float inv = sg == 0.0f ? 0.0f : __frcp_rn(sg);
+    uint32_t w[2] = {0u, 0u};
+#pragma unroll
+    for (int j = 0; j < 8; ++j) {
+      // nearest e2m1 (ties to even, saturating at 6) of both elements
+      const uint32_t pair = e2m1x2_from_f32(__fmul_rn(v[2 * j], inv), __fmul_rn(v[2 * j + 1], inv));
+      const float2 dq = e2m1x2_to_float2(pair);
+      // the MMA sees e2m1 * e4m3 * g; the next term quantises what is left
+      v[2 * j] -= __fmul_rn(dq.x, sg);
+      v[2 * j + 1] -= __fmul_rn(dq.y, sg);
+      w[j >> 2] |= pair << (8 * (j & 3));
     }
+    for (int d = 0; d < ndst; ++d) {
+      const int64_t dst = slot_of ? static_cast<int64_t>(s_dst[d]) : row;
+      if (dst < 0) continue;
+      const int64_t orow = dst * NT + t;
+      *reinterpret_cast<uint2*>(q + orow * (K / 2) + blk * 8) = make_uint2(w[0], w[1]);
+      sf[orow * (K / 16) + blk] = static_cast<uint8_t>(s8);
+    }
+    G = __fmul_rn(G, 4.0f);
+    g = __fmul_rn(g, 0.25f);
   }
 }
 
@@ -658,16 +662,9 @@ cudaError_t launch_split(const void* src, int src_dt, const int32_t* slot_of, in
                          const int32_t* n_rows_dev, int64_t n_rows, int K, uint8_t* q,
                          uint8_t* sf, float* g, cudaStream_t stream) {
   if (n_rows <= 0) return cudaSuccess;
-  const int pairs = (K + 2 * kSplitThreads - 1) / (2 * kSplitThreads);
-  const unsigned grid = static_cast<unsigned>(n_rows);
-#define SBB_SPLIT(P)                                                                         \
-  split_nvfp4_kernel<P><<<grid, kSplitThreads, 0, stream>>>(src, src_dt, slot_of, top_k,     \
-                                                            n_rows_dev, K, kSplitTerms, q, sf, g)
-  if (pairs <= 1) SBB_SPLIT(1);
-  else if (pairs <= 4) SBB_SPLIT(4);
-  else if (pairs <= 8) SBB_SPLIT(8);
-  else SBB_SPLIT(kSplitMaxPairs);
-#undef SBB_SPLIT
+  const dim3 grid(static_cast<unsigned>(n_rows), (K + kSplitChunk - 1) / kSplitChunk);
+  split_nvfp4_kernel<<<grid, kSplitThreads, 0, stream>>>(src, src_dt, slot_of, top_k, n_rows_dev,
+                                                         K, kSplitTerms, q, sf, g);
   return cudaGetLastError();
 }
 
