@@ -49,6 +49,9 @@ def parse():
     ap.add_argument("--cpu-seconds", type=float, default=12.0)
     ap.add_argument("--eager", action="store_true",
                     help="time eager calls instead of CUDA-graph replay")
+    ap.add_argument("--replicas", action="store_true",
+                    help="with N > 1, run N independent single-GPU replicas instead of "
+                         "expert parallelism")
     ap.add_argument("--layers", type=int, default=4,
                     help="independent layers rotated across steps (>= 2 keeps weights out of L2)")
     return ap.parse_args()
@@ -343,6 +346,154 @@ def run_reference_arm(args):
     print(json.dumps(line), flush=True)
 
 
+def run_expert_parallel(args, sbb, rank, world, local):
+    """Expert parallelism over NVLink, strong scaling: the global batch of T
+    tokens (config 1) is split evenly over the ranks, the 170 experts are
+    sharded contiguously, and every step runs one sbb200_ep_forward per rank.
+    `value` = T / (max over ranks of the per-step time)."""
+    import importlib
+
+    import torch
+    ep_mod = importlib.import_module(sbb.__name__ + ".ep")
+    device = torch.device("cuda", local)
+    T = args.tokens
+    if T % world:
+        raise SystemExit(f"--tokens {T} must divide evenly over {world} ranks")
+    Tr = T // world
+    N_LAYERS = args.layers
+    # identical full layers and global batches on every rank; each keeps its
+    # expert shard and its slice of the tokens
+    ep = ep_mod.ExpertParallel(rank=rank, world=world, device=local, max_tokens=Tr, top_k=TOP_K,
+                               E=E, K=D, I=I)
+    layers = []
+    for lw in make_layers(device, N_LAYERS, seed=1000):
+        layers.append(tuple(ep.local_experts(t).contiguous() for t in lw))
+        del lw
+    torch.cuda.empty_cache()
+    gbatches = [make_batch(device, T, seed=2000 + 17 * i) for i in range(N_LAYERS)]
+    batches = [tuple(x[rank * Tr:(rank + 1) * Tr].contiguous() for x in b) for b in gbatches]
+    out = torch.empty((Tr, D), dtype=torch.bfloat16, device=device)
+    stream = torch.cuda.current_stream(device)
+
+    def step(i):
+        h, ids, w = batches[i % N_LAYERS]
+        ep.forward(h, ids, w, *layers[i % N_LAYERS], out=out)
+
+    def timed(run_one, use_clocks):
+        torch.cuda.synchronize()
+        barrier(world)
+        torch.cuda.synchronize()
+        ev0 = torch.cuda.Event(enable_timing=True)
+        ev1 = torch.cuda.Event(enable_timing=True)
+        clk = ClockSampler(local) if use_clocks else None
+        if clk is not None:
+            clk.__enter__()
+            clk.wait_first_sample()
+        ev0.record(stream)
+        for i in range(args.steps):
+            run_one(i)
+        ev1.record(stream)
+        torch.cuda.synchronize()
+        if clk is not None:
+            clk.__exit__(None, None, None)
+        barrier(world)
+        return max_over_ranks(ev0.elapsed_time(ev1), world) / args.steps, clk
+
+    for i in range(max(args.warmup, 3)):
+        step(i)
+    graphs = []
+    if not args.eager:
+        cap = torch.cuda.Stream(device)
+        cap.wait_stream(stream)
+        torch.cuda.synchronize()
+        for i in range(N_LAYERS):
+            gr = torch.cuda.CUDAGraph()
+            with torch.cuda.graph(gr, stream=cap):
+                step(i)
+            graphs.append(gr)
+        torch.cuda.synchronize()
+        barrier(world)
+        for i in range(max(args.warmup, 3)):
+            graphs[i % N_LAYERS].replay()
+        ms, clk = timed(lambda i: graphs[i % N_LAYERS].replay(), True)
+        eager_ms, _ = timed(step, False)
+    else:
+        ms, clk = timed(step, True)
+        eager_ms = ms
+    clocks = clk.summary()
+
+    # end to end: this rank's tokens from pinned host memory, result back
+    host_in = [(h.cpu().pin_memory(), ids.cpu().pin_memory(), w.cpu().pin_memory())
+               for (h, ids, w) in batches]
+    host_out = torch.empty((Tr, D), dtype=torch.bfloat16).pin_memory()
+    dh, di, dw = (torch.empty_like(x) for x in batches[0])
+
+    def e2e_step(i):
+        hh, hi, hw = host_in[i % N_LAYERS]
+        dh.copy_(hh, non_blocking=True)
+        di.copy_(hi, non_blocking=True)
+        dw.copy_(hw, non_blocking=True)
+        o = ep.forward(dh, di, dw, *layers[i % N_LAYERS], out_dtype=torch.bfloat16)
+        host_out.copy_(o, non_blocking=True)
+
+    for i in range(max(args.warmup, 3)):
+        e2e_step(i)
+    e2e_ms, _ = timed(e2e_step, False)
+    errors = ep.device_errors()
+
+    ids_all = [b[1].cpu().numpy() for b in gbatches]
+    byts = [algorithmic_bytes(x, T) for x in ids_all]
+    avg_bytes = sum(b for b, _ in byts) / len(byts)
+    avg_distinct = sum(d for _, d in byts) / len(byts)
+    peaks = {}
+    try:
+        peaks = json.loads((ROOT / "MEASURED_PEAKS.json").read_text())
+    except Exception:
+        pass
+    hbm_peak = float(peaks.get("hbm_gbs", 6650.0))
+    peak_src = "measured" if "hbm_gbs" in peaks else "fallback"
+    per_gpu = avg_bytes / world / (ms * 1e-3) / 1e9
+    # publish + gather + the shard's MoE kernels + the final sum
+    launches = 2 + sbb.kernels_per_call(world * Tr, ep.expert_count, TOP_K, D, I) + 1
+    del graphs
+    if rank == 0:
+        line = {
+            "metric": METRIC, "value": T / (ms * 1e-3), "unit": "tokens/s", "n_gpus": world,
+            "steps": args.steps, "warmup": args.warmup, "ms_per_step": ms,
+            "higher_is_better": True, "scaling": "strong", "vs_baseline": None,
+            "dtype": "nvfp4 W4A16: e2m1 weights x 4-term e2m1 activation split, mxf4nvf4 MMA, "
+                     "fp32 accumulate",
+            "data": "synthetic",
+            "config": {"workload": f"config1-decode E={E} d={D} I={I} top{TOP_K} T={T}, "
+                                   f"experts sharded over {world} GPUs",
+                       "global_batch": T, "tokens_per_gpu": Tr, "parallelism": f"ep{world}",
+                       "exchange": "NVLink peer loads/stores (CUDA IPC), no NCCL on the data path",
+                       "l2": f"inputs larger than L2: {N_LAYERS} rotating layers of "
+                             f"{E * EXPERT_BYTES / 1e9:.2f} GB sharded",
+                       "distinct_experts_avg": avg_distinct,
+                       "algorithmic_bytes_per_step": avg_bytes},
+            "timing": "CUDA graph replay" if not args.eager else "eager calls",
+            "eager_ms_per_step": eager_ms,
+            "roofline": {"bound": "hbm", "achieved": per_gpu, "peak": hbm_peak, "unit": "GB/s",
+                         "frac": per_gpu / hbm_peak, "traffic": None,
+                         "kernel": "whole expert-parallel step per GPU (weight stream of the "
+                                   "shard + exchange)",
+                         "peak_source": f"{peak_src} hbm_gbs"},
+            "cpu_baseline": None,
+            "e2e": {"value": T / (e2e_ms * 1e-3), "unit": "tokens/s",
+                    "h2d_bytes_per_step": Tr * D * 2 + Tr * TOP_K * 8,
+                    "d2h_bytes_per_step": Tr * D * 2, "ms_per_step": e2e_ms},
+            "gpu_launches": launches * args.steps,
+            "device_errors": errors,
+            "clocks": clocks,
+        }
+        print(json.dumps(line), flush=True)
+    ep.close()
+    import torch.distributed as dist
+    dist.barrier()
+    dist.destroy_process_group()
+
+
 def main():
     args = parse()
     if args.impl == "reference":
@@ -357,6 +508,9 @@ def main():
     torch.cuda.set_device(device)
     sbb = g.load_package()
     T = args.tokens
+    if world > 1 and not args.replicas:
+        run_expert_parallel(args, sbb, rank, world, local)
+        return
 
     N_LAYERS = args.layers
     layers = make_layers(device, N_LAYERS, seed=1000 + rank)

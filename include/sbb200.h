@@ -213,6 +213,55 @@ int sbb200_moe_forward(sbb200_provider_t* p, size_t layer, void* stream, const v
 int sbb200_health(sbb200_provider_t* p, sbb200_health_t* health, char* last_error,
                   size_t last_error_size);
 
+/* ---------------------------------------------------------------------------
+ * Expert parallelism over NVLink: one process per GPU of one node, the E
+ * routed experts sharded contiguously (the first E % world ranks hold one
+ * extra), tokens kept by the rank that owns them. Replaces the reference's
+ * multi-card split, where every card sees all routes with foreign experts as
+ * -1 and the host sums the per-card outputs (src/phase4/src/
+ * shooting_brake_vllm/routed_experts.py:354-382, 2460-2463, 2522-2524).
+ * Bring-up: create on every rank, exchange the SBB200_EP_HANDLE_BYTES handle
+ * of each rank (any host transport; rank order), connect. Every rank then
+ * calls sbb200_ep_forward once per step, in the same order; the exchange is
+ * device-resident (no NCCL on the data path, no host synchronisation).
+ * ------------------------------------------------------------------------- */
+
+#define SBB200_EP_HANDLE_BYTES 64
+
+typedef struct sbb200_ep sbb200_ep_t;
+
+/* Expert shard [*begin, *begin + *count) of `rank`. */
+int sbb200_ep_shard(size_t E, int world, int rank, size_t* begin, size_t* count);
+
+/* Exchange state of `rank` of `world` on `device` for up to max_tokens
+ * tokens per rank (hidden K in act_dt, top_k routes, E experts in total,
+ * intermediate I; K and I multiples of 256). NULL on failure. */
+sbb200_ep_t* sbb200_ep_create(int device, int rank, int world, size_t max_tokens, size_t top_k,
+                              size_t E, size_t K, size_t I, int act_dt);
+
+/* This rank's exchange-buffer handle (SBB200_EP_HANDLE_BYTES bytes). */
+int sbb200_ep_ipc_handle(sbb200_ep_t* ep, void* out, size_t size);
+
+/* Map every other rank's buffer: `handles` holds world handles in rank order. */
+int sbb200_ep_connect(sbb200_ep_t* ep, const void* handles, size_t size);
+
+/* One expert-parallel layer step on `stream`: this rank's M tokens (hidden
+ * [M, K] in act_dt, topk_ids int32 [M, top_k] with global expert ids,
+ * topk_weights fp32 [M, top_k]) in, out [M, K] in out_dt; w13..w2_global_scales
+ * are this rank's shard (sbb200_ep_shard) in the layout of sbb200_nvfp4_moe,
+ * indexed by local expert id. M may be 0 (the rank still serves its experts). */
+int sbb200_ep_forward(sbb200_ep_t* ep, void* stream, const void* hidden, const int32_t* topk_ids,
+                      const float* topk_weights, size_t M, const void* w13,
+                      const void* w13_scales, const float* w13_global_scales, const void* w2,
+                      const void* w2_scales, const float* w2_global_scales, void* out,
+                      int out_dt, int multiply_router_weight);
+
+/* Error bits raised on the device since the last read (bit 0: a wait for
+ * another rank passed its 2 s deadline); reads, clears, synchronises. */
+int sbb200_ep_device_errors(sbb200_ep_t* ep, void* stream, uint32_t* errors);
+
+void sbb200_ep_destroy(sbb200_ep_t* ep);
+
 #ifdef __cplusplus
 }
 #endif

@@ -12,7 +12,8 @@ this module reaches it through ctypes and exposes:
   :func:`nvfp4_dequant`, :func:`nvfp4_quantize`);
 * :class:`Provider` -- registered layers with an owned workspace
   (the device-resident replacement of the B70 provider C-ABI);
-* :mod:`.plugin` -- the vLLM ``RoutedExperts`` hook adapter.
+* :mod:`.plugin` -- the vLLM ``RoutedExperts`` hook adapter;
+* :mod:`.ep` -- expert parallelism over NVLink (one process per GPU).
 
 There is no CPU fallback: every entry point raises if the CUDA library is
 missing or the tensors are not on a CUDA device.
@@ -93,6 +94,20 @@ def lib() -> ctypes.CDLL:
         L.sbb200_moe_forward.argtypes = [P, S, P, P, I, P, P, P, I, S, I]
         L.sbb200_health.restype = I
         L.sbb200_health.argtypes = [P, P, ctypes.c_char_p, S]
+        L.sbb200_ep_shard.restype = I
+        L.sbb200_ep_shard.argtypes = [S, I, I, P, P]
+        L.sbb200_ep_create.restype = P
+        L.sbb200_ep_create.argtypes = [I, I, I, S, S, S, S, S, I]
+        L.sbb200_ep_ipc_handle.restype = I
+        L.sbb200_ep_ipc_handle.argtypes = [P, P, S]
+        L.sbb200_ep_connect.restype = I
+        L.sbb200_ep_connect.argtypes = [P, P, S]
+        L.sbb200_ep_forward.restype = I
+        L.sbb200_ep_forward.argtypes = [P, P, P, P, P, S, P, P, P, P, P, P, P, I, I]
+        L.sbb200_ep_device_errors.restype = I
+        L.sbb200_ep_device_errors.argtypes = [P, P, P]
+        L.sbb200_ep_destroy.restype = None
+        L.sbb200_ep_destroy.argtypes = [P]
         _lib = L
     return _lib
 

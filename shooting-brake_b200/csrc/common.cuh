@@ -70,3 +70,42 @@ __device__ __forceinline__ uint64_t globaltimer_ns() {
 }
 
 }  // namespace sbb
+
+namespace sbb {
+
+// --------------------------------------------------------------------------
+// Cross-GPU flags (expert-parallel exchange over NVLink peer memory).
+// --------------------------------------------------------------------------
+
+__device__ __forceinline__ void st_release_sys(unsigned long long* p, unsigned long long v) {
+  asm volatile("st.release.sys.global.u64 [%0], %1;" ::"l"(p), "l"(v) : "memory");
+}
+
+__device__ __forceinline__ unsigned long long ld_acquire_sys(const unsigned long long* p) {
+  unsigned long long v;
+  asm volatile("ld.acquire.sys.global.u64 %0, [%1];" : "=l"(v) : "l"(p) : "memory");
+  return v;
+}
+
+// Called by every thread of every CTA after its last write of the kernel.
+// The CTA that finishes last sets each flag to `value` once all CTAs' writes
+// are visible at system scope, then rearms the counter for the next launch.
+__device__ __forceinline__ void signal_after_all_ctas(unsigned int* counter,
+                                                      unsigned long long* const* flags, int n,
+                                                      unsigned long long value) {
+  __shared__ unsigned int s_last;
+  __threadfence_system();
+  __syncthreads();
+  if (threadIdx.x == 0) {
+    const unsigned int total = gridDim.x * gridDim.y * gridDim.z;
+    s_last = atomicAdd(counter, 1u) == total - 1u;
+  }
+  __syncthreads();
+  if (s_last) {
+    __threadfence_system();
+    for (int i = threadIdx.x; i < n; i += blockDim.x) st_release_sys(flags[i], value);
+    if (threadIdx.x == 0) *counter = 0u;
+  }
+}
+
+}  // namespace sbb

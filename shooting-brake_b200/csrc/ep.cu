@@ -1,0 +1,580 @@
+// Expert parallelism over NVLink: the routed experts of a layer are sharded
+// contiguously over the GPUs of one node (one process per GPU), the tokens
+// stay with the rank that owns them, and each step exchanges activations and
+// partial outputs through peer memory.
+//
+// The reference splits experts disjointly over its cards with dense per-card
+// slot maps; every card sees all routes with foreign experts as -1 and the
+// host sums the per-card partial outputs (src/phase4/src/shooting_brake_vllm/
+// routed_experts.py:354-382, 2460-2463, 2522-2524). Here the exchange is
+// device-resident and stream-ordered:
+//
+//   publish  (source s)  copy this step's hidden rows, ids and weights into
+//                        s's exchange buffer; the last CTA bumps the device
+//                        epoch and sets ready[s] = epoch << 32 | M on every
+//                        rank (system-scope release store through NVLink).
+//   gather   (dest d)    wait for every ready flag (bounded), read each
+//                        source's ids over NVLink and keep the routes to d's
+//                        experts as local ids (-1 elsewhere) for the virtual
+//                        token list v = s * max_tokens + t.
+//   MoE      (dest d)    the single-GPU pipeline on the virtual tokens: the
+//                        activation split reads each routed token's row
+//                        straight from its source GPU (pull), the GEMMs run
+//                        on d's shard, and the combine stores each token's
+//                        fp32 partial sum (router weights applied) into its
+//                        source's partial[d] rows (push); its last CTA sets
+//                        done[d] = epoch on every rank.
+//   final    (source s)  wait for every done flag (bounded) and sum the
+//                        partials of the ranks that own the token's experts in
+//                        ascending rank order (a fixed order, so repeat runs
+//                        are bit-identical).
+//
+// No NCCL call is on the data path; the process group only exchanges the
+// CUDA IPC handles of the exchange buffers once. The buffers are reused
+// every step without a barrier: a source republishes only after its final
+// combine has seen every destination's done flag, and a destination sends
+// partials for step i+1 only after it saw ready for step i+1, so neither
+// side can overwrite data the other still reads. Every wait gives up after a
+// deadline and raises an error bit instead of spinning forever. No TMA or
+// bulk copy reads peer memory: peer data moves with plain loads and stores.
+#include <cuda_runtime.h>
+
+#include <algorithm>
+#include <cstddef>
+#include <cstring>
+#include <mutex>
+#include <new>
+#include <string>
+#include <vector>
+
+#include "common.cuh"
+#include "kernels.h"
+#include "moe_driver.h"
+#include "sbb200.h"
+
+namespace sbb {
+namespace {
+
+constexpr int kMaxWorld = 64;
+constexpr uint64_t kWaitNs = 2000000000ull;  // 2 s per wait
+constexpr int kEpThreads = 256;
+
+inline size_t align256(size_t v) { return (v + 255) / 256 * 256; }
+
+// Exchange buffer of one rank (identical layout on every rank; peers write
+// ready/done flags and partial rows into it).
+struct ExLayout {
+  size_t ready;    // u64[world]: ready[s] written by source s
+  size_t done;     // u64[world]: done[d] written by destination d
+  size_t hidden;   // act [max_tokens, K]
+  size_t ids;      // i32 [max_tokens, top_k]
+  size_t weights;  // f32 [max_tokens, top_k]
+  size_t partial;  // f32 [world, max_tokens, K]: partial[d] written by d
+  size_t total;
+};
+
+ExLayout ex_layout(int world, size_t max_tokens, size_t top_k, size_t K, size_t act_bytes) {
+  ExLayout l{};
+  size_t at = 0;
+  auto take = [&](size_t b) {
+    const size_t h = at;
+    at = align256(at + b);
+    return h;
+  };
+  l.ready = take(world * 8);
+  l.done = take(world * 8);
+  l.hidden = take(max_tokens * K * act_bytes);
+  l.ids = take(max_tokens * top_k * 4);
+  l.weights = take(max_tokens * top_k * 4);
+  l.partial = take(static_cast<size_t>(world) * max_tokens * K * 4);
+  l.total = at;
+  return l;
+}
+
+// Device-side state of this rank (local memory).
+struct EpDev {
+  unsigned long long epoch;     // step counter, bumped by publish
+  unsigned int publish_ctr;     // last-CTA counters
+  unsigned int combine_ctr;
+  unsigned int errors;          // bit 0: a wait timed out (sticky until read)
+  unsigned int pad[3];
+};
+
+struct EpTables {
+  // [world] each
+  unsigned long long* ready_at_peer[kMaxWorld];  // &peer.ready[rank]
+  unsigned long long* done_at_peer[kMaxWorld];   // &peer.done[rank]
+  const void* peer_hidden[kMaxWorld];
+  const int32_t* peer_ids[kMaxWorld];
+  const float* peer_weights[kMaxWorld];
+  void* partial_at_peer[kMaxWorld];              // &peer.partial[rank][0]
+  int shard_begin[kMaxWorld + 1];
+};
+
+__device__ __forceinline__ bool wait_epoch(const unsigned long long* flag, unsigned long long epoch,
+                                           bool hi_word, unsigned long long* seen,
+                                           unsigned int* errors, uint64_t deadline) {
+  for (uint32_t i = 0;; ++i) {
+    const unsigned long long v = ld_acquire_sys(flag);
+    if ((hi_word ? (v >> 32) : v) == epoch) {
+      *seen = v;
+      return true;
+    }
+    if ((i & 63u) == 63u) {
+      if (globaltimer_ns() > deadline || (*reinterpret_cast<volatile unsigned int*>(errors) & 1u)) {
+        atomicOr(errors, 1u);
+        return false;
+      }
+    }
+  }
+}
+
+// Copy this step's tokens into the exchange buffer, then signal every rank.
+__global__ void __launch_bounds__(kEpThreads) ep_publish_kernel(
+    const uint4* __restrict__ hidden, int64_t hidden_vec, const int32_t* __restrict__ ids,
+    const float* __restrict__ weights, int64_t routes, uint4* __restrict__ ex_hidden,
+    int32_t* __restrict__ ex_ids, float* __restrict__ ex_weights, EpDev* dev,
+    const EpTables* __restrict__ tab, int world, int64_t M) {
+  const int64_t stride = static_cast<int64_t>(gridDim.x) * blockDim.x;
+  for (int64_t i = blockIdx.x * blockDim.x + threadIdx.x; i < hidden_vec; i += stride)
+    ex_hidden[i] = hidden[i];
+  for (int64_t i = blockIdx.x * blockDim.x + threadIdx.x; i < routes; i += stride) {
+    ex_ids[i] = ids[i];
+    ex_weights[i] = weights[i];
+  }
+  // the epoch this step signals: every CTA reads the old value before the
+  // last one stores the new one (the store happens after all increments)
+  const unsigned long long next = dev->epoch + 1ull;
+  __shared__ unsigned int s_last;
+  __threadfence_system();
+  __syncthreads();
+  if (threadIdx.x == 0) s_last = atomicAdd(&dev->publish_ctr, 1u) == gridDim.x - 1u;
+  __syncthreads();
+  if (s_last) {
+    __threadfence_system();
+    for (int p = threadIdx.x; p < world; p += blockDim.x)
+      st_release_sys(tab->ready_at_peer[p], (next << 32) | static_cast<unsigned long long>(M));
+    if (threadIdx.x == 0) {
+      dev->epoch = next;
+      dev->publish_ctr = 0u;
+    }
+  }
+}
+
+// Local routes of every virtual token v = s * max_tokens + t.
+__global__ void __launch_bounds__(kEpThreads) ep_gather_kernel(
+    const unsigned long long* __restrict__ ready, EpDev* dev, const EpTables* __restrict__ tab,
+    int world, int64_t max_tokens, int top_k, int rank, int32_t* __restrict__ local_ids,
+    float* __restrict__ local_w) {
+  __shared__ int64_t s_count[kMaxWorld];
+  const unsigned long long epoch = dev->epoch;
+  const uint64_t deadline = globaltimer_ns() + kWaitNs;
+  for (int s = threadIdx.x; s < world; s += blockDim.x) {
+    unsigned long long v = 0;
+    s_count[s] = wait_epoch(&ready[s], epoch, true, &v, &dev->errors, deadline)
+                     ? static_cast<int64_t>(v & 0xffffffffull)
+                     : 0;
+  }
+  __syncthreads();
+  const int e_lo = tab->shard_begin[rank];
+  const int e_hi = tab->shard_begin[rank + 1];
+  const int64_t total = static_cast<int64_t>(world) * max_tokens * top_k;
+  for (int64_t i = blockIdx.x * static_cast<int64_t>(blockDim.x) + threadIdx.x; i < total;
+       i += static_cast<int64_t>(gridDim.x) * blockDim.x) {
+    const int64_t v = i / top_k;
+    const int s = static_cast<int>(v / max_tokens);
+    const int64_t t = v % max_tokens;
+    int32_t lid = -1;
+    float w = 0.0f;
+    if (t < s_count[s]) {
+      const int64_t r = t * top_k + (i % top_k);
+      const int32_t e = __ldcg(tab->peer_ids[s] + r);
+      if (e >= e_lo && e < e_hi) {
+        lid = e - e_lo;
+        w = __ldcg(tab->peer_weights[s] + r);
+      }
+    }
+    local_ids[i] = lid;
+    local_w[i] = w;
+  }
+}
+
+// out[t] = sum over owning ranks d (ascending) of partial[d][t].
+__global__ void __launch_bounds__(kEpThreads) ep_final_kernel(
+    const unsigned long long* __restrict__ done, EpDev* dev, const EpTables* __restrict__ tab,
+    int world, const int32_t* __restrict__ ids, int top_k, int E, const float* __restrict__ partial,
+    int64_t max_tokens, int K, void* __restrict__ out, int out_dt) {
+  __shared__ unsigned long long s_mask;
+  const int64_t t = blockIdx.x;
+  const unsigned long long epoch = dev->epoch;
+  if (threadIdx.x == 0) {
+    unsigned long long mask = 0;
+    for (int k = 0; k < top_k; ++k) {
+      const int32_t e = ids[t * top_k + k];
+      if (e < 0 || e >= E) continue;
+      int d = 0;
+      while (d + 1 < world && tab->shard_begin[d + 1] <= e) ++d;
+      mask |= 1ull << d;
+    }
+    s_mask = mask;
+  }
+  const uint64_t deadline = globaltimer_ns() + kWaitNs;
+  for (int d = threadIdx.x; d < world; d += blockDim.x) {
+    unsigned long long v = 0;
+    wait_epoch(&done[d], epoch, false, &v, &dev->errors, deadline);
+  }
+  __syncthreads();
+  const unsigned long long mask = s_mask;
+  for (int n4 = (blockIdx.y * blockDim.x + threadIdx.x) * 4; n4 < K;
+       n4 += gridDim.y * blockDim.x * 4) {
+    float4 acc = make_float4(0.f, 0.f, 0.f, 0.f);
+    for (int d = 0; d < world; ++d) {
+      if (!((mask >> d) & 1ull)) continue;
+      const float4 p = __ldcg(reinterpret_cast<const float4*>(
+          partial + (static_cast<int64_t>(d) * max_tokens + t) * K + n4));
+      acc.x += p.x;
+      acc.y += p.y;
+      acc.z += p.z;
+      acc.w += p.w;
+    }
+    const int64_t at = t * K + n4;
+    if (out_dt == kF32) {
+      *reinterpret_cast<float4*>(static_cast<float*>(out) + at) = acc;
+    } else if (out_dt == kBF16) {
+      __nv_bfloat162 a = __floats2bfloat162_rn(acc.x, acc.y);
+      __nv_bfloat162 b = __floats2bfloat162_rn(acc.z, acc.w);
+      *reinterpret_cast<uint2*>(static_cast<__nv_bfloat16*>(out) + at) =
+          make_uint2(*reinterpret_cast<uint32_t*>(&a), *reinterpret_cast<uint32_t*>(&b));
+    } else {
+      __half2 a = __floats2half2_rn(acc.x, acc.y);
+      __half2 b = __floats2half2_rn(acc.z, acc.w);
+      *reinterpret_cast<uint2*>(static_cast<__half*>(out) + at) =
+          make_uint2(*reinterpret_cast<uint32_t*>(&a), *reinterpret_cast<uint32_t*>(&b));
+    }
+  }
+}
+
+size_t act_size(int dt) { return dt == SBB200_F32 ? 4 : 2; }
+
+}  // namespace
+
+// Contiguous expert shards: the first E % world ranks hold one extra expert.
+void ep_shard(size_t E, int world, int rank, size_t* begin, size_t* count) {
+  const size_t base = E / world, extra = E % world;
+  const size_t r = static_cast<size_t>(rank);
+  *begin = r * base + (r < extra ? r : extra);
+  *count = base + (r < extra ? 1 : 0);
+}
+
+}  // namespace sbb
+
+struct sbb200_ep {
+  int device = 0, rank = 0, world = 1, act_dt = SBB200_BF16;
+  size_t max_tokens = 0, top_k = 0, E = 0, K = 0, I = 0, e_begin = 0, e_count = 0;
+  sbb::ExLayout lay{};
+  char* ex = nullptr;                 // this rank's exchange buffer (IPC-exported)
+  std::vector<char*> peers;           // opened peer buffers (own buffer at [rank])
+  sbb::EpDev* dev = nullptr;          // local device state
+  sbb::EpTables* tab = nullptr;       // device copy of the peer tables
+  sbb::EpTables host_tab{};
+  int32_t* local_ids = nullptr;       // [world * max_tokens, top_k]
+  float* local_w = nullptr;
+  void* workspace = nullptr;          // MoE workspace for world * max_tokens tokens
+  sbb::WorkspacePlan plan{};
+  bool connected = false;
+  std::mutex mu;
+};
+
+namespace {
+
+int ep_fail(int code, const std::string& msg) {
+  sbb::set_last_error(msg);
+  return code;
+}
+
+struct DeviceGuard {
+  int prev = 0;
+  bool ok = false;
+  explicit DeviceGuard(int dev) {
+    cudaGetDevice(&prev);
+    ok = cudaSetDevice(dev) == cudaSuccess;
+  }
+  ~DeviceGuard() { cudaSetDevice(prev); }
+};
+
+void ep_free(sbb200_ep* p) {
+  DeviceGuard g(p->device);
+  for (int i = 0; i < static_cast<int>(p->peers.size()); ++i)
+    if (p->peers[i] && i != p->rank) cudaIpcCloseMemHandle(p->peers[i]);
+  cudaFree(p->ex);
+  cudaFree(p->dev);
+  cudaFree(p->tab);
+  cudaFree(p->local_ids);
+  cudaFree(p->local_w);
+  cudaFree(p->workspace);
+}
+
+}  // namespace
+
+extern "C" {
+
+int sbb200_ep_shard(size_t E, int world, int rank, size_t* begin, size_t* count) {
+  if (world < 1 || world > sbb::kMaxWorld || rank < 0 || rank >= world || !begin || !count ||
+      E < static_cast<size_t>(world))
+    return ep_fail(SBB200_EINVAL, "ep shard: need 1 <= world <= 64, 0 <= rank < world, E >= world");
+  sbb::ep_shard(E, world, rank, begin, count);
+  return SBB200_OK;
+}
+
+sbb200_ep_t* sbb200_ep_create(int device, int rank, int world, size_t max_tokens, size_t top_k,
+                              size_t E, size_t K, size_t I, int act_dt) {
+  try {
+    std::string why;
+    if (world < 1 || world > sbb::kMaxWorld || rank < 0 || rank >= world) {
+      sbb::set_last_error("ep create: need 1 <= world <= 64 and 0 <= rank < world");
+      return nullptr;
+    }
+    if (max_tokens == 0 || E < static_cast<size_t>(world) ||
+        sbb::validate_shape(max_tokens * world, E, top_k, K, I, act_dt, SBB200_F32, &why) != 0) {
+      sbb::set_last_error("ep create: " + (why.empty() ? std::string("need max_tokens > 0 and E >= world") : why));
+      return nullptr;
+    }
+    if (K % 256 != 0 || I % 256 != 0 || E >= (1u << 31)) {
+      sbb::set_last_error("ep create: expert parallelism needs K and I multiples of 256");
+      return nullptr;
+    }
+    auto* p = new (std::nothrow) sbb200_ep();
+    if (!p) return nullptr;
+    p->device = device;
+    p->rank = rank;
+    p->world = world;
+    p->act_dt = act_dt;
+    p->max_tokens = max_tokens;
+    p->top_k = top_k;
+    p->E = E;
+    p->K = K;
+    p->I = I;
+    sbb::ep_shard(E, world, rank, &p->e_begin, &p->e_count);
+    p->lay = sbb::ex_layout(world, max_tokens, top_k, K, sbb::act_size(act_dt));
+    const size_t vt = static_cast<size_t>(world) * max_tokens;
+    const size_t e_local_max = (E + world - 1) / world;
+    p->plan = sbb::plan_workspace(vt, e_local_max, top_k, K, I);
+    DeviceGuard g(device);
+    cudaError_t e = g.ok ? cudaSuccess : cudaErrorInvalidDevice;
+    if (e == cudaSuccess) e = cudaMalloc(&p->ex, p->lay.total);
+    if (e == cudaSuccess) e = cudaMemset(p->ex, 0, p->lay.hidden);  // ready and done flags
+    if (e == cudaSuccess) e = cudaMalloc(&p->dev, sizeof(sbb::EpDev));
+    if (e == cudaSuccess) e = cudaMemset(p->dev, 0, sizeof(sbb::EpDev));
+    if (e == cudaSuccess) e = cudaMalloc(&p->tab, sizeof(sbb::EpTables));
+    if (e == cudaSuccess) e = cudaMalloc(&p->local_ids, vt * top_k * 4);
+    if (e == cudaSuccess) e = cudaMalloc(&p->local_w, vt * top_k * 4);
+    if (e == cudaSuccess) e = cudaMalloc(&p->workspace, p->plan.total);
+    if (e == cudaSuccess) e = cudaDeviceSynchronize();
+    if (e != cudaSuccess) {
+      sbb::set_last_error(std::string("ep create: ") + cudaGetErrorString(e));
+      ep_free(p);
+      delete p;
+      return nullptr;
+    }
+    return p;
+  } catch (...) {
+    sbb::set_last_error("ep create: host exception");
+    return nullptr;
+  }
+}
+
+int sbb200_ep_ipc_handle(sbb200_ep_t* p, void* out, size_t size) {
+  if (!p || !out || size < sizeof(cudaIpcMemHandle_t))
+    return ep_fail(SBB200_EINVAL, "ep handle: null handle or buffer below SBB200_EP_HANDLE_BYTES");
+  DeviceGuard g(p->device);
+  cudaIpcMemHandle_t h;
+  const cudaError_t e = cudaIpcGetMemHandle(&h, p->ex);
+  if (e != cudaSuccess) return ep_fail(SBB200_ECUDA, std::string("ep handle: ") + cudaGetErrorString(e));
+  std::memcpy(out, &h, sizeof h);
+  return SBB200_OK;
+}
+
+int sbb200_ep_connect(sbb200_ep_t* p, const void* handles, size_t size) {
+  if (!p || !handles || size < sizeof(cudaIpcMemHandle_t) * p->world)
+    return ep_fail(SBB200_EINVAL, "ep connect: need world * SBB200_EP_HANDLE_BYTES handle bytes");
+  std::lock_guard<std::mutex> lk(p->mu);
+  if (p->connected) return ep_fail(SBB200_EINVAL, "ep connect: already connected");
+  DeviceGuard g(p->device);
+  p->peers.assign(p->world, nullptr);
+  for (int r = 0; r < p->world; ++r) {
+    if (r == p->rank) {
+      p->peers[r] = p->ex;
+      continue;
+    }
+    cudaIpcMemHandle_t h;
+    std::memcpy(&h, static_cast<const char*>(handles) + r * sizeof h, sizeof h);
+    void* ptr = nullptr;
+    const cudaError_t e = cudaIpcOpenMemHandle(&ptr, h, cudaIpcMemLazyEnablePeerAccess);
+    if (e != cudaSuccess) {
+      for (int i = 0; i < r; ++i)
+        if (i != p->rank && p->peers[i]) cudaIpcCloseMemHandle(p->peers[i]);
+      p->peers.assign(p->world, nullptr);
+      return ep_fail(SBB200_ECUDA, "ep connect: opening the buffer of rank " + std::to_string(r) +
+                                       ": " + cudaGetErrorString(e));
+    }
+    p->peers[r] = static_cast<char*>(ptr);
+  }
+  sbb::EpTables& t = p->host_tab;
+  std::memset(&t, 0, sizeof t);
+  for (int r = 0; r < p->world; ++r) {
+    char* b = p->peers[r];
+    t.ready_at_peer[r] = reinterpret_cast<unsigned long long*>(b + p->lay.ready) + p->rank;
+    t.done_at_peer[r] = reinterpret_cast<unsigned long long*>(b + p->lay.done) + p->rank;
+    t.peer_hidden[r] = b + p->lay.hidden;
+    t.peer_ids[r] = reinterpret_cast<const int32_t*>(b + p->lay.ids);
+    t.peer_weights[r] = reinterpret_cast<const float*>(b + p->lay.weights);
+    t.partial_at_peer[r] =
+        reinterpret_cast<float*>(b + p->lay.partial) + static_cast<size_t>(p->rank) * p->max_tokens * p->K;
+  }
+  for (int r = 0; r <= p->world; ++r) {
+    size_t b = 0, c = 0;
+    if (r < p->world) {
+      sbb::ep_shard(p->E, p->world, r, &b, &c);
+    } else {
+      b = p->E;
+    }
+    t.shard_begin[r] = static_cast<int>(b);
+  }
+  const cudaError_t e = cudaMemcpy(p->tab, &t, sizeof t, cudaMemcpyHostToDevice);
+  if (e != cudaSuccess) return ep_fail(SBB200_ECUDA, std::string("ep connect: ") + cudaGetErrorString(e));
+  p->connected = true;
+  return SBB200_OK;
+}
+
+int sbb200_ep_forward(sbb200_ep_t* p, void* stream, const void* hidden, const int32_t* topk_ids,
+                      const float* topk_weights, size_t M, const void* w13, const void* w13_scales,
+                      const float* w13_global_scales, const void* w2, const void* w2_scales,
+                      const float* w2_global_scales, void* out, int out_dt,
+                      int multiply_router_weight) {
+  try {
+    if (!p) return ep_fail(SBB200_EINVAL, "ep forward: null handle");
+    if (!p->connected) return ep_fail(SBB200_EINVAL, "ep forward: connect the ranks first");
+    if (M > p->max_tokens)
+      return ep_fail(SBB200_EINVAL, "ep forward: M above the max_tokens given at create");
+    if ((M && (!hidden || !topk_ids || !topk_weights || !out)) || !w13 || !w13_scales ||
+        !w13_global_scales || !w2 || !w2_scales || !w2_global_scales)
+      return ep_fail(SBB200_EINVAL, "ep forward: null pointer argument");
+    if (out_dt != SBB200_F32 && out_dt != SBB200_F16 && out_dt != SBB200_BF16)
+      return ep_fail(SBB200_EINVAL, "ep forward: output dtype must be f32, f16 or bf16");
+    if ((reinterpret_cast<uintptr_t>(hidden) | reinterpret_cast<uintptr_t>(out)) % 16 != 0)
+      return ep_fail(SBB200_EINVAL, "ep forward: hidden and out must be 16-byte aligned");
+    std::lock_guard<std::mutex> lk(p->mu);
+    DeviceGuard g(p->device);
+    auto s = static_cast<cudaStream_t>(stream);
+    const int64_t K = static_cast<int64_t>(p->K);
+    const int64_t routes = static_cast<int64_t>(M * p->top_k);
+    char* ex = p->ex;
+    // 1. publish
+    {
+      const int64_t vec = static_cast<int64_t>(M) * K * sbb::act_size(p->act_dt) / 16;
+      int blocks = static_cast<int>(std::min<int64_t>(148 * 4, (vec + sbb::kEpThreads - 1) / sbb::kEpThreads));
+      if (blocks < 1) blocks = 1;
+      sbb::ep_publish_kernel<<<blocks, sbb::kEpThreads, 0, s>>>(
+          static_cast<const uint4*>(hidden), vec, topk_ids, topk_weights, routes,
+          reinterpret_cast<uint4*>(ex + p->lay.hidden), reinterpret_cast<int32_t*>(ex + p->lay.ids),
+          reinterpret_cast<float*>(ex + p->lay.weights), p->dev, p->tab, p->world,
+          static_cast<int64_t>(M));
+      const cudaError_t e = cudaGetLastError();
+      if (e != cudaSuccess) return ep_fail(SBB200_ECUDA, std::string("ep publish: ") + cudaGetErrorString(e));
+    }
+    // 2. gather the local routes of every source
+    const int64_t vt = static_cast<int64_t>(p->world) * p->max_tokens;
+    {
+      const int64_t total = vt * p->top_k;
+      const int blocks = static_cast<int>(std::min<int64_t>(148 * 2, (total + sbb::kEpThreads - 1) / sbb::kEpThreads));
+      sbb::ep_gather_kernel<<<blocks, sbb::kEpThreads, 0, s>>>(
+          reinterpret_cast<const unsigned long long*>(ex + p->lay.ready), p->dev, p->tab, p->world,
+          static_cast<int64_t>(p->max_tokens), static_cast<int>(p->top_k), p->rank, p->local_ids,
+          p->local_w);
+      const cudaError_t e = cudaGetLastError();
+      if (e != cudaSuccess) return ep_fail(SBB200_ECUDA, std::string("ep gather: ") + cudaGetErrorString(e));
+    }
+    // 3. the shard's MoE on the virtual tokens: rows pulled from their
+    // sources, partials pushed back, done flags raised
+    {
+      sbb::MoeArgs a{};
+      a.hidden = nullptr;
+      a.act_dt = p->act_dt;
+      a.ids = p->local_ids;
+      a.weights = p->local_w;
+      a.multiply_router_weight = multiply_router_weight;
+      a.w13 = static_cast<const uint8_t*>(w13);
+      a.s13 = static_cast<const uint8_t*>(w13_scales);
+      a.g13 = w13_global_scales;
+      a.w2 = static_cast<const uint8_t*>(w2);
+      a.s2 = static_cast<const uint8_t*>(w2_scales);
+      a.g2 = w2_global_scales;
+      a.out = nullptr;
+      a.out_dt = SBB200_F32;
+      a.M = vt;
+      a.E = static_cast<int>(p->e_count);
+      a.top_k = static_cast<int>(p->top_k);
+      a.K = static_cast<int>(p->K);
+      a.I = static_cast<int>(p->I);
+      a.stage_events = nullptr;
+      // device addresses of the tables inside p->tab (never dereferenced here)
+      char* tab = reinterpret_cast<char*>(p->tab);
+      char* dev = reinterpret_cast<char*>(p->dev);
+      a.hidden_rows = sbb::SplitRows{
+          reinterpret_cast<const void* const*>(tab + offsetof(sbb::EpTables, peer_hidden)),
+          static_cast<int64_t>(p->max_tokens)};
+      a.out_rows = sbb::SplitRows{
+          reinterpret_cast<const void* const*>(tab + offsetof(sbb::EpTables, partial_at_peer)),
+          static_cast<int64_t>(p->max_tokens)};
+      a.done = sbb::PeerSignal{
+          reinterpret_cast<unsigned int*>(dev + offsetof(sbb::EpDev, combine_ctr)),
+          reinterpret_cast<unsigned long long* const*>(tab + offsetof(sbb::EpTables, done_at_peer)),
+          reinterpret_cast<const unsigned long long*>(dev + offsetof(sbb::EpDev, epoch)), p->world};
+      std::string why;
+      const cudaError_t e = sbb::run_moe(a, p->plan, p->workspace, s, &why);
+      if (e != cudaSuccess) return ep_fail(SBB200_ECUDA, "ep expert step (" + why + "): " + cudaGetErrorString(e));
+    }
+    // 4. sum the partials of this rank's tokens
+    if (M > 0) {
+      const dim3 grid(static_cast<unsigned>(M), static_cast<unsigned>((K + 4 * sbb::kEpThreads - 1) / (4 * sbb::kEpThreads)));
+      sbb::ep_final_kernel<<<grid, sbb::kEpThreads, 0, s>>>(
+          reinterpret_cast<const unsigned long long*>(ex + p->lay.done), p->dev, p->tab, p->world,
+          topk_ids, static_cast<int>(p->top_k), static_cast<int>(p->E),
+          reinterpret_cast<const float*>(ex + p->lay.partial), static_cast<int64_t>(p->max_tokens),
+          static_cast<int>(K), out, out_dt);
+    } else {
+      // no tokens here: still consume the done flags so the exchange stays in step
+      sbb::ep_final_kernel<<<dim3(1, 1), sbb::kEpThreads, 0, s>>>(
+          reinterpret_cast<const unsigned long long*>(ex + p->lay.done), p->dev, p->tab, p->world,
+          nullptr, 0, static_cast<int>(p->E), reinterpret_cast<const float*>(ex + p->lay.partial),
+          static_cast<int64_t>(p->max_tokens), 0, nullptr, out_dt);
+    }
+    const cudaError_t e = cudaGetLastError();
+    if (e != cudaSuccess) return ep_fail(SBB200_ECUDA, std::string("ep final: ") + cudaGetErrorString(e));
+    return SBB200_OK;
+  } catch (...) {
+    return ep_fail(SBB200_ECUDA, "ep forward: host exception");
+  }
+}
+
+int sbb200_ep_device_errors(sbb200_ep_t* p, void* stream, uint32_t* errors) {
+  if (!p || !errors) return ep_fail(SBB200_EINVAL, "ep errors: null argument");
+  DeviceGuard g(p->device);
+  auto s = static_cast<cudaStream_t>(stream);
+  uint32_t v = 0;
+  char* errs = reinterpret_cast<char*>(p->dev) + offsetof(sbb::EpDev, errors);
+  cudaError_t e = cudaMemcpyAsync(&v, errs, 4, cudaMemcpyDeviceToHost, s);
+  if (e == cudaSuccess) e = cudaMemsetAsync(errs, 0, 4, s);
+  if (e == cudaSuccess) e = cudaStreamSynchronize(s);
+  if (e != cudaSuccess) return ep_fail(SBB200_ECUDA, std::string("ep errors: ") + cudaGetErrorString(e));
+  *errors = v;
+  return SBB200_OK;
+}
+
+void sbb200_ep_destroy(sbb200_ep_t* p) {
+  if (!p) return;
+  ep_free(p);
+  delete p;
+}
+
+}  // extern "C"

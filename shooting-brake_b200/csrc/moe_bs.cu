@@ -480,14 +480,16 @@ __device__ __forceinline__ float2 e2m1x2_to_float2(uint32_t byte) {
 }
 
 
-// Splits rows into NT NVFP4 terms. Grid (rows, ceil(K / kSplitChunk)): each
-// CTA takes kSplitChunk elements of one source row, one 16-element block per
-// thread, so block maxima need no shuffles and a thread's packed block is one
-// 8-byte store. Every CTA of a row reduces the whole row for the row maximum
-// (at most 64 KB, read again from L2). Without slot_of, row i is written to
-// output rows i*NT + t; with slot_of (token mode) source row i is token i and
-// its terms go to every route slot the token feeds (slot_of[i*top_k + k], -1
-// skipped), so a token is split once however many experts it visits.
+// Splits rows into NT NVFP4 terms. Grid (rows, chunks): each CTA takes
+// 16 * blockDim elements of one source row, one 16-element block per thread,
+// so block maxima need no shuffles and a thread's packed block is one 8-byte
+// store. With several chunks per row every CTA reduces the whole row for the
+// row maximum (re-read from L2); with one chunk (rows read from another GPU,
+// blockDim = K / 16) each element is read once. Without slot_of, row i is
+// written to output rows i*NT + t; with slot_of (token mode) source row i is
+// token i and its terms go to every route slot the token feeds
+// (slot_of[i*top_k + k], -1 skipped), so a token is split once however many
+// experts it visits, and a token with no slot is not read at all.
 // Outputs: packed e2m1 [row*NT + t, K/2], e4m3 scales [row*NT + t, K/16] and
 // the dequant global g [row*NT + t].
 constexpr int kSplitThreads = 64;
@@ -516,35 +518,62 @@ __device__ __forceinline__ void load8(const void* src, int src_dt, int64_t at, f
   }
 }
 
-__global__ void __launch_bounds__(kSplitThreads) split_nvfp4_kernel(
-    const void* __restrict__ src, int src_dt, const int32_t* __restrict__ slot_of, int top_k,
-    const int32_t* __restrict__ n_rows_dev, int K, int NT, uint8_t* __restrict__ q,
+__global__ void __launch_bounds__(1024) split_nvfp4_kernel(
+    const void* __restrict__ src, int src_dt, SplitRows rows, const int32_t* __restrict__ slot_of,
+    int top_k, const int32_t* __restrict__ n_rows_dev, int K, int NT, uint8_t* __restrict__ q,
     uint8_t* __restrict__ sf, float* __restrict__ gout) {
-  __shared__ float s_max[kSplitThreads / 32];
+  __shared__ float s_max[32];
   __shared__ int32_t s_dst[kMaxTopK];
+  __shared__ int s_any;
   const int64_t row = blockIdx.x;
   if (n_rows_dev && row >= static_cast<int64_t>(*n_rows_dev)) return;
   const int tid = threadIdx.x;
+  const int nwarps = blockDim.x >> 5;
   int ndst = 1;
   if (slot_of) {
-    for (int i = tid; i < top_k; i += kSplitThreads) s_dst[i] = slot_of[row * top_k + i];
+    if (tid == 0) s_any = 0;
+    __syncthreads();
+    for (int i = tid; i < top_k; i += blockDim.x) {
+      s_dst[i] = slot_of[row * top_k + i];
+      if (s_dst[i] >= 0) s_any = 1;
+    }
+    __syncthreads();
+    if (!s_any) return;  // the whole CTA leaves together
     ndst = top_k;
   }
-  // row maximum
+  const void* rsrc = src;
+  int64_t rbase = row * K;
+  if (rows.base) {
+    rsrc = rows.base[row / rows.rows_per_src];
+    rbase = (row % rows.rows_per_src) * K;
+  }
+  const int blk = blockIdx.y * blockDim.x + tid;  // this thread's 16-element block
+  const bool active = blk * 16 < K;
+  float v[16];
   float amax = 0.0f;
-  for (int k = tid * 8; k < K; k += kSplitThreads * 8) {
-    float v8[8];
-    load8(src, src_dt, row * K + k, v8);
+  if (active) {
+    load8(rsrc, src_dt, rbase + blk * 16, v);
+    load8(rsrc, src_dt, rbase + blk * 16 + 8, v + 8);
+  }
+  if (gridDim.y == 1) {
+    if (active) {
 #pragma unroll
-    for (int i = 0; i < 8; ++i) amax = fmaxf(amax, fabsf(v8[i]));
+      for (int i = 0; i < 16; ++i) amax = fmaxf(amax, fabsf(v[i]));
+    }
+  } else {
+    for (int k = tid * 8; k < K; k += blockDim.x * 8) {
+      float v8[8];
+      load8(rsrc, src_dt, rbase + k, v8);
+#pragma unroll
+      for (int i = 0; i < 8; ++i) amax = fmaxf(amax, fabsf(v8[i]));
+    }
   }
 #pragma unroll
   for (int d = 16; d > 0; d >>= 1) amax = fmaxf(amax, __shfl_xor_sync(0xffffffffu, amax, d));
   if ((tid & 31) == 0) s_max[tid >> 5] = amax;
   __syncthreads();
   amax = s_max[0];
-#pragma unroll
-  for (int w = 1; w < kSplitThreads / 32; ++w) amax = fmaxf(amax, s_max[w]);
+  for (int w = 1; w < nwarps; ++w) amax = fmaxf(amax, s_max[w]);
   const float G0 = amax > 0.0f ? __fdiv_rn(2688.0f, amax) : 1.0f;
   const float g0 = __fdiv_rn(1.0f, G0);
   if (blockIdx.y == 0 && tid < ndst) {
@@ -552,11 +581,7 @@ __global__ void __launch_bounds__(kSplitThreads) split_nvfp4_kernel(
     if (dst >= 0)
       for (int t = 0; t < NT; ++t) gout[dst * NT + t] = ldexpf(g0, -2 * t);
   }
-  const int blk = blockIdx.y * kSplitThreads + tid;  // this thread's 16-element block
-  if (blk * 16 >= K) return;
-  float v[16];
-  load8(src, src_dt, row * K + blk * 16, v);
-  load8(src, src_dt, row * K + blk * 16 + 8, v + 8);
+  if (!active) return;
   float G = G0, g = g0;
   for (int t = 0; t < NT; ++t) {
     float bmax = 0.0f;
@@ -658,13 +683,17 @@ int sm_count() {
 // slot_of != nullptr: token mode (n_rows source tokens, terms scattered to
 // their route slots); otherwise n_rows rows (device count n_rows_dev when
 // given, n_rows an upper bound).
-cudaError_t launch_split(const void* src, int src_dt, const int32_t* slot_of, int top_k,
-                         const int32_t* n_rows_dev, int64_t n_rows, int K, uint8_t* q,
-                         uint8_t* sf, float* g, cudaStream_t stream) {
+cudaError_t launch_split(const void* src, int src_dt, const SplitRows* rows,
+                         const int32_t* slot_of, int top_k, const int32_t* n_rows_dev,
+                         int64_t n_rows, int K, uint8_t* q, uint8_t* sf, float* g,
+                         cudaStream_t stream) {
   if (n_rows <= 0) return cudaSuccess;
-  const dim3 grid(static_cast<unsigned>(n_rows), (K + kSplitChunk - 1) / kSplitChunk);
-  split_nvfp4_kernel<<<grid, kSplitThreads, 0, stream>>>(src, src_dt, slot_of, top_k, n_rows_dev,
-                                                         K, kSplitTerms, q, sf, g);
+  const SplitRows r = rows ? *rows : SplitRows{nullptr, 1};
+  // rows on another GPU: one CTA per row, so each element crosses NVLink once
+  const int threads = r.base ? K / 16 : kSplitThreads;
+  const dim3 grid(static_cast<unsigned>(n_rows), r.base ? 1 : (K + kSplitChunk - 1) / kSplitChunk);
+  split_nvfp4_kernel<<<grid, threads, 0, stream>>>(src, src_dt, r, slot_of, top_k, n_rows_dev, K,
+                                                   kSplitTerms, q, sf, g);
   return cudaGetLastError();
 }
 
@@ -735,8 +764,8 @@ cudaError_t launch_moe_bs(const BsLaunch& a, cudaStream_t stream, const char** s
 
   // 1. split each token once; its terms go to all of its route slots
   *step = "activation split";
-  cudaError_t err = launch_split(a.hidden, a.act_dt, a.slot_of, a.top_k, nullptr, a.M, a.K,
-                                 a.xq, a.xsf, a.xg, stream);
+  cudaError_t err = launch_split(a.hidden, a.act_dt, &a.hidden_rows, a.slot_of, a.top_k, nullptr,
+                                 a.M, a.K, a.xq, a.xsf, a.xg, stream);
   if (err != cudaSuccess) return err;
   if (a.stage_mark) a.stage_mark(a.stage_ctx, 1);
   // 2. gate/up + SwiGLU
@@ -746,7 +775,8 @@ cudaError_t launch_moe_bs(const BsLaunch& a, cudaStream_t stream, const char** s
   if (a.stage_mark) a.stage_mark(a.stage_ctx, 2);
   // 3. split the SwiGLU rows, down projection
   *step = "h split";
-  err = launch_split(a.h, kF32, nullptr, 1, a.offsets + a.E, R, a.I, a.hq, a.hsf, a.hg, stream);
+  err = launch_split(a.h, kF32, nullptr, nullptr, 1, a.offsets + a.E, R, a.I, a.hq, a.hsf, a.hg,
+                     stream);
   if (err != cudaSuccess) return err;
   *step = "down";
   err = launch_bnr<kDown>(bnr2, m2a, m2sa, m2b, m2sb, p2, grid, stream);

@@ -78,6 +78,7 @@ cudaError_t run_moe(const MoeArgs& a, const WorkspacePlan& plan, void* workspace
     BsLaunch t{};
     t.hidden = a.hidden;
     t.act_dt = a.act_dt;
+    t.hidden_rows = a.hidden_rows;
     t.counts = counts;
     t.offsets = offsets;
     t.sorted = sorted;
@@ -118,6 +119,10 @@ cudaError_t run_moe(const MoeArgs& a, const WorkspacePlan& plan, void* workspace
     err = launch_moe_bs(t, stream, &step);
     if (err != cudaSuccess) { *why = step; return err; }
   } else {
+    if (a.hidden_rows.base) {
+      *why = "expert-parallel rows need K and I multiples of 256";
+      return cudaErrorInvalidValue;
+    }
     if ((err = mark(1)) != cudaSuccess) { *why = "stage event"; return err; }
     err = launch_gateup_simt(a.hidden, a.act_dt, a.top_k, a.w13, a.s13, a.g13, counts, offsets,
                              sorted, h, a.E, a.K, a.I, stream);
@@ -128,7 +133,8 @@ cudaError_t run_moe(const MoeArgs& a, const WorkspacePlan& plan, void* workspace
     if ((err = mark(3)) != cudaSuccess) { *why = "stage event"; return err; }
   }
   err = launch_combine(y, slot_of, a.weights, a.multiply_router_weight, a.out, a.out_dt, a.M,
-                       a.top_k, a.K, stream);
+                       a.top_k, a.K, stream, a.out_rows.base ? &a.out_rows : nullptr,
+                       a.done.counter ? &a.done : nullptr);
   if (err != cudaSuccess) { *why = "combine"; return err; }
   if ((err = mark(4)) != cudaSuccess) { *why = "stage event"; return err; }
   return cudaSuccess;

@@ -7,6 +7,8 @@
 
 #include <string>
 
+#include "kernels.h"
+
 namespace sbb {
 
 constexpr size_t kStatusOffset = 0;  // uint32 status words at the workspace start
@@ -44,6 +46,11 @@ struct MoeArgs {
   int64_t M;
   int E, top_k, K, I;
   void* const* stage_events;  // optional cudaEvent_t[SBB200_STAGE_EVENTS]
+  // expert parallel (block-scaled path only): token rows read from the
+  // source GPUs, fp32 partial rows stored back to them, then a signal
+  SplitRows hidden_rows{nullptr, 1};
+  SplitRows out_rows{nullptr, 1};
+  PeerSignal done{nullptr, nullptr, nullptr, 0};
 };
 
 int validate_shape(size_t M, size_t E, size_t top_k, size_t K, size_t I, int act_dt, int out_dt,

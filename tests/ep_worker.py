@@ -1,0 +1,90 @@
+"""Child-process bodies for the expert-parallel tests (started with the
+``spawn`` method; one process per rank, 127.0.0.1 rendezvous, gloo process
+group with a short timeout). Not collected by pytest."""
+
+from __future__ import annotations
+
+import datetime
+import os
+import sys
+import traceback
+from pathlib import Path
+
+ROOT = Path(__file__).resolve().parent.parent
+
+
+def _init(rank: int, world: int, port: int):
+    sys.path.insert(0, str(ROOT))
+    sys.path.insert(0, str(ROOT / "tests"))
+    os.environ["MASTER_ADDR"] = "127.0.0.1"
+    os.environ["MASTER_PORT"] = str(port)
+    import torch.distributed as dist
+    dist.init_process_group("gloo", rank=rank, world_size=world,
+                            timeout=datetime.timedelta(seconds=60))
+    return dist
+
+
+def handles_worker(rank: int, world: int, port: int, q):
+    """exchange_handles over gloo: every rank gets all handles in rank order
+    (host logic only; the CUDA library is not loaded)."""
+    try:
+        dist = _init(rank, world, port)
+        import importlib
+        import __graft_entry__ as g
+        ep_mod = importlib.import_module(g.load_package().__name__ + ".ep")
+        got = ep_mod.exchange_handles(bytes([rank + 1]) * ep_mod.HANDLE_BYTES)
+        q.put((rank, got))
+        dist.destroy_process_group()
+    except Exception:
+        q.put((rank, traceback.format_exc()))
+
+
+def ep_forward_worker(rank: int, world: int, port: int, shape: tuple, steps: list, q):
+    """Expert-parallel forward on GPU `rank` vs the oracle, several steps."""
+    try:
+        dist = _init(rank, world, port)
+        import numpy as np
+        import torch
+        import __graft_entry__ as g
+        from oracle import nvfp4 as O
+        from conftest import cosine, rel_err
+
+        torch.cuda.set_device(rank)
+        sbb = g.load_package()
+        import importlib
+        ep_mod = importlib.import_module(sbb.__name__ + ".ep")
+        E, K, I, top_k, max_tokens = shape
+        L = O.make_layer(E, K, I, seed=500)
+        ep = ep_mod.ExpertParallel(rank=rank, world=world, device=rank, max_tokens=max_tokens,
+                                   top_k=top_k, E=E, K=K, I=I)
+        dev = torch.device("cuda", rank)
+        b, c = ep.expert_begin, ep.expert_count
+        ws = [torch.from_numpy(np.ascontiguousarray(x[b:b + c])).to(dev)
+              for x in (L.w13, L.s13, L.g13, L.w2, L.s2, L.g2)]
+        results = []
+        for i, counts in enumerate(steps):
+            T = counts[rank]
+            seed = 1000 * i + 10 * rank
+            hidden = O.make_hidden(max(T, 1), K, seed=seed)[:T]
+            ids, w = O.route_logits(max(T, 1), E, top_k, seed=seed + 1)
+            ids, w = ids[:T], w[:T]
+            if T > 2:
+                ids[1, 0] = -1          # a dropped route
+                ids[2, :] = ids[2, 0]   # one expert repeated
+            h = torch.from_numpy(np.ascontiguousarray(hidden)).to(dev).view(torch.bfloat16)
+            out = ep.forward(h, torch.from_numpy(ids).to(dev), torch.from_numpy(w).to(dev), *ws,
+                             out_dtype=torch.float32)
+            torch.cuda.synchronize()
+            got = out.cpu().numpy()
+            if T:
+                want = O.moe_forward(hidden, ids, w, L)
+                results.append((T, rel_err(got, want), cosine(got, want)))
+            else:
+                results.append((0, 0.0, 1.0))
+        errs = ep.device_errors()
+        ep.close()
+        dist.barrier()
+        dist.destroy_process_group()
+        q.put((rank, {"results": results, "errors": errs}))
+    except Exception:
+        q.put((rank, traceback.format_exc()))
