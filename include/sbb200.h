@@ -256,6 +256,21 @@ int sbb200_ep_forward(sbb200_ep_t* ep, void* stream, const void* hidden, const i
                       const void* w2_scales, const float* w2_global_scales, void* out,
                       int out_dt, int multiply_router_weight);
 
+/* sbb200_ep_forward that also records SBB200_EP_STAGE_EVENTS cudaEvent_t on
+ * `stream`: [0] start, [1] after publish, [2] after the gather (including the
+ * wait for every rank's publish), [3] after the route plan and the pulled
+ * activation split, [4] after gate/up, [5] after down, [6] after the combine
+ * push, [7] after the final sum (including the wait for every rank). No
+ * counterpart in the reference; it times the exchange against the GEMMs. */
+#define SBB200_EP_STAGE_EVENTS 8
+int sbb200_ep_forward_staged(sbb200_ep_t* ep, void* stream, const void* hidden,
+                             const int32_t* topk_ids, const float* topk_weights, size_t M,
+                             const void* w13, const void* w13_scales,
+                             const float* w13_global_scales, const void* w2,
+                             const void* w2_scales, const float* w2_global_scales, void* out,
+                             int out_dt, int multiply_router_weight, void* const* stage_events,
+                             size_t n_stage_events);
+
 /* Error bits raised on the device since the last read (bit 0: a wait for
  * another rank passed its 2 s deadline); reads, clears, synchronises. */
 int sbb200_ep_device_errors(sbb200_ep_t* ep, void* stream, uint32_t* errors);

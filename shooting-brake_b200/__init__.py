@@ -104,6 +104,8 @@ def lib() -> ctypes.CDLL:
         L.sbb200_ep_connect.argtypes = [P, P, S]
         L.sbb200_ep_forward.restype = I
         L.sbb200_ep_forward.argtypes = [P, P, P, P, P, S, P, P, P, P, P, P, P, I, I]
+        L.sbb200_ep_forward_staged.restype = I
+        L.sbb200_ep_forward_staged.argtypes = [P, P, P, P, P, S, P, P, P, P, P, P, P, I, I, P, S]
         L.sbb200_ep_device_errors.restype = I
         L.sbb200_ep_device_errors.argtypes = [P, P, P]
         L.sbb200_ep_destroy.restype = None

@@ -10,6 +10,7 @@
 // valid route get zeros.
 #include "common.cuh"
 #include "kernels.h"
+#include "launch.cuh"
 
 namespace sbb {
 
@@ -47,6 +48,8 @@ __global__ void __launch_bounds__(kThreads) combine_kernel(
   __shared__ int32_t s_slot[kMaxTopK];
   __shared__ float s_w[kMaxTopK];
   __shared__ int s_any;
+  pdl_wait();
+  pdl_trigger();
   if (threadIdx.x == 0) s_any = 0;
   __syncthreads();
   if (threadIdx.x < top_k) {
@@ -93,9 +96,8 @@ cudaError_t launch_combine(const float* y, const int32_t* slot_of, const float* 
   dim3 grid((unsigned)M, (unsigned)((K + per_cta - 1) / per_cta));
   const SplitRows d = dst ? *dst : SplitRows{nullptr, 1};
   const PeerSignal sg = signal ? *signal : PeerSignal{nullptr, nullptr, nullptr, 0};
-  combine_kernel<<<grid, kThreads, 0, stream>>>(y, slot_of, weights, multiply_router_weight, out,
-                                                 out_dt, top_k, K, d, sg);
-  return cudaGetLastError();
+  return launch_kernel(true, combine_kernel, grid, dim3(kThreads), 0, stream, y, slot_of, weights,
+                       multiply_router_weight, out, out_dt, top_k, K, d, sg);
 }
 
 }  // namespace sbb

@@ -49,6 +49,7 @@
 
 #include "common.cuh"
 #include "kernels.h"
+#include "launch.cuh"
 #include "moe_driver.h"
 #include "sbb200.h"
 
@@ -135,6 +136,8 @@ __global__ void __launch_bounds__(kEpThreads) ep_publish_kernel(
     const float* __restrict__ weights, int64_t routes, uint4* __restrict__ ex_hidden,
     int32_t* __restrict__ ex_ids, float* __restrict__ ex_weights, EpDev* dev,
     const EpTables* __restrict__ tab, int world, int64_t M) {
+  pdl_wait();
+  pdl_trigger();
   const int64_t stride = static_cast<int64_t>(gridDim.x) * blockDim.x;
   for (int64_t i = blockIdx.x * blockDim.x + threadIdx.x; i < hidden_vec; i += stride)
     ex_hidden[i] = hidden[i];
@@ -146,9 +149,11 @@ __global__ void __launch_bounds__(kEpThreads) ep_publish_kernel(
   // last one stores the new one (the store happens after all increments)
   const unsigned long long next = dev->epoch + 1ull;
   __shared__ unsigned int s_last;
-  __threadfence_system();
   __syncthreads();
-  if (threadIdx.x == 0) s_last = atomicAdd(&dev->publish_ctr, 1u) == gridDim.x - 1u;
+  if (threadIdx.x == 0) {
+    __threadfence_system();  // cumulative over the CTA's copies (barrier above)
+    s_last = atomicAdd(&dev->publish_ctr, 1u) == gridDim.x - 1u;
+  }
   __syncthreads();
   if (s_last) {
     __threadfence_system();
@@ -167,6 +172,8 @@ __global__ void __launch_bounds__(kEpThreads) ep_gather_kernel(
     int world, int64_t max_tokens, int top_k, int rank, int32_t* __restrict__ local_ids,
     float* __restrict__ local_w) {
   __shared__ int64_t s_count[kMaxWorld];
+  pdl_wait();
+  pdl_trigger();
   const unsigned long long epoch = dev->epoch;
   const uint64_t deadline = globaltimer_ns() + kWaitNs;
   for (int s = threadIdx.x; s < world; s += blockDim.x) {
@@ -206,6 +213,8 @@ __global__ void __launch_bounds__(kEpThreads) ep_final_kernel(
     int64_t max_tokens, int K, void* __restrict__ out, int out_dt) {
   __shared__ unsigned long long s_mask;
   const int64_t t = blockIdx.x;
+  pdl_wait();
+  pdl_trigger();
   const unsigned long long epoch = dev->epoch;
   if (threadIdx.x == 0) {
     unsigned long long mask = 0;
@@ -446,12 +455,16 @@ int sbb200_ep_connect(sbb200_ep_t* p, const void* handles, size_t size) {
   return SBB200_OK;
 }
 
-int sbb200_ep_forward(sbb200_ep_t* p, void* stream, const void* hidden, const int32_t* topk_ids,
-                      const float* topk_weights, size_t M, const void* w13, const void* w13_scales,
-                      const float* w13_global_scales, const void* w2, const void* w2_scales,
-                      const float* w2_global_scales, void* out, int out_dt,
-                      int multiply_router_weight) {
+int sbb200_ep_forward_staged(sbb200_ep_t* p, void* stream, const void* hidden,
+                             const int32_t* topk_ids, const float* topk_weights, size_t M,
+                             const void* w13, const void* w13_scales,
+                             const float* w13_global_scales, const void* w2,
+                             const void* w2_scales, const float* w2_global_scales, void* out,
+                             int out_dt, int multiply_router_weight, void* const* stage_events,
+                             size_t n_stage_events) {
   try {
+    if (stage_events && n_stage_events < SBB200_EP_STAGE_EVENTS)
+      return ep_fail(SBB200_EINVAL, "ep forward: need SBB200_EP_STAGE_EVENTS stage events");
     if (!p) return ep_fail(SBB200_EINVAL, "ep forward: null handle");
     if (!p->connected) return ep_fail(SBB200_EINVAL, "ep forward: connect the ranks first");
     if (M > p->max_tokens)
@@ -466,6 +479,11 @@ int sbb200_ep_forward(sbb200_ep_t* p, void* stream, const void* hidden, const in
     std::lock_guard<std::mutex> lk(p->mu);
     DeviceGuard g(p->device);
     auto s = static_cast<cudaStream_t>(stream);
+    auto mark = [&](int i) {
+      if (stage_events && stage_events[i])
+        cudaEventRecord(static_cast<cudaEvent_t>(stage_events[i]), s);
+    };
+    mark(0);
     const int64_t K = static_cast<int64_t>(p->K);
     const int64_t routes = static_cast<int64_t>(M * p->top_k);
     char* ex = p->ex;
@@ -482,18 +500,20 @@ int sbb200_ep_forward(sbb200_ep_t* p, void* stream, const void* hidden, const in
       const cudaError_t e = cudaGetLastError();
       if (e != cudaSuccess) return ep_fail(SBB200_ECUDA, std::string("ep publish: ") + cudaGetErrorString(e));
     }
+    mark(1);
     // 2. gather the local routes of every source
     const int64_t vt = static_cast<int64_t>(p->world) * p->max_tokens;
     {
       const int64_t total = vt * p->top_k;
       const int blocks = static_cast<int>(std::min<int64_t>(148 * 2, (total + sbb::kEpThreads - 1) / sbb::kEpThreads));
-      sbb::ep_gather_kernel<<<blocks, sbb::kEpThreads, 0, s>>>(
+      const cudaError_t e = sbb::launch_kernel(
+          true, sbb::ep_gather_kernel, dim3(blocks), dim3(sbb::kEpThreads), 0, s,
           reinterpret_cast<const unsigned long long*>(ex + p->lay.ready), p->dev, p->tab, p->world,
           static_cast<int64_t>(p->max_tokens), static_cast<int>(p->top_k), p->rank, p->local_ids,
           p->local_w);
-      const cudaError_t e = cudaGetLastError();
       if (e != cudaSuccess) return ep_fail(SBB200_ECUDA, std::string("ep gather: ") + cudaGetErrorString(e));
     }
+    mark(2);
     // 3. the shard's MoE on the virtual tokens: rows pulled from their
     // sources, partials pushed back, done flags raised
     {
@@ -516,7 +536,10 @@ int sbb200_ep_forward(sbb200_ep_t* p, void* stream, const void* hidden, const in
       a.top_k = static_cast<int>(p->top_k);
       a.K = static_cast<int>(p->K);
       a.I = static_cast<int>(p->I);
-      a.stage_events = nullptr;
+      // the expert step's own marks land in events [2..6]: [3] after the
+      // route plan and split, [4] after gate/up, [5] after down, [6] after
+      // the combine push
+      a.stage_events = stage_events ? stage_events + 2 : nullptr;
       // device addresses of the tables inside p->tab (never dereferenced here)
       char* tab = reinterpret_cast<char*>(p->tab);
       char* dev = reinterpret_cast<char*>(p->dev);
@@ -535,26 +558,33 @@ int sbb200_ep_forward(sbb200_ep_t* p, void* stream, const void* hidden, const in
       if (e != cudaSuccess) return ep_fail(SBB200_ECUDA, "ep expert step (" + why + "): " + cudaGetErrorString(e));
     }
     // 4. sum the partials of this rank's tokens
-    if (M > 0) {
-      const dim3 grid(static_cast<unsigned>(M), static_cast<unsigned>((K + 4 * sbb::kEpThreads - 1) / (4 * sbb::kEpThreads)));
-      sbb::ep_final_kernel<<<grid, sbb::kEpThreads, 0, s>>>(
-          reinterpret_cast<const unsigned long long*>(ex + p->lay.done), p->dev, p->tab, p->world,
-          topk_ids, static_cast<int>(p->top_k), static_cast<int>(p->E),
-          reinterpret_cast<const float*>(ex + p->lay.partial), static_cast<int64_t>(p->max_tokens),
-          static_cast<int>(K), out, out_dt);
-    } else {
-      // no tokens here: still consume the done flags so the exchange stays in step
-      sbb::ep_final_kernel<<<dim3(1, 1), sbb::kEpThreads, 0, s>>>(
-          reinterpret_cast<const unsigned long long*>(ex + p->lay.done), p->dev, p->tab, p->world,
-          nullptr, 0, static_cast<int>(p->E), reinterpret_cast<const float*>(ex + p->lay.partial),
-          static_cast<int64_t>(p->max_tokens), 0, nullptr, out_dt);
-    }
-    const cudaError_t e = cudaGetLastError();
+    // (with no tokens here the kernel still consumes the done flags, so the
+    // exchange stays in step)
+    const dim3 grid(M > 0 ? static_cast<unsigned>(M) : 1u,
+                    M > 0 ? static_cast<unsigned>((K + 4 * sbb::kEpThreads - 1) / (4 * sbb::kEpThreads)) : 1u);
+    const cudaError_t e = sbb::launch_kernel(
+        true, sbb::ep_final_kernel, grid, dim3(sbb::kEpThreads), 0, s,
+        reinterpret_cast<const unsigned long long*>(ex + p->lay.done), p->dev,
+        static_cast<const sbb::EpTables*>(p->tab), p->world, M > 0 ? topk_ids : nullptr,
+        M > 0 ? static_cast<int>(p->top_k) : 0, static_cast<int>(p->E),
+        reinterpret_cast<const float*>(ex + p->lay.partial), static_cast<int64_t>(p->max_tokens),
+        M > 0 ? static_cast<int>(K) : 0, out, out_dt);
     if (e != cudaSuccess) return ep_fail(SBB200_ECUDA, std::string("ep final: ") + cudaGetErrorString(e));
+    mark(7);
     return SBB200_OK;
   } catch (...) {
     return ep_fail(SBB200_ECUDA, "ep forward: host exception");
   }
+}
+
+int sbb200_ep_forward(sbb200_ep_t* p, void* stream, const void* hidden, const int32_t* topk_ids,
+                      const float* topk_weights, size_t M, const void* w13, const void* w13_scales,
+                      const float* w13_global_scales, const void* w2, const void* w2_scales,
+                      const float* w2_global_scales, void* out, int out_dt,
+                      int multiply_router_weight) {
+  return sbb200_ep_forward_staged(p, stream, hidden, topk_ids, topk_weights, M, w13, w13_scales,
+                                  w13_global_scales, w2, w2_scales, w2_global_scales, out, out_dt,
+                                  multiply_router_weight, nullptr, SBB200_EP_STAGE_EVENTS);
 }
 
 int sbb200_ep_device_errors(sbb200_ep_t* p, void* stream, uint32_t* errors) {

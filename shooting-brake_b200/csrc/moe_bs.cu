@@ -48,6 +48,7 @@
 
 #include "common.cuh"
 #include "kernels.h"
+#include "launch.cuh"
 #include "tc_ptx.cuh"
 
 namespace sbb {
@@ -210,6 +211,10 @@ __global__ void __launch_bounds__(kThreads, 1)
     tmem_alloc(&tmem_base_s, kTmemCols);
     tmem_relinquish();
   }
+  // everything above is local to the CTA; from here on the kernel reads what
+  // the previous kernel wrote
+  pdl_wait();
+  pdl_trigger();
   if (warp == 2) {
     int carry = 0;
     for (int e0 = 0; e0 < p.E; e0 += 32) {
@@ -526,6 +531,8 @@ __global__ void __launch_bounds__(1024) split_nvfp4_kernel(
   __shared__ int32_t s_dst[kMaxTopK];
   __shared__ int s_any;
   const int64_t row = blockIdx.x;
+  pdl_wait();
+  pdl_trigger();
   if (n_rows_dev && row >= static_cast<int64_t>(*n_rows_dev)) return;
   const int tid = threadIdx.x;
   const int nwarps = blockDim.x >> 5;
@@ -657,8 +664,7 @@ cudaError_t launch_gemm(const CUtensorMap& a, const CUtensorMap& sa, const CUten
     if (err != cudaSuccess) return err;
     attr[dev] = true;
   }
-  kern<<<grid, kThreads, C::kSmem, stream>>>(a, sa, b, sb, p);
-  return cudaGetLastError();
+  return launch_kernel(true, kern, dim3(grid), dim3(kThreads), C::kSmem, stream, a, sa, b, sb, p);
 }
 
 template <int MODE>
@@ -692,9 +698,8 @@ cudaError_t launch_split(const void* src, int src_dt, const SplitRows* rows,
   // rows on another GPU: one CTA per row, so each element crosses NVLink once
   const int threads = r.base ? K / 16 : kSplitThreads;
   const dim3 grid(static_cast<unsigned>(n_rows), r.base ? 1 : (K + kSplitChunk - 1) / kSplitChunk);
-  split_nvfp4_kernel<<<grid, threads, 0, stream>>>(src, src_dt, r, slot_of, top_k, n_rows_dev, K,
-                                                   kSplitTerms, q, sf, g);
-  return cudaGetLastError();
+  return launch_kernel(true, split_nvfp4_kernel, grid, dim3(threads), 0, stream, src, src_dt, r,
+                       slot_of, top_k, n_rows_dev, K, static_cast<int>(kSplitTerms), q, sf, g);
 }
 
 }  // namespace

@@ -17,6 +17,7 @@
 // chunk, pass 2 computes the histogram itself and pass 1 is skipped.
 #include "common.cuh"
 #include "kernels.h"
+#include "launch.cuh"
 
 namespace sbb {
 
@@ -31,6 +32,8 @@ __global__ void __launch_bounds__(kThreads) route_hist_kernel(
     const int32_t* __restrict__ ids, int64_t R, int E, int32_t* __restrict__ chunk_counts,
     uint32_t* __restrict__ status) {
   extern __shared__ int32_t s_hist[];
+  pdl_wait();
+  pdl_trigger();
   for (int e = threadIdx.x; e < E; e += kThreads) s_hist[e] = 0;
   __syncthreads();
   const int64_t begin = (int64_t)blockIdx.x * kRouteChunk;
@@ -67,6 +70,8 @@ __global__ void __launch_bounds__(kThreads) route_scatter_kernel(
   const int c = blockIdx.x;
   const int64_t begin = (int64_t)c * kRouteChunk;
   const int64_t end = min(begin + (int64_t)kRouteChunk, R);
+  pdl_wait();
+  pdl_trigger();
 
   // 1. per-expert totals and this chunk's base.
   if (nchunks == 1) {
@@ -181,14 +186,16 @@ cudaError_t launch_route_plan(const int32_t* ids, int64_t R, int E, int32_t* chu
     if (err != cudaSuccess) return err;
     attr_set[dev] = true;
   }
+  // the first launch of the plan waits for everything before it; the
+  // scatter overlaps the histogram's tail
   if (nchunks > 1) {
-    route_hist_kernel<<<nchunks, kThreads, sizeof(int32_t) * E, stream>>>(ids, R, E, chunk_counts,
-                                                                          status);
+    err = launch_kernel(false, route_hist_kernel, dim3(nchunks), dim3(kThreads),
+                        sizeof(int32_t) * E, stream, ids, R, E, chunk_counts, status);
+    if (err != cudaSuccess) return err;
   }
-  route_scatter_kernel<<<nchunks, kThreads, smem, stream>>>(ids, R, E, nchunks, chunk_counts,
-                                                            counts, offsets, sorted, slot_of,
-                                                            status);
-  return cudaGetLastError();
+  return launch_kernel(nchunks > 1, route_scatter_kernel, dim3(nchunks), dim3(kThreads), smem,
+                       stream, ids, R, E, nchunks, static_cast<const int32_t*>(chunk_counts),
+                       counts, offsets, sorted, slot_of, status);
 }
 
 }  // namespace sbb

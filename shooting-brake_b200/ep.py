@@ -25,6 +25,9 @@ import torch
 from . import DTYPE_CODE, Sbb200Error, _check, _check_cuda, _p, _stream, last_error, lib
 
 HANDLE_BYTES = 64
+STAGE_EVENTS = 8
+STAGE_NAMES = ("publish", "gather+wait", "route_plan+split(pull)", "gate_up", "h_split+down",
+               "combine(push)", "final+wait")
 
 
 def expert_shard(E: int, world: int, rank: int) -> tuple[int, int]:
@@ -37,6 +40,8 @@ def expert_shard(E: int, world: int, rank: int) -> tuple[int, int]:
 def exchange_handles(handle: bytes, group=None) -> bytes:
     """All ranks' handles concatenated in rank order (one all_gather_object)."""
     import torch.distributed as dist
+    if not dist.is_available() or not dist.is_initialized():
+        return bytes(handle)  # a single process: its own handle is the whole table
     world = dist.get_world_size(group)
     got = [None] * world
     dist.all_gather_object(got, bytes(handle), group=group)
@@ -74,9 +79,12 @@ class ExpertParallel:
                 w13: torch.Tensor, w13_scales: torch.Tensor, w13_global_scales: torch.Tensor,
                 w2: torch.Tensor, w2_scales: torch.Tensor, w2_global_scales: torch.Tensor,
                 out: torch.Tensor | None = None, out_dtype: torch.dtype = torch.bfloat16,
-                multiply_router_weight: bool = True) -> torch.Tensor:
+                multiply_router_weight: bool = True,
+                stage_events: list | None = None) -> torch.Tensor:
         """This rank's tokens through all E experts. The weights are this
-        rank's shard (``local_experts`` of the full layer)."""
+        rank's shard (``local_experts`` of the full layer). ``stage_events``
+        (STAGE_EVENTS recorded CUDA events, see STAGE_NAMES) times the step's
+        phases."""
         for name, t in (("hidden", hidden), ("topk ids", topk_ids), ("router weights", topk_weights),
                         ("w13", w13), ("w13 scales", w13_scales),
                         ("w13 global scales", w13_global_scales), ("w2", w2),
@@ -93,10 +101,15 @@ class ExpertParallel:
             raise ValueError(f"sbb200 ep: rank {self.rank} holds {self.expert_count} experts")
         if out is None:
             out = torch.empty((M, self.K), dtype=out_dtype, device=hidden.device)
-        _check(lib().sbb200_ep_forward(
-            self.h, _stream(hidden), _p(hidden), _p(topk_ids), _p(topk_weights), M, _p(w13),
-            _p(w13_scales), _p(w13_global_scales), _p(w2), _p(w2_scales), _p(w2_global_scales),
-            _p(out), DTYPE_CODE[out.dtype], int(bool(multiply_router_weight))))
+        args = (self.h, _stream(hidden), _p(hidden), _p(topk_ids), _p(topk_weights), M, _p(w13),
+                _p(w13_scales), _p(w13_global_scales), _p(w2), _p(w2_scales),
+                _p(w2_global_scales), _p(out), DTYPE_CODE[out.dtype],
+                int(bool(multiply_router_weight)))
+        if stage_events is None:
+            _check(lib().sbb200_ep_forward(*args))
+        else:
+            arr = (ctypes.c_void_p * STAGE_EVENTS)(*[ev.cuda_event for ev in stage_events])
+            _check(lib().sbb200_ep_forward_staged(*args, arr, STAGE_EVENTS))
         return out
 
     def device_errors(self) -> int:
