@@ -37,7 +37,8 @@
 //                of every 32-lane quarter. Writing them from registers keeps
 //                the tensor core's queue for MMAs only (a tcgen05.cp costs as
 //                much as an MMA there, and mixing the two serialises).
-//   warps 12-15  epilogue: fold terms, global scale, SwiGLU (gate/up) or the
+//   warps 8-15   epilogue, two teams of four warps on alternate 16-column
+//                chunks: fold terms, global scale, SwiGLU (gate/up) or the
 //                fp32 route output (down).
 // Every wait is bounded (the kernel raises status[1], drains and returns).
 #include <cuda.h>
@@ -81,6 +82,10 @@ struct BsParams {
   int k_stages;         // reduction / 256
   int rows_per_expert;  // 2I or K
   int out_ld;           // I or K
+  int stream_weights;   // 1: each weight tile is read by about one token tile
+                        // (decode): weights evict_first, term rows evict_last;
+                        // 0: tiles are shared by several token tiles in
+                        // flight (prefill): both evict_normal
 };
 
 template <int MODE, int BNR, int NT>
@@ -101,22 +106,29 @@ struct BsCfg {
   static constexpr int kOffB = kA;
   static constexpr int kOffSA = kA + kB;
   static constexpr int kOffSB = kOffSA + kSA;
-  // tensor memory: accumulators, then two scale buffers. Each operand gets 4
-  // columns per K group (the 4 row quarters of a 128-row block), so every
-  // scale address handed to the MMA is 4-column aligned; B fills the first
-  // ceil(rows / 32) of its 4.
+  // tensor memory: accumulators, then the scale buffers. Row n of an operand
+  // keeps the 4 scales of a 64-wide K group in column n / 32 of that group's
+  // columns, lane n % 32 of every 32-lane quarter: a 128-row A block takes 4
+  // columns per K group, B takes 4 (up to 128 rows) or 8 (up to 256), so
+  // every scale address handed to the MMA is 4-column aligned; B fills the
+  // first ceil(rows / 32) of its columns and zeroes the rest.
   static constexpr int kDCols = kNA * BNR;
-  static constexpr int kBQ = (BNR + 31) / 32;  // B row quarters in use
+  static constexpr int kBQ = (BNR + 31) / 32;        // B row quarters in use
+  static constexpr int kBC = BNR > 128 ? 8 : 4;      // B scale columns per K group
   // per buffer, a multiple of 16 so every tcgen05.st (x4/x8/x16) starts on a
   // column aligned to its width
-  static constexpr int kSfCols = (kNA + 1) * 16;
+  static constexpr int kSfCols = kNA * 16 + 4 * kBC;
   static constexpr int kDBufs = 2 * kDCols + 2 * kSfCols <= kTmemCols ? 2 : 1;
   static constexpr int kSfCol0 = kDBufs * kDCols;
+  // scale-factor ring: as many buffers as tensor memory leaves room for, up
+  // to 4, so the scale warps can run that many stages ahead of the MMAs
+  static constexpr int kSfFit = (kTmemCols - kSfCol0) / kSfCols;
+  static constexpr int kSfBufs = kSfFit > 4 ? 4 : kSfFit;
   static constexpr uint32_t kIdesc =
       (1u << 7) | (1u << 10) | (static_cast<uint32_t>(BNR >> 3) << 17) | ((kM >> 4) << 24);
   static_assert(kSmem <= 227 * 1024, "shared memory");
   static_assert(kSfCol0 % 16 == 0 && kSfCols % 16 == 0, "tensor-memory store alignment");
-  static_assert(kSfCol0 + 2 * kSfCols <= kTmemCols, "tensor memory");
+  static_assert(kSfBufs >= 2 && kSfCol0 + kSfBufs * kSfCols <= kTmemCols, "tensor memory");
   static_assert(BNR % 16 == 0 && BNR >= 16 && BNR <= 256 && BNR % NT == 0, "tile");
 };
 
@@ -173,8 +185,9 @@ __global__ void __launch_bounds__(kThreads, 1)
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) &
                                              ~static_cast<uintptr_t>(1023));
-  __shared__ __align__(8) uint64_t full[S], empty[S], sfready[2], dfull[NB], dempty[NB],
-      sffree[2], done_bar;
+  constexpr int NSF = C::kSfBufs;
+  __shared__ __align__(8) uint64_t full[S], empty[S], sfready[NSF], dfull[NB], dempty[NB],
+      sffree[NSF], done_bar;
   __shared__ uint32_t tmem_base_s;
   __shared__ int abort_s;
   __shared__ int prefix[kMaxExperts + 1];
@@ -190,13 +203,14 @@ __global__ void __launch_bounds__(kThreads, 1)
       mbar_init(&full[i], 1);
       mbar_init(&empty[i], 1 + 4);  // MMA commit + the four scale warps
     }
-    for (int i = 0; i < 2; ++i) mbar_init(&sfready[i], 4);
+    for (int i = 0; i < NSF; ++i) {
+      mbar_init(&sfready[i], 4);
+      mbar_init(&sffree[i], 1);
+    }
     for (int i = 0; i < NB; ++i) {
       mbar_init(&dfull[i], 1);
-      mbar_init(&dempty[i], 4);
+      mbar_init(&dempty[i], 8);  // both epilogue teams
     }
-    mbar_init(&sffree[0], 1);
-    mbar_init(&sffree[1], 1);
     mbar_init(&done_bar, 1);
     abort_s = 0;
     fence_mbar_init();
@@ -239,8 +253,8 @@ __global__ void __launch_bounds__(kThreads, 1)
   if (warp == 0) {
     // ---------------- TMA producer ----------------
     if (lane == 0) {
-      const uint64_t pol_w = policy_evict_first();
-      const uint64_t pol_x = policy_evict_last();
+      const uint64_t pol_w = p.stream_weights ? policy_evict_first() : policy_evict_normal();
+      const uint64_t pol_x = p.stream_weights ? policy_evict_last() : policy_evict_normal();
       int s = 0;
       uint32_t ph = 0;
       uint32_t issued_phase[S];
@@ -291,7 +305,7 @@ __global__ void __launch_bounds__(kThreads, 1)
     if (lane == 0) {
       int s = 0;
       uint32_t ph = 0;
-      uint32_t it = 0;  // stage sequence number (scale buffer = it & 1)
+      uint32_t it = 0;  // stage sequence number (scale buffer = it % NSF)
       uint32_t ui = 0;
       bool ok = true;
       for (int u = blockIdx.x; u < total_units && ok; u += gridDim.x, ++ui) {
@@ -300,10 +314,9 @@ __global__ void __launch_bounds__(kThreads, 1)
         tc_fence_after();
         const uint32_t d_tm = tmem + d * C::kDCols;
         for (int kk = 0; kk < p.k_stages; ++kk) {
-          const int sb = it & 1;
-          // the scale buffer's previous MMAs (two stages ago) are complete
+          const int sb = it % NSF;
           if (!mbar_wait(&full[s], ph, abort, deadline) ||
-              !mbar_wait(&sfready[sb], (it >> 1) & 1u, abort, deadline)) {
+              !mbar_wait(&sfready[sb], (it / NSF) & 1u, abort, deadline)) {
             ok = false;
             break;
           }
@@ -320,7 +333,7 @@ __global__ void __launch_bounds__(kThreads, 1)
             for (int a = 0; a < C::kNA; ++a) {
               const uint64_t ad = desc_sw128(a_sa + a * kM * kRowBytes + kg * 32);
               mma_bs(d_tm + a * BNR, ad, bd, C::kIdesc, sf0 + a * 16 + kg * 4,
-                     sf0 + C::kNA * 16 + kg * 4, acc);
+                     sf0 + C::kNA * 16 + kg * C::kBC, acc);
             }
           }
           mma_commit(&empty[s]);
@@ -345,14 +358,14 @@ __global__ void __launch_bounds__(kThreads, 1)
     const uint32_t lane_base = static_cast<uint32_t>(q * 32) << 16;
     int s = 0;
     uint32_t ph = 0;
-    uint32_t it = 0;  // stage sequence number (scale buffer = it & 1)
+    uint32_t it = 0;  // stage sequence number (scale buffer = it % NSF)
     bool ok = true;
     for (int u = blockIdx.x; u < total_units && ok; u += gridDim.x) {
       for (int kk = 0; kk < p.k_stages; ++kk) {
-        const int sb = it & 1;
-        // the buffer's previous MMAs (two stages ago) are complete
+        const int sb = it % NSF;
+        // the buffer's previous MMAs (NSF stages ago) are complete
         if (!warp_wait(&full[s], ph, abort, deadline) ||
-            !warp_wait(&sffree[sb], ((it >> 1) & 1u) ^ 1u, abort, deadline)) {
+            !warp_wait(&sffree[sb], ((it / NSF) & 1u) ^ 1u, abort, deadline)) {
           ok = false;
           break;
         }
@@ -373,19 +386,21 @@ __global__ void __launch_bounds__(kThreads, 1)
           }
           tmem_st16(sf0 + a * 16, ra);
         }
-        uint32_t rb[16];
+        constexpr int BC = C::kBC;
+        uint32_t rb[4 * BC];
 #pragma unroll
-        for (int r1 = 0; r1 < 4; ++r1) {
+        for (int r1 = 0; r1 < BC; ++r1) {
           const int n = r1 * 32 + lane;
           uint4 v = make_uint4(0, 0, 0, 0);
           if (r1 < C::kBQ && n < BNR)
             v = *reinterpret_cast<const uint4*>(st + C::kOffSB + n * kRowScales);
-          rb[0 * 4 + r1] = v.x;
-          rb[1 * 4 + r1] = v.y;
-          rb[2 * 4 + r1] = v.z;
-          rb[3 * 4 + r1] = v.w;
+          rb[0 * BC + r1] = v.x;
+          rb[1 * BC + r1] = v.y;
+          rb[2 * BC + r1] = v.z;
+          rb[3 * BC + r1] = v.w;
         }
-        tmem_st16(sf0 + C::kNA * 16, rb);
+#pragma unroll
+        for (int c = 0; c < 4 * BC; c += 16) tmem_st16(sf0 + C::kNA * 16 + c, rb + c);
         tmem_wait_st();
         tc_fence_before();
         __syncwarp();
@@ -400,9 +415,12 @@ __global__ void __launch_bounds__(kThreads, 1)
         }
       }
     }
-  } else if (warp >= 12) {
-    // ---------------- epilogue ----------------
+  } else if (warp >= 8) {
+    // ---------------- epilogue: two teams of four warps ----------------
+    // warps 8-11 and 12-15 each cover the four 32-lane quarters and take
+    // alternate 16-column chunks, so the accumulator drains twice as fast
     const int q = warp & 3;
+    const int team = (warp >> 2) & 1;
     const int r = q * 32 + lane;
     const uint32_t lane_base = static_cast<uint32_t>(q * 32) << 16;
     uint32_t ui = 0;
@@ -417,7 +435,7 @@ __global__ void __launch_bounds__(kThreads, 1)
       const float gs = p.gscale[e];
       const uint32_t taddr = tmem + lane_base + d * C::kDCols;
 #pragma unroll 1
-      for (int c0 = 0; c0 < BNR; c0 += 16) {
+      for (int c0 = team * 16; c0 < BNR; c0 += 32) {
         uint32_t t0[16], t1[16];
         tmem_ld16(taddr + c0, t0);
         tmem_ld16(taddr + BNR + c0, t1);
@@ -674,7 +692,9 @@ cudaError_t launch_bnr(int bnr, const CUtensorMap& a, const CUtensorMap& sa, con
     case 16: return launch_gemm<MODE, 16, kSplitTerms>(a, sa, b, sb, p, grid, stream);
     case 32: return launch_gemm<MODE, 32, kSplitTerms>(a, sa, b, sb, p, grid, stream);
     case 64: return launch_gemm<MODE, 64, kSplitTerms>(a, sa, b, sb, p, grid, stream);
+    case 96: return launch_gemm<MODE, 96, kSplitTerms>(a, sa, b, sb, p, grid, stream);
     case 128: return launch_gemm<MODE, 128, kSplitTerms>(a, sa, b, sb, p, grid, stream);
+    case 192: return launch_gemm<MODE, 192, kSplitTerms>(a, sa, b, sb, p, grid, stream);
     default: return cudaErrorInvalidValue;
   }
 }
@@ -709,13 +729,17 @@ bool bs_supported(int K, int I) {
 }
 
 // Term rows per MMA tile: enough for ~1.5x the mean routes per expert, up to
-// 128 (32 tokens). From N = 128 the block-scaled MMA runs at full rate; below
-// N = 64 it costs a fixed ~46 cycles per instruction.
+// 32 tokens (from N = 128 the block-scaled MMA runs at full rate; below N =
+// 64 it costs a fixed ~46 cycles per instruction). When experts see more than
+// a full tile (prefill), gate/up takes 48 tokens (N = 192: the weight tile is
+// reused by 50 % more tokens per byte staged; one accumulator buffer) and
+// down 24 (N = 96: two accumulator buffers fit, so a unit's epilogue overlaps
+// the next unit's MMAs, which matters with only I / 256 K stages per unit).
 int bs_tile_rows(int64_t routes, int E, int mode) {
   const double per = static_cast<double>(routes) / E * 1.5;
   int tok = 4;
-  (void)mode;
   while (tok < per && tok * kSplitTerms < 128) tok *= 2;
+  if (tok == 32 && per > 48.0) return (mode == kGateUp ? 48 : 24) * kSplitTerms;
   return tok * kSplitTerms;
 }
 
@@ -757,6 +781,8 @@ cudaError_t launch_moe_bs(const BsLaunch& a, cudaStream_t stream, const char** s
   p1.k_stages = a.K / kBK;
   p1.rows_per_expert = 2 * a.I;
   p1.out_ld = a.I;
+  // about one token tile per expert: every weight tile is read once
+  p1.stream_weights = R <= static_cast<int64_t>(a.E) * (bnr1 / NT);
   BsParams p2 = p1;
   p2.gscale = a.g2;
   p2.bg = a.hg;
@@ -766,6 +792,7 @@ cudaError_t launch_moe_bs(const BsLaunch& a, cudaStream_t stream, const char** s
   p2.k_stages = a.I / kBK;
   p2.rows_per_expert = a.K;
   p2.out_ld = a.K;
+  p2.stream_weights = R <= static_cast<int64_t>(a.E) * (bnr2 / NT);
 
   // 1. split each token once; its terms go to all of its route slots
   *step = "activation split";
