@@ -49,6 +49,10 @@ def parse():
     ap.add_argument("--cpu-seconds", type=float, default=12.0)
     ap.add_argument("--eager", action="store_true",
                     help="time eager calls instead of CUDA-graph replay")
+    ap.add_argument("--routing", default=None, choices=["uniform", "biased", "zipf"],
+                    help="routing (default: uniform for decode sizes, biased from 1024 tokens)")
+    ap.add_argument("--w4a4", action="store_true",
+                    help="quantise activations once (W4A4, dynamic per-row globals)")
     ap.add_argument("--replicas", action="store_true",
                     help="with N > 1, run N independent single-GPU replicas instead of "
                          "expert parallelism")
@@ -168,14 +172,31 @@ def layer_to_host(tensors):
     return O.Layer(E, D, I, w13, s13, g13, w2, s2, g2)
 
 
-def make_batch(device, T, seed):
-    """bf16 N(0,1) hidden [T, d]; uniform-random top-8 (distinct experts, the
-    top-8 of N(0,1) logits) with softmax-renormalised weights."""
+def make_batch(device, T, seed, routing="uniform"):
+    """bf16 N(0,1) hidden [T, d] and top-8 routing with softmax-renormalised
+    weights: "uniform" (top-8 of N(0,1) logits, config 1), "biased" (logits
+    N(0,1) plus a per-expert bias N(0,0.5): mildly uneven loads, config 2) or
+    "zipf" (8 distinct experts drawn with probability rank^-1.2 over a seeded
+    permutation, weights a softmax of N(0,1) logits: config 4)."""
     import torch
     gen = torch.Generator(device=device)
     gen.manual_seed(seed)
     hidden = torch.randn((T, D), generator=gen, device=device).to(torch.bfloat16)
     logits = torch.randn((T, E), generator=gen, device=device)
+    if routing == "biased":
+        bgen = torch.Generator(device=device)
+        bgen.manual_seed(7)  # one bias vector per layer stack
+        logits = logits + torch.randn(E, generator=bgen, device=device) * 0.5
+    if routing == "zipf":
+        pgen = torch.Generator(device=device)
+        pgen.manual_seed(11)
+        perm = torch.randperm(E, generator=pgen, device=device)
+        p = 1.0 / torch.arange(1, E + 1, device=device, dtype=torch.float64) ** 1.2
+        pick = torch.multinomial((p / p.sum()).float().expand(T, E), TOP_K, replacement=False,
+                                 generator=gen)
+        ids = perm[pick]
+        w = torch.softmax(torch.randn((T, TOP_K), generator=gen, device=device), dim=1)
+        return hidden, ids.to(torch.int32).contiguous(), w.float().contiguous()
     vals, ids = torch.topk(logits, TOP_K, dim=1)
     w = torch.softmax(vals, dim=1)
     return hidden, ids.to(torch.int32).contiguous(), w.float().contiguous()
@@ -513,15 +534,25 @@ def main():
         return
 
     N_LAYERS = args.layers
+    routing = args.routing or ("uniform" if T < 1024 else "biased")
     layers = make_layers(device, N_LAYERS, seed=1000 + rank)
-    batches = [make_batch(device, T, seed=2000 + 17 * i + rank) for i in range(N_LAYERS)]
+    batches = [make_batch(device, T, seed=2000 + 17 * i + rank, routing=routing)
+               for i in range(N_LAYERS)]
     out = torch.empty((T, D), dtype=torch.bfloat16, device=device)
     stream = torch.cuda.current_stream(device)
 
+    def forward(h, ids, w, lw, out=None, stage_events=None, out_dtype=torch.bfloat16):
+        if args.w4a4:
+            return sbb.nvfp4_moe_w4a4(h, ids, w, *lw, out_dtype=out_dtype, out=out,
+                                      stage_events=stage_events)
+        if out is None and stage_events is None:
+            return sbb.nvfp4_moe(h, ids, w, *lw, out_dtype=out_dtype)  # the public custom op
+        return sbb._nvfp4_moe_impl(h, ids, w, *lw, True, out_dtype, out=out,
+                                   stage_events=stage_events)
+
     def step(i):
-        lw = layers[i % N_LAYERS]
         h, ids, w = batches[i % N_LAYERS]
-        sbb._nvfp4_moe_impl(h, ids, w, *lw, True, torch.bfloat16, out=out)
+        forward(h, ids, w, layers[i % N_LAYERS], out=out)
 
     def timed(run_one, use_clocks):
         """Per-step ms of args.steps calls, bracketed by barrier + synchronize,
@@ -576,9 +607,8 @@ def main():
     evsets = [sbb.stage_events(stream) for _ in range(args.steps)]
     torch.cuda.synchronize()
     for i in range(args.steps):
-        lw = layers[i % N_LAYERS]
         h, ids, w = batches[i % N_LAYERS]
-        sbb._nvfp4_moe_impl(h, ids, w, *lw, True, torch.bfloat16, out=out, stage_events=evsets[i])
+        forward(h, ids, w, layers[i % N_LAYERS], out=out, stage_events=evsets[i])
     torch.cuda.synchronize()
     stage_ms = {name: statistics.mean(evs[j].elapsed_time(evs[j + 1]) for evs in evsets)
                 for j, name in enumerate(sbb.STAGE_NAMES)}
@@ -597,7 +627,7 @@ def main():
         dh.copy_(hh, non_blocking=True)
         di.copy_(hi, non_blocking=True)
         dw.copy_(hw, non_blocking=True)
-        o = sbb.nvfp4_moe(dh, di, dw, *layers[i % N_LAYERS], out_dtype=torch.bfloat16)
+        o = forward(dh, di, dw, layers[i % N_LAYERS])
         host_out.copy_(o, non_blocking=True)
 
     for i in range(max(args.warmup, 3)):
@@ -648,6 +678,26 @@ def main():
                 "launch_ms": stage_ms["gate_up"], "peak_source": f"{peak_src} hbm_gbs",
                 "stages_ms": stage_ms, "down_gbs": dn_gbs,
                 "whole_step_gbs": achieved_step, "whole_step_frac": achieved_step / hbm_peak}
+    if T >= 1024:
+        # prefill sizes: tensor-bound. Algorithmic FLOPs 2 * routes * 2I * d for
+        # gate/up and 2 * routes * d * I for down (W4A16 work counts as bf16;
+        # W4A4 against the FP4 rate, 4x the measured bf16 figure). The kernels
+        # are timed inside a seconds-long loop, so the sustained figure applies.
+        routes = T * TOP_K
+        fl_gu = 2.0 * routes * 2 * I * D
+        fl_all = fl_gu * 1.5
+        tf_peak = float(peaks.get("bf16_tflops_sustained", 1400.0)) * (4.0 if args.w4a4 else 1.0)
+        tf_src = ("measured bf16_tflops_sustained" if "bf16_tflops_sustained" in peaks
+                  else "fallback 1.4 PF sustained") + (" x4 (FP4 rate)" if args.w4a4 else "")
+        gu_tf = fl_gu / (stage_ms["gate_up"] * 1e-3) / 1e12
+        step_tf = fl_all / (ms * 1e-3) / 1e12
+        roofline = {"bound": "tensor", "achieved": gu_tf, "peak": tf_peak, "unit": "TFLOP/s",
+                    "frac": gu_tf / tf_peak, "traffic": None,
+                    "kernel": "moe_gemm_bs_kernel<gate/up> (grouped GEMM + SwiGLU)",
+                    "algorithmic_flops_per_launch": fl_gu, "launch_ms": stage_ms["gate_up"],
+                    "peak_source": tf_src, "stages_ms": stage_ms,
+                    "whole_step_tflops": step_tf, "whole_step_frac": step_tf / tf_peak,
+                    "bf16_burst_peak": float(peaks.get("bf16_tflops", 1590.0))}
 
     cpu_baseline = None
     if rank == 0 and world == 1 and not args.no_cpu_baseline:
@@ -669,9 +719,16 @@ def main():
         line = {
             "metric": METRIC, "value": world * T / (ms * 1e-3), "unit": "tokens/s",
             "n_gpus": world, "steps": args.steps, "warmup": args.warmup, "ms_per_step": ms,
-            "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "nvfp4 W4A16: e2m1 weights x 4-term e2m1 activation split, mxf4nvf4 MMA, fp32 accumulate",
+            "higher_is_better": True, "scaling": "weak", "vs_baseline": None,
+            "dtype": ("nvfp4 W4A4: e2m1 weights x e2m1 activations (dynamic per-row globals), "
+                      "mxf4nvf4 MMA, fp32 accumulate") if args.w4a4 else
+                     "nvfp4 W4A16: e2m1 weights x 4-term e2m1 activation split, mxf4nvf4 MMA, "
+                     "fp32 accumulate",
             "data": "synthetic",
-            "config": {"workload": f"config1-decode E={E} d={D} I={I} top{TOP_K} T={T}",
+            "config": {"workload": (f"config4-skewed-w4a4" if args.w4a4 else
+                                    "config1-decode" if T <= 64 else
+                                    "config2-prefill" if T >= 8192 else "layer")
+                                   + f" E={E} d={D} I={I} top{TOP_K} T={T} routing={routing}",
                        "global_batch": world * T, "tokens_per_gpu": T,
                        "parallelism": f"replicas x{world}" if world > 1 else "single",
                        "l2": f"inputs larger than L2: {N_LAYERS} rotating layers of "

@@ -123,6 +123,54 @@ int sbb200_nvfp4_moe_device_errors(void* stream, const void* workspace, uint32_t
  * routing step. All stream-ordered.
  * ------------------------------------------------------------------------- */
 
+/* W4A4 variant of sbb200_nvfp4_moe: the activations entering each GEMM
+ * (hidden rows, then the SwiGLU rows) are quantised once to NVFP4 (16-element
+ * e4m3 scales, vLLM ref_nvfp4_quant rounding) and multiplied with the NVFP4
+ * weights by the block-scaled tensor-core MMA, fp32 accumulate.
+ * Static scales (the 5090-style convention of the reference's hook, vLLM's
+ * a1_gscale / a2_gscale and g1_alphas / g2_alphas, src/phase4/src/
+ * shooting_brake_vllm/expert_bank.py:270-295): a13_gscale[E] and a2_gscale[E]
+ * are the activation quantisation globals of each expert's inputs (scale =
+ * G * blockmax / 6), and alpha13[E] / alpha2[E] multiply the MMA results
+ * (alpha = 1 / (G_activation * G_weight)); the *_global_scales are unused.
+ * Dynamic scales (all four NULL): each row is quantised under its own global
+ * 448 * 6 / max|row| and results are scaled by 1/G_row * *_global_scales.
+ * K and I multiples of 256; stage_events (NULL, or SBB200_STAGE_EVENTS
+ * events) as sbb200_nvfp4_moe_staged; other arguments as sbb200_nvfp4_moe. No
+ * counterpart op in the reference's extension (its W4A4 path is vLLM's). */
+int sbb200_nvfp4_moe_w4a4(void* stream, const void* hidden, const int32_t* topk_ids,
+                          const float* topk_weights, const void* w13, const void* w13_scales,
+                          const float* w13_global_scales, const void* w2, const void* w2_scales,
+                          const float* w2_global_scales, const float* a13_gscale,
+                          const float* a2_gscale, const float* alpha13, const float* alpha2,
+                          void* workspace, size_t workspace_bytes, void* out, int out_dt,
+                          size_t M, size_t E, size_t top_k, size_t K, size_t I, int act_dt,
+                          int multiply_router_weight, void* const* stage_events,
+                          size_t n_stage_events);
+
+/* Top-k routing (ops::moe_route_topk, src/QuixiCore-XPU/include/quixicore/
+ * xpu/ops.hpp:262-272; moe_route.sycl.cpp:16-50): for each of M tokens pick
+ * the top_k of E router logits (dt f32/f16/bf16) by k rounds of argmax with
+ * the lowest index winning ties, then softmax over the chosen k. topk_ids
+ * int32 [M, top_k] in selection order, topk_weights fp32 [M, top_k].
+ * E <= 512, top_k <= min(E, 64). Stream-ordered. */
+int sbb200_router_topk(void* stream, const void* router_logits, int dt, size_t M, size_t E,
+                       size_t top_k, int32_t* topk_ids, float* topk_weights);
+
+/* sbb200_nvfp4_moe with the routing computed in front of the permute from
+ * router_logits [M, E] (logits_dt): the top-k ids and softmax weights are
+ * written to topk_ids / topk_weights (outputs here) and used by the forward.
+ * Up to 4096 routes the routing runs inside the route-plan kernel itself, so
+ * it adds no launch. Same workspace as sbb200_nvfp4_moe. */
+int sbb200_nvfp4_moe_from_logits(void* stream, const void* hidden, const void* router_logits,
+                                 int logits_dt, int32_t* topk_ids, float* topk_weights,
+                                 const void* w13, const void* w13_scales,
+                                 const float* w13_global_scales, const void* w2,
+                                 const void* w2_scales, const float* w2_global_scales,
+                                 void* workspace, size_t workspace_bytes, void* out, int out_dt,
+                                 size_t M, size_t E, size_t top_k, size_t K, size_t I,
+                                 int act_dt, int multiply_router_weight);
+
 /* Stable route permutation (nvfp4_moe_grouped.sycl.cpp:140-204 with the CPU
  * tier's order, src/phase7/cpu_expert_capi.cpp:563-599): counts int32 [E],
  * offsets int32 [E + 1], sorted int32 [M*top_k] (route ids r = m*top_k + k

@@ -337,6 +337,65 @@ def route_zipf(T: int, E: int, top_k: int, seed: int, s: float = 1.2) -> tuple[n
 # oracle entry points
 # --------------------------------------------------------------------------
 
+def router_topk(logits: np.ndarray, k: int) -> tuple[np.ndarray, np.ndarray]:
+    """fp32 restatement of the reference's top-k router
+    (src/QuixiCore-XPU/kernels/moe/moe_route/variants/xpu_sycl/
+    moe_route.sycl.cpp:16-50): k rounds of argmax over the untaken experts with
+    a strict '>' from -inf (lowest index wins ties; a round that finds nothing
+    picks expert 0), then exp(v - max) of the chosen logits summed in
+    selection order, times 1/sum. Pure-Python loops over the k rounds, numpy
+    over tokens: for test sizes."""
+    x = np.asarray(logits, dtype=np.float32)
+    M, E = x.shape
+    ids = np.zeros((M, k), np.int32)
+    val = np.zeros((M, k), np.float32)
+    taken = np.zeros((M, E), bool)
+    cols = np.arange(E)
+    for i in range(k):
+        cand = np.where(taken, np.float32(-np.inf), x)
+        cand = np.where(np.isnan(cand), np.float32(-np.inf), cand)
+        best = cand.max(axis=1)
+        # lowest index among the maxima; rows whose best is -inf pick expert 0
+        first = np.argmax(cand == best[:, None], axis=1)
+        first = np.where(np.isneginf(best), 0, first)
+        ids[:, i] = first
+        val[:, i] = np.where(np.isneginf(best), np.float32(-np.inf), best)
+        taken[np.arange(M), first] = True
+    m = val.max(axis=1, keepdims=True)
+    ex = np.exp(val - m).astype(np.float32)
+    s = np.zeros(M, np.float32)
+    for i in range(k):
+        s = (s + ex[:, i]).astype(np.float32)
+    inv = (np.float32(1.0) / s).astype(np.float32)
+    return ids, (ex * inv[:, None]).astype(np.float32)
+
+
+def kat_router_reference(logits: np.ndarray, k: int) -> tuple[np.ndarray, np.ndarray]:
+    """The double-precision check loop of the reference's router test
+    (src/QuixiCore-XPU/tests/xpu_ops_smoke.cpp:436-450): argmax with strict
+    '>' from -1e30, softmax over the chosen k in double."""
+    x = np.asarray(logits, dtype=np.float64)
+    M, E = x.shape
+    ids = np.zeros((M, k), np.int32)
+    w = np.zeros((M, k), np.float64)
+    for t in range(M):
+        taken = np.zeros(E, bool)
+        rv = []
+        for i in range(k):
+            best, be = -1e30, 0
+            for e in range(E):
+                if not taken[e] and x[t, e] > best:
+                    best, be = x[t, e], e
+            taken[be] = True
+            ids[t, i] = be
+            rv.append(best)
+        m = max(rv)
+        ex = [np.exp(v - m) for v in rv]
+        tot = sum(ex)
+        w[t] = [v / tot for v in ex]
+    return ids, w
+
+
 def route_plan(ids: np.ndarray, E: int) -> dict:
     """Stable routing permutation: counts, offsets, sorted route ids (expert,
     then token*top_k + k ascending) and each route's slot (-1 if dropped)."""
@@ -376,6 +435,59 @@ def moe_forward(hidden_bf16: np.ndarray, ids: np.ndarray, weights: np.ndarray,
     if rc != 0:
         raise RuntimeError(f"oracle moe_forward failed rc={rc}")
     return out
+
+
+def moe_forward_w4a4(hidden_bf16: np.ndarray, ids: np.ndarray, weights: np.ndarray,
+                     layer: Layer, a13: np.ndarray | None = None, a2: np.ndarray | None = None,
+                     alpha13: np.ndarray | None = None, alpha2: np.ndarray | None = None,
+                     multiply_router_weight: bool = True) -> np.ndarray:
+    """W4A4 expert path: every activation row entering a GEMM is quantised to
+    NVFP4 with ``quantize_nvfp4`` (vLLM ref_nvfp4_quant, pinned against vLLM's
+    own output) and the products e2m1*e4m3 x e2m1*e4m3 are summed in fp64,
+    then scaled. Static (a13/a2/alpha13/alpha2 given, vLLM's a1/a2_gscale and
+    g1/g2_alphas per expert): G = a13[e] or a2[e], result * alpha. Dynamic:
+    G = 448*6/max|row| (fp32), result * (1/G) * g13[e] or g2[e]. SwiGLU in
+    fp32 as ``moe_forward``. Routes outside [0, E) contribute nothing."""
+    x = bf16_bits_to_f32(np.asarray(hidden_bf16, np.uint16))
+    T, K = x.shape
+    E, I = layer.E, layer.I
+    top_k = ids.shape[1]
+    static = a13 is not None
+    out = np.zeros((T, K), np.float64)
+
+    def quant_rows(rows: np.ndarray, G: np.ndarray):
+        deq = np.empty_like(rows, dtype=np.float64)
+        for i in range(rows.shape[0]):
+            q, sf = quantize_nvfp4(rows[i:i + 1], float(G[i]))
+            deq[i] = dequant(q, sf, 1.0)[0]
+        return deq
+
+    def dyn_g(rows: np.ndarray) -> np.ndarray:
+        amax = np.abs(rows).max(axis=1).astype(np.float32)
+        return np.where(amax > 0, np.float32(2688.0) / np.where(amax > 0, amax, 1), np.float32(1.0)).astype(np.float32)
+
+    for e in range(E):
+        t_idx, k_idx = np.nonzero(ids == e)
+        if len(t_idx) == 0:
+            continue
+        w13 = dequant(layer.w13[e], layer.s13[e], 1.0).astype(np.float64)
+        w2 = dequant(layer.w2[e], layer.s2[e], 1.0).astype(np.float64)
+        xr = x[t_idx]
+        G1 = np.full(len(t_idx), a13[e], np.float32) if static else dyn_g(xr)
+        d13 = quant_rows(xr, G1) @ w13.T
+        s1 = (np.full(len(t_idx), alpha13[e], np.float32) if static
+              else (np.float32(1.0) / G1).astype(np.float32) * np.float32(layer.g13[e]))
+        gu = (d13 * s1[:, None].astype(np.float64)).astype(np.float32)
+        g, u = gu[:, :I], gu[:, I:]
+        h = (g / (np.float32(1.0) + np.exp(-g)) * u).astype(np.float32)
+        G2 = np.full(len(t_idx), a2[e], np.float32) if static else dyn_g(h)
+        d2 = quant_rows(h, G2) @ w2.T
+        s2 = (np.full(len(t_idx), alpha2[e], np.float32) if static
+              else (np.float32(1.0) / G2).astype(np.float32) * np.float32(layer.g2[e]))
+        y = (d2 * s2[:, None].astype(np.float64))
+        wr = weights[t_idx, k_idx].astype(np.float64) if multiply_router_weight else 1.0
+        np.add.at(out, t_idx, y * (wr[:, None] if multiply_router_weight else 1.0))
+    return out.astype(np.float32)
 
 
 class ReferenceCpuTier:

@@ -94,6 +94,14 @@ def lib() -> ctypes.CDLL:
         L.sbb200_moe_forward.argtypes = [P, S, P, P, I, P, P, P, I, S, I]
         L.sbb200_health.restype = I
         L.sbb200_health.argtypes = [P, P, ctypes.c_char_p, S]
+        L.sbb200_nvfp4_moe_w4a4.restype = I
+        L.sbb200_nvfp4_moe_w4a4.argtypes = [P, P, P, P, P, P, P, P, P, P, P, P, P, P, P, S, P, I,
+                                            S, S, S, S, S, I, I, P, S]
+        L.sbb200_router_topk.restype = I
+        L.sbb200_router_topk.argtypes = [P, P, I, S, S, S, P, P]
+        L.sbb200_nvfp4_moe_from_logits.restype = I
+        L.sbb200_nvfp4_moe_from_logits.argtypes = [P, P, P, I, P, P, P, P, P, P, P, P, P, S, P, I,
+                                                   S, S, S, S, S, I, I]
         L.sbb200_ep_shard.restype = I
         L.sbb200_ep_shard.argtypes = [S, I, I, P, P]
         L.sbb200_ep_create.restype = P
@@ -334,6 +342,85 @@ def nvfp4_moe_device_errors(device: torch.device | None = None) -> int:
 # --------------------------------------------------------------------------
 # building blocks
 # --------------------------------------------------------------------------
+
+def nvfp4_moe_w4a4(hidden: torch.Tensor, topk_ids: torch.Tensor, topk_weights: torch.Tensor,
+                   w13: torch.Tensor, w13_scales: torch.Tensor, w13_global_scales: torch.Tensor,
+                   w2: torch.Tensor, w2_scales: torch.Tensor, w2_global_scales: torch.Tensor,
+                   a13_gscale: torch.Tensor | None = None, a2_gscale: torch.Tensor | None = None,
+                   alpha13: torch.Tensor | None = None, alpha2: torch.Tensor | None = None,
+                   multiply_router_weight: bool = True,
+                   out_dtype: torch.dtype = torch.float32, out: torch.Tensor | None = None,
+                   stage_events: list | None = None) -> torch.Tensor:
+    """W4A4 routed-expert forward (see sbb200_nvfp4_moe_w4a4): activations
+    quantised once to NVFP4, dynamically per row, or with vLLM's static
+    per-expert a1/a2_gscale and g1/g2_alphas when all four are given."""
+    M, K, E, top_k, I = _validate(hidden, topk_ids, topk_weights, w13, w13_scales,
+                                  w13_global_scales, w2, w2_scales, w2_global_scales)
+    static = [a13_gscale, a2_gscale, alpha13, alpha2]
+    for name, t in zip(("a13_gscale", "a2_gscale", "alpha13", "alpha2"), static):
+        if t is not None:
+            _check_cuda(name, t)
+            if t.dtype != torch.float32 or t.numel() != E:
+                raise ValueError(f"sbb200: {name} must be float32 [E]")
+    if out is None:
+        out = torch.empty((M, K), dtype=out_dtype, device=hidden.device)
+    nbytes = nvfp4_moe_workspace_bytes(M, E, top_k, K, I, hidden.dtype)
+    ws = _workspace(hidden.device, nbytes)
+    evs = None
+    if stage_events is not None:
+        evs = (ctypes.c_void_p * STAGE_EVENTS)(*[ev.cuda_event for ev in stage_events])
+    _check(lib().sbb200_nvfp4_moe_w4a4(
+        _stream(hidden), _p(hidden), _p(topk_ids), _p(topk_weights), _p(w13), _p(w13_scales),
+        _p(w13_global_scales), _p(w2), _p(w2_scales), _p(w2_global_scales), *map(_p, static),
+        _p(ws), ws.numel(), _p(out), DTYPE_CODE[out.dtype], M, E, top_k, K, I,
+        DTYPE_CODE[hidden.dtype], int(bool(multiply_router_weight)), evs,
+        STAGE_EVENTS if evs is not None else 0))
+    return out
+
+
+def router_topk(router_logits: torch.Tensor, top_k: int) -> tuple[torch.Tensor, torch.Tensor]:
+    """Top-k expert ids (int32, selection order) and softmax weights (fp32)
+    of router logits [M, E] (ops::moe_route_topk of the reference, ops.hpp:262-272)."""
+    _check_cuda("router logits", router_logits)
+    if router_logits.dim() != 2 or router_logits.dtype not in DTYPE_CODE:
+        raise ValueError("sbb200: router logits must be float32/float16/bfloat16 [M,E]")
+    M, E = router_logits.shape
+    ids = torch.empty((M, top_k), dtype=torch.int32, device=router_logits.device)
+    w = torch.empty((M, top_k), dtype=torch.float32, device=router_logits.device)
+    _check(lib().sbb200_router_topk(_stream(router_logits), _p(router_logits),
+                                    DTYPE_CODE[router_logits.dtype], M, E, top_k, _p(ids), _p(w)))
+    return ids, w
+
+
+def nvfp4_moe_from_logits(hidden: torch.Tensor, router_logits: torch.Tensor, top_k: int,
+                          w13: torch.Tensor, w13_scales: torch.Tensor,
+                          w13_global_scales: torch.Tensor, w2: torch.Tensor,
+                          w2_scales: torch.Tensor, w2_global_scales: torch.Tensor,
+                          multiply_router_weight: bool = True,
+                          out_dtype: torch.dtype = torch.float32):
+    """The routed-expert forward with top-k routing fused in front of the
+    permute: returns (out, topk_ids, topk_weights)."""
+    _check_cuda("router logits", router_logits)
+    M = hidden.shape[0]
+    if router_logits.dim() != 2 or router_logits.shape[0] != M or router_logits.dtype not in DTYPE_CODE:
+        raise ValueError("sbb200: router logits must be float32/float16/bfloat16 [M,E]")
+    dev = hidden.device
+    ids = torch.empty((M, top_k), dtype=torch.int32, device=dev)
+    w = torch.empty((M, top_k), dtype=torch.float32, device=dev)
+    _, K, E, _, I = _validate(hidden, ids, w, w13, w13_scales, w13_global_scales, w2,
+                              w2_scales, w2_global_scales)
+    if router_logits.shape[1] != E:
+        raise ValueError("sbb200: router logits must have one column per expert")
+    out = torch.empty((M, K), dtype=out_dtype, device=dev)
+    nbytes = nvfp4_moe_workspace_bytes(M, E, top_k, K, I, hidden.dtype)
+    ws = _workspace(dev, nbytes)
+    _check(lib().sbb200_nvfp4_moe_from_logits(
+        _stream(hidden), _p(hidden), _p(router_logits), DTYPE_CODE[router_logits.dtype], _p(ids),
+        _p(w), _p(w13), _p(w13_scales), _p(w13_global_scales), _p(w2), _p(w2_scales),
+        _p(w2_global_scales), _p(ws), ws.numel(), _p(out), DTYPE_CODE[out.dtype], M, E, top_k, K,
+        I, DTYPE_CODE[hidden.dtype], int(bool(multiply_router_weight))))
+    return out, ids, w
+
 
 def route_plan(topk_ids: torch.Tensor, E: int) -> dict:
     """Stable device routing permutation; see sbb200_route_plan."""

@@ -165,6 +165,136 @@ int sbb200_nvfp4_moe_staged(void* stream, const void* hidden, const int32_t* top
   }
 }
 
+int sbb200_nvfp4_moe_w4a4(void* stream, const void* hidden, const int32_t* topk_ids,
+                          const float* topk_weights, const void* w13, const void* w13_scales,
+                          const float* w13_global_scales, const void* w2, const void* w2_scales,
+                          const float* w2_global_scales, const float* a13_gscale,
+                          const float* a2_gscale, const float* alpha13, const float* alpha2,
+                          void* workspace, size_t workspace_bytes, void* out, int out_dt,
+                          size_t M, size_t E, size_t top_k, size_t K, size_t I, int act_dt,
+                          int multiply_router_weight, void* const* stage_events,
+                          size_t n_stage_events) {
+  try {
+    if (stage_events && n_stage_events != SBB200_STAGE_EVENTS)
+      return fail(SBB200_EINVAL, "stage_events must hold SBB200_STAGE_EVENTS entries");
+    std::string why;
+    int rc = sbb::validate_shape(M, E, top_k, K, I, act_dt, out_dt, &why);
+    if (rc != SBB200_OK) return fail(rc, why);
+    const bool stat = a13_gscale || a2_gscale || alpha13 || alpha2;
+    if (stat && !(a13_gscale && a2_gscale && alpha13 && alpha2))
+      return fail(SBB200_EINVAL, "nvfp4_moe_w4a4: static scales need a13_gscale, a2_gscale, "
+                                 "alpha13 and alpha2 together");
+    if (!hidden || !topk_ids || !w13 || !w13_scales || !w2 || !w2_scales || !workspace || !out ||
+        (!stat && (!w13_global_scales || !w2_global_scales)) ||
+        (multiply_router_weight && !topk_weights))
+      return fail(SBB200_EINVAL, "nvfp4_moe_w4a4 received a null pointer");
+    if (!sbb::bs_supported((int)K, (int)I))
+      return fail(SBB200_EUNSUPPORTED, "nvfp4_moe_w4a4 needs K and I multiples of 256");
+    const sbb::WorkspacePlan plan = sbb::plan_workspace(M, E, top_k, K, I);
+    if (workspace_bytes < plan.total)
+      return fail(SBB200_EWORKSPACE, "workspace holds " + std::to_string(workspace_bytes) +
+                                         " bytes, the call needs " + std::to_string(plan.total));
+    sbb::MoeArgs a{};
+    a.hidden = hidden;
+    a.act_dt = act_dt;
+    a.ids = topk_ids;
+    a.weights = topk_weights;
+    a.multiply_router_weight = multiply_router_weight;
+    a.w13 = static_cast<const uint8_t*>(w13);
+    a.s13 = static_cast<const uint8_t*>(w13_scales);
+    a.g13 = w13_global_scales;
+    a.w2 = static_cast<const uint8_t*>(w2);
+    a.s2 = static_cast<const uint8_t*>(w2_scales);
+    a.g2 = w2_global_scales;
+    a.out = out;
+    a.out_dt = out_dt;
+    a.M = (int64_t)M;
+    a.E = (int)E;
+    a.top_k = (int)top_k;
+    a.K = (int)K;
+    a.I = (int)I;
+    a.act_terms = 1;
+    a.a13_gscale = a13_gscale;
+    a.a2_gscale = a2_gscale;
+    a.alpha13 = alpha13;
+    a.alpha2 = alpha2;
+    a.stage_events = stage_events;
+    cudaError_t err = sbb::run_moe(a, plan, workspace, static_cast<cudaStream_t>(stream), &why);
+    if (err != cudaSuccess) return fail(SBB200_ECUDA, why + ": " + cudaGetErrorString(err));
+    return SBB200_OK;
+  } catch (...) {
+    return fail(SBB200_ECUDA, "nvfp4_moe_w4a4: host exception");
+  }
+}
+
+int sbb200_router_topk(void* stream, const void* router_logits, int dt, size_t M, size_t E,
+                       size_t top_k, int32_t* topk_ids, float* topk_weights) {
+  if (!dtype_ok(dt)) return fail(SBB200_EINVAL, "router logits dtype must be f32, f16 or bf16");
+  if (E == 0 || E > (size_t)sbb::kMaxExperts || top_k == 0 || top_k > E ||
+      top_k > (size_t)sbb::kMaxTopK)
+    return fail(SBB200_EINVAL, "router top-k needs 1 <= top_k <= min(E, 64) and E <= 512");
+  if (M == 0) return SBB200_OK;
+  if (!router_logits || !topk_ids || !topk_weights)
+    return fail(SBB200_EINVAL, "router top-k received a null pointer");
+  const cudaError_t err = sbb::launch_router_topk(router_logits, dt, (int64_t)M, (int)E,
+                                                  (int)top_k, topk_ids, topk_weights,
+                                                  static_cast<cudaStream_t>(stream));
+  if (err != cudaSuccess) return cuda_fail(err, "router top-k");
+  return SBB200_OK;
+}
+
+int sbb200_nvfp4_moe_from_logits(void* stream, const void* hidden, const void* router_logits,
+                                 int logits_dt, int32_t* topk_ids, float* topk_weights,
+                                 const void* w13, const void* w13_scales,
+                                 const float* w13_global_scales, const void* w2,
+                                 const void* w2_scales, const float* w2_global_scales,
+                                 void* workspace, size_t workspace_bytes, void* out, int out_dt,
+                                 size_t M, size_t E, size_t top_k, size_t K, size_t I,
+                                 int act_dt, int multiply_router_weight) {
+  try {
+    std::string why;
+    int rc = sbb::validate_shape(M, E, top_k, K, I, act_dt, out_dt, &why);
+    if (rc != SBB200_OK) return fail(rc, why);
+    if (!dtype_ok(logits_dt)) return fail(SBB200_EINVAL, "router logits dtype must be f32, f16 or bf16");
+    if (top_k > E) return fail(SBB200_EINVAL, "router top-k needs top_k <= E");
+    if (!hidden || !router_logits || !topk_ids || !topk_weights || !w13 || !w13_scales ||
+        !w13_global_scales || !w2 || !w2_scales || !w2_global_scales || !workspace || !out)
+      return fail(SBB200_EINVAL, "nvfp4_moe_from_logits received a null pointer");
+    const sbb::WorkspacePlan plan = sbb::plan_workspace(M, E, top_k, K, I);
+    if (workspace_bytes < plan.total)
+      return fail(SBB200_EWORKSPACE, "workspace holds " + std::to_string(workspace_bytes) +
+                                         " bytes, the call needs " + std::to_string(plan.total));
+    sbb::MoeArgs a{};
+    a.hidden = hidden;
+    a.act_dt = act_dt;
+    a.ids = topk_ids;
+    a.weights = topk_weights;
+    a.router_logits = router_logits;
+    a.logits_dt = logits_dt;
+    a.routed_ids = topk_ids;
+    a.routed_weights = topk_weights;
+    a.multiply_router_weight = multiply_router_weight;
+    a.w13 = static_cast<const uint8_t*>(w13);
+    a.s13 = static_cast<const uint8_t*>(w13_scales);
+    a.g13 = w13_global_scales;
+    a.w2 = static_cast<const uint8_t*>(w2);
+    a.s2 = static_cast<const uint8_t*>(w2_scales);
+    a.g2 = w2_global_scales;
+    a.out = out;
+    a.out_dt = out_dt;
+    a.M = (int64_t)M;
+    a.E = (int)E;
+    a.top_k = (int)top_k;
+    a.K = (int)K;
+    a.I = (int)I;
+    cudaError_t err = sbb::run_moe(a, plan, workspace, static_cast<cudaStream_t>(stream), &why);
+    if (err != cudaSuccess) return fail(SBB200_ECUDA, why + ": " + cudaGetErrorString(err));
+    return SBB200_OK;
+  } catch (...) {
+    return fail(SBB200_ECUDA, "nvfp4_moe_from_logits: host exception");
+  }
+}
+
 int sbb200_nvfp4_moe_bad_ids(void* stream, const void* workspace, uint32_t* count) {
   if (!workspace || !count) return fail(SBB200_EINVAL, "bad_ids received a null pointer");
   const uint32_t* status = reinterpret_cast<const uint32_t*>(

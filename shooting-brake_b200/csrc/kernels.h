@@ -20,9 +20,18 @@ constexpr int kMaxTopK = 64;
 size_t route_plan_chunks(int64_t R);
 size_t route_scatter_smem(int E);
 
+// With `logits` ([R / top_k, E] in logits_dt) the plan first routes every
+// token (top-k + softmax) into `ids` (then written, not read) and `weights`;
+// a single-chunk plan does it inside its one CTA.
 cudaError_t launch_route_plan(const int32_t* ids, int64_t R, int E, int32_t* chunk_counts,
                               int32_t* counts, int32_t* offsets, int32_t* sorted,
-                              int32_t* slot_of, uint32_t* status, cudaStream_t stream);
+                              int32_t* slot_of, uint32_t* status, cudaStream_t stream,
+                              const void* logits = nullptr, int logits_dt = 0, int top_k = 1,
+                              float* weights = nullptr);
+
+// Top-k routing: ids int32 [M, k], weights fp32 [M, k] from logits [M, E].
+cudaError_t launch_router_topk(const void* logits, int dt, int64_t M, int E, int k, int32_t* ids,
+                               float* weights, cudaStream_t stream);
 
 // CUDA-core grouped expert kernels: any K, I that are multiples of 32.
 // h: fp32 [R, I] in sorted-slot order; y: fp32 [R, K] (global scale applied,
@@ -80,6 +89,11 @@ struct BsLaunch {
   const void* hidden;
   int act_dt;
   SplitRows hidden_rows;   // base != nullptr: token rows read from other GPUs
+  int nt;                  // activation terms: kSplitTerms (W4A16) or 1 (W4A4)
+  const int32_t* ids;      // route expert ids (static W4A4 global lookup)
+  // static W4A4 (a13_gscale != nullptr): activation quantisation globals and
+  // output scales per expert, vLLM's a1/a2_gscale and g1/g2_alphas
+  const float *a13_gscale, *a2_gscale, *alpha13, *alpha2;
   const int32_t* counts;
   const int32_t* offsets;
   const int32_t* sorted;
@@ -102,7 +116,7 @@ struct BsLaunch {
 };
 
 bool bs_supported(int K, int I);
-int bs_tile_rows(int64_t routes, int E, int mode);
+int bs_tile_rows(int64_t routes, int E, int mode, int nt);
 cudaError_t launch_moe_bs(const BsLaunch& a, cudaStream_t stream, const char** step);
 
 }  // namespace sbb

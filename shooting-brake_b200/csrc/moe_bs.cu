@@ -541,10 +541,47 @@ __device__ __forceinline__ void load8(const void* src, int src_dt, int64_t at, f
   }
 }
 
+// One 16-element block to one NVFP4 term under quantisation global G (g =
+// 1/G): scale = min(G * bmax / 6, 448) to e4m3, elements to the nearest e2m1
+// of x / (e4m3 * g) (vLLM ref_nvfp4_quant). With RESID the block is left
+// holding what the term does not represent.
+template <bool RESID>
+__device__ __forceinline__ void quant_block(float* v, float G, float g, uint32_t* w,
+                                            uint8_t* scale_byte) {
+  float bmax = 0.0f;
+#pragma unroll
+  for (int i = 0; i < 16; ++i) bmax = fmaxf(bmax, fabsf(v[i]));
+  const float scale = fminf(__fmul_rn(G, __fmul_rn(bmax, 1.0f / 6.0f)), 448.0f);
+  const __nv_fp8_storage_t s8 = __nv_cvt_float_to_fp8(scale, __NV_SATFINITE, __NV_E4M3);
+  const float sg = __fmul_rn(e4m3_to_f32_hw(s8), g);  // one e2m1 step of this block
+  const float inv = sg == 0.0f ? 0.0f : __frcp_rn(sg);
+  w[0] = w[1] = 0u;
+#pragma unroll
+  for (int j = 0; j < 8; ++j) {
+    // nearest e2m1 (ties to even, saturating at 6) of both elements
+    const uint32_t pair = e2m1x2_from_f32(__fmul_rn(v[2 * j], inv), __fmul_rn(v[2 * j + 1], inv));
+    if (RESID) {
+      // the MMA sees e2m1 * e4m3 * g; the next term quantises what is left
+      const float2 dq = e2m1x2_to_float2(pair);
+      v[2 * j] -= __fmul_rn(dq.x, sg);
+      v[2 * j + 1] -= __fmul_rn(dq.y, sg);
+    }
+    w[j >> 2] |= pair << (8 * (j & 3));
+  }
+  *scale_byte = static_cast<uint8_t>(s8);
+}
+
+// gstatic != nullptr (W4A4 with static activation globals, NT = 1): the
+// block of each destination slot is quantised under gstatic[e] of that
+// slot's expert e (token mode: eids[row * top_k + k]; row mode:
+// eids[sorted[row]]) and its g is 1, because the GEMM epilogue then scales by
+// the caller's per-expert alpha. Otherwise the row's global is dynamic,
+// G0 = 448 * 6 / max|row|, with NT terms at G0 * 4^t.
 __global__ void __launch_bounds__(1024) split_nvfp4_kernel(
     const void* __restrict__ src, int src_dt, SplitRows rows, const int32_t* __restrict__ slot_of,
     int top_k, const int32_t* __restrict__ n_rows_dev, int K, int NT, uint8_t* __restrict__ q,
-    uint8_t* __restrict__ sf, float* __restrict__ gout) {
+    uint8_t* __restrict__ sf, float* __restrict__ gout, const float* __restrict__ gstatic,
+    const int32_t* __restrict__ eids, const int32_t* __restrict__ sorted) {
   __shared__ float s_max[32];
   __shared__ int32_t s_dst[kMaxTopK];
   __shared__ int s_any;
@@ -575,11 +612,30 @@ __global__ void __launch_bounds__(1024) split_nvfp4_kernel(
   const int blk = blockIdx.y * blockDim.x + tid;  // this thread's 16-element block
   const bool active = blk * 16 < K;
   float v[16];
-  float amax = 0.0f;
   if (active) {
     load8(rsrc, src_dt, rbase + blk * 16, v);
     load8(rsrc, src_dt, rbase + blk * 16 + 8, v + 8);
   }
+  if (gstatic) {
+    for (int d = 0; d < ndst; ++d) {
+      const int64_t dst = slot_of ? static_cast<int64_t>(s_dst[d]) : row;
+      if (dst < 0) continue;
+      const int32_t e = slot_of ? eids[row * top_k + d] : eids[sorted[row]];
+      const float G = gstatic[e];
+      if (blockIdx.y == 0 && tid == 0) gout[dst] = 1.0f;
+      if (!active) continue;
+      float x[16];
+#pragma unroll
+      for (int i = 0; i < 16; ++i) x[i] = v[i];
+      uint32_t w[2];
+      uint8_t s8;
+      quant_block<false>(x, G, __fdiv_rn(1.0f, G), w, &s8);
+      *reinterpret_cast<uint2*>(q + dst * (K / 2) + blk * 8) = make_uint2(w[0], w[1]);
+      sf[dst * (K / 16) + blk] = s8;
+    }
+    return;
+  }
+  float amax = 0.0f;
   if (gridDim.y == 1) {
     if (active) {
 #pragma unroll
@@ -609,30 +665,15 @@ __global__ void __launch_bounds__(1024) split_nvfp4_kernel(
   if (!active) return;
   float G = G0, g = g0;
   for (int t = 0; t < NT; ++t) {
-    float bmax = 0.0f;
-#pragma unroll
-    for (int i = 0; i < 16; ++i) bmax = fmaxf(bmax, fabsf(v[i]));
-    const float scale = fminf(__fmul_rn(G, __fmul_rn(bmax, 1.0f / 6.0f)), 448.0f);
-    const __nv_fp8_storage_t s8 = __nv_cvt_float_to_fp8(scale, __NV_SATFINITE, __NV_E4M3);
-    const float sg = __fmul_rn(e4m3_to_f32_hw(s8), g);  // one e2m1 step of this block
-    const float inv = sg == 0.0f ? 0.0f : __frcp_rn(sg);
-    uint32_t w[2] = {0u, 0u};
-#pragma unroll
-    for (int j = 0; j < 8; ++j) {
-      // nearest e2m1 (ties to even, saturating at 6) of both elements
-      const uint32_t pair = e2m1x2_from_f32(__fmul_rn(v[2 * j], inv), __fmul_rn(v[2 * j + 1], inv));
-      const float2 dq = e2m1x2_to_float2(pair);
-      // the MMA sees e2m1 * e4m3 * g; the next term quantises what is left
-      v[2 * j] -= __fmul_rn(dq.x, sg);
-      v[2 * j + 1] -= __fmul_rn(dq.y, sg);
-      w[j >> 2] |= pair << (8 * (j & 3));
-    }
+    uint32_t w[2];
+    uint8_t s8;
+    quant_block<true>(v, G, g, w, &s8);
     for (int d = 0; d < ndst; ++d) {
       const int64_t dst = slot_of ? static_cast<int64_t>(s_dst[d]) : row;
       if (dst < 0) continue;
       const int64_t orow = dst * NT + t;
       *reinterpret_cast<uint2*>(q + orow * (K / 2) + blk * 8) = make_uint2(w[0], w[1]);
-      sf[orow * (K / 16) + blk] = static_cast<uint8_t>(s8);
+      sf[orow * (K / 16) + blk] = s8;
     }
     G = __fmul_rn(G, 4.0f);
     g = __fmul_rn(g, 0.25f);
@@ -685,18 +726,30 @@ cudaError_t launch_gemm(const CUtensorMap& a, const CUtensorMap& sa, const CUten
   return launch_kernel(true, kern, dim3(grid), dim3(kThreads), C::kSmem, stream, a, sa, b, sb, p);
 }
 
-template <int MODE>
-cudaError_t launch_bnr(int bnr, const CUtensorMap& a, const CUtensorMap& sa, const CUtensorMap& b,
-                       const CUtensorMap& sb, const BsParams& p, int grid, cudaStream_t stream) {
+template <int MODE, int NT>
+cudaError_t launch_bnr_nt(int bnr, const CUtensorMap& a, const CUtensorMap& sa,
+                          const CUtensorMap& b, const CUtensorMap& sb, const BsParams& p, int grid,
+                          cudaStream_t stream) {
   switch (bnr) {
-    case 16: return launch_gemm<MODE, 16, kSplitTerms>(a, sa, b, sb, p, grid, stream);
-    case 32: return launch_gemm<MODE, 32, kSplitTerms>(a, sa, b, sb, p, grid, stream);
-    case 64: return launch_gemm<MODE, 64, kSplitTerms>(a, sa, b, sb, p, grid, stream);
-    case 96: return launch_gemm<MODE, 96, kSplitTerms>(a, sa, b, sb, p, grid, stream);
-    case 128: return launch_gemm<MODE, 128, kSplitTerms>(a, sa, b, sb, p, grid, stream);
-    case 192: return launch_gemm<MODE, 192, kSplitTerms>(a, sa, b, sb, p, grid, stream);
+    case 16: return launch_gemm<MODE, 16, NT>(a, sa, b, sb, p, grid, stream);
+    case 32: return launch_gemm<MODE, 32, NT>(a, sa, b, sb, p, grid, stream);
+    case 64: return launch_gemm<MODE, 64, NT>(a, sa, b, sb, p, grid, stream);
+    case 96: return launch_gemm<MODE, 96, NT>(a, sa, b, sb, p, grid, stream);
+    case 128: return launch_gemm<MODE, 128, NT>(a, sa, b, sb, p, grid, stream);
+    case 192: return launch_gemm<MODE, 192, NT>(a, sa, b, sb, p, grid, stream);
     default: return cudaErrorInvalidValue;
   }
+}
+
+// nt = 4: bf16/f16/f32 activations as four NVFP4 terms (W4A16 results);
+// nt = 1: activations quantised once (W4A4).
+template <int MODE>
+cudaError_t launch_bnr(int bnr, int nt, const CUtensorMap& a, const CUtensorMap& sa,
+                       const CUtensorMap& b, const CUtensorMap& sb, const BsParams& p, int grid,
+                       cudaStream_t stream) {
+  if (nt == kSplitTerms) return launch_bnr_nt<MODE, kSplitTerms>(bnr, a, sa, b, sb, p, grid, stream);
+  if (nt == 1) return launch_bnr_nt<MODE, 1>(bnr, a, sa, b, sb, p, grid, stream);
+  return cudaErrorInvalidValue;
 }
 
 int sm_count() {
@@ -711,7 +764,8 @@ int sm_count() {
 // given, n_rows an upper bound).
 cudaError_t launch_split(const void* src, int src_dt, const SplitRows* rows,
                          const int32_t* slot_of, int top_k, const int32_t* n_rows_dev,
-                         int64_t n_rows, int K, uint8_t* q, uint8_t* sf, float* g,
+                         int64_t n_rows, int K, int nt, uint8_t* q, uint8_t* sf, float* g,
+                         const float* gstatic, const int32_t* eids, const int32_t* sorted,
                          cudaStream_t stream) {
   if (n_rows <= 0) return cudaSuccess;
   const SplitRows r = rows ? *rows : SplitRows{nullptr, 1};
@@ -719,7 +773,7 @@ cudaError_t launch_split(const void* src, int src_dt, const SplitRows* rows,
   const int threads = r.base ? K / 16 : kSplitThreads;
   const dim3 grid(static_cast<unsigned>(n_rows), r.base ? 1 : (K + kSplitChunk - 1) / kSplitChunk);
   return launch_kernel(true, split_nvfp4_kernel, grid, dim3(threads), 0, stream, src, src_dt, r,
-                       slot_of, top_k, n_rows_dev, K, static_cast<int>(kSplitTerms), q, sf, g);
+                       slot_of, top_k, n_rows_dev, K, nt, q, sf, g, gstatic, eids, sorted);
 }
 
 }  // namespace
@@ -735,24 +789,25 @@ bool bs_supported(int K, int I) {
 // reused by 50 % more tokens per byte staged; one accumulator buffer) and
 // down 24 (N = 96: two accumulator buffers fit, so a unit's epilogue overlaps
 // the next unit's MMAs, which matters with only I / 256 K stages per unit).
-int bs_tile_rows(int64_t routes, int E, int mode) {
-  const double per = static_cast<double>(routes) / E * 1.5;
-  int tok = 4;
-  while (tok < per && tok * kSplitTerms < 128) tok *= 2;
-  if (tok == 32 && per > 48.0) return (mode == kGateUp ? 48 : 24) * kSplitTerms;
-  return tok * kSplitTerms;
+int bs_tile_rows(int64_t routes, int E, int mode, int nt) {
+  const double want = static_cast<double>(routes) / E * 1.5 * nt;  // term rows
+  int rows = 16;
+  while (rows < want && rows < 128) rows *= 2;
+  if (rows == 128 && want > 192.0) return mode == kGateUp ? 192 : 96;
+  return rows;
 }
 
 cudaError_t launch_moe_bs(const BsLaunch& a, cudaStream_t stream, const char** step) {
   const int64_t R = a.R;
-  const int NT = kSplitTerms;
+  const int NT = a.nt;
+  const bool w4a4_static = a.a13_gscale != nullptr;
   const int grid = sm_count();
   const uint64_t brows = static_cast<uint64_t>(R > 0 ? R : 1) * NT;
   // All tensor maps are encoded before the first launch, so the host never
   // holds the stream up between kernels.
   *step = "tensor maps";
-  const int bnr1 = bs_tile_rows(R, a.E, kGateUp);
-  const int bnr2 = bs_tile_rows(R, a.E, kDown);
+  const int bnr1 = bs_tile_rows(R, a.E, kGateUp, NT);
+  const int bnr2 = bs_tile_rows(R, a.E, kDown, NT);
   CUtensorMap m1a, m1sa, m1b, m1sb, m2a, m2sa, m2b, m2sb;
   if (!encode_u8(&m1a, a.w13, a.K / 2, (uint64_t)a.E * 2 * a.I, kRowBytes, kM,
                  CU_TENSOR_MAP_SWIZZLE_128B) ||
@@ -770,7 +825,8 @@ cudaError_t launch_moe_bs(const BsLaunch& a, cudaStream_t stream, const char** s
   BsParams p1{};
   p1.counts = a.counts;
   p1.offsets = a.offsets;
-  p1.gscale = a.g13;
+  // static W4A4: the caller's per-expert alpha scales the MMA result alone
+  p1.gscale = w4a4_static ? a.alpha13 : a.g13;
   p1.bg = a.xg;
   p1.out = a.h;
   p1.status = a.status;
@@ -784,7 +840,7 @@ cudaError_t launch_moe_bs(const BsLaunch& a, cudaStream_t stream, const char** s
   // about one token tile per expert: every weight tile is read once
   p1.stream_weights = R <= static_cast<int64_t>(a.E) * (bnr1 / NT);
   BsParams p2 = p1;
-  p2.gscale = a.g2;
+  p2.gscale = w4a4_static ? a.alpha2 : a.g2;
   p2.bg = a.hg;
   p2.out = a.y;
   p2.m_tiles = a.K / (2 * kM);
@@ -797,21 +853,22 @@ cudaError_t launch_moe_bs(const BsLaunch& a, cudaStream_t stream, const char** s
   // 1. split each token once; its terms go to all of its route slots
   *step = "activation split";
   cudaError_t err = launch_split(a.hidden, a.act_dt, &a.hidden_rows, a.slot_of, a.top_k, nullptr,
-                                 a.M, a.K, a.xq, a.xsf, a.xg, stream);
+                                 a.M, a.K, NT, a.xq, a.xsf, a.xg, a.a13_gscale, a.ids, a.sorted,
+                                 stream);
   if (err != cudaSuccess) return err;
   if (a.stage_mark) a.stage_mark(a.stage_ctx, 1);
   // 2. gate/up + SwiGLU
   *step = "gate/up";
-  err = launch_bnr<kGateUp>(bnr1, m1a, m1sa, m1b, m1sb, p1, grid, stream);
+  err = launch_bnr<kGateUp>(bnr1, NT, m1a, m1sa, m1b, m1sb, p1, grid, stream);
   if (err != cudaSuccess) return err;
   if (a.stage_mark) a.stage_mark(a.stage_ctx, 2);
   // 3. split the SwiGLU rows, down projection
   *step = "h split";
-  err = launch_split(a.h, kF32, nullptr, nullptr, 1, a.offsets + a.E, R, a.I, a.hq, a.hsf, a.hg,
-                     stream);
+  err = launch_split(a.h, kF32, nullptr, nullptr, 1, a.offsets + a.E, R, a.I, NT, a.hq, a.hsf,
+                     a.hg, a.a2_gscale, a.ids, a.sorted, stream);
   if (err != cudaSuccess) return err;
   *step = "down";
-  err = launch_bnr<kDown>(bnr2, m2a, m2sa, m2b, m2sb, p2, grid, stream);
+  err = launch_bnr<kDown>(bnr2, NT, m2a, m2sa, m2b, m2sb, p2, grid, stream);
   if (err != cudaSuccess) return err;
   if (a.stage_mark) a.stage_mark(a.stage_ctx, 3);
   return cudaSuccess;

@@ -71,14 +71,22 @@ cudaError_t run_moe(const MoeArgs& a, const WorkspacePlan& plan, void* workspace
   if (err != cudaSuccess) { *why = "stage event"; return err; }
   err = cudaMemsetAsync(status, 0, 256, stream);
   if (err != cudaSuccess) { *why = "status clear"; return err; }
-  err = launch_route_plan(a.ids, R, a.E, chunk_counts, counts, offsets, sorted, slot_of, status,
-                          stream);
+  const int32_t* ids = a.router_logits ? a.routed_ids : a.ids;
+  const float* weights = a.router_logits ? a.routed_weights : a.weights;
+  err = launch_route_plan(ids, R, a.E, chunk_counts, counts, offsets, sorted, slot_of, status,
+                          stream, a.router_logits, a.logits_dt, a.top_k, a.routed_weights);
   if (err != cudaSuccess) { *why = "route plan"; return err; }
   if (bs_supported(a.K, a.I)) {
     BsLaunch t{};
     t.hidden = a.hidden;
     t.act_dt = a.act_dt;
     t.hidden_rows = a.hidden_rows;
+    t.nt = a.act_terms;
+    t.ids = ids;
+    t.a13_gscale = a.a13_gscale;
+    t.a2_gscale = a.a2_gscale;
+    t.alpha13 = a.alpha13;
+    t.alpha2 = a.alpha2;
     t.counts = counts;
     t.offsets = offsets;
     t.sorted = sorted;
@@ -119,8 +127,9 @@ cudaError_t run_moe(const MoeArgs& a, const WorkspacePlan& plan, void* workspace
     err = launch_moe_bs(t, stream, &step);
     if (err != cudaSuccess) { *why = step; return err; }
   } else {
-    if (a.hidden_rows.base) {
-      *why = "expert-parallel rows need K and I multiples of 256";
+    if (a.hidden_rows.base || a.act_terms != kSplitTerms) {
+      *why = a.hidden_rows.base ? "expert-parallel rows need K and I multiples of 256"
+                                : "W4A4 needs K and I multiples of 256";
       return cudaErrorInvalidValue;
     }
     if ((err = mark(1)) != cudaSuccess) { *why = "stage event"; return err; }
@@ -132,7 +141,7 @@ cudaError_t run_moe(const MoeArgs& a, const WorkspacePlan& plan, void* workspace
     if (err != cudaSuccess) { *why = "down"; return err; }
     if ((err = mark(3)) != cudaSuccess) { *why = "stage event"; return err; }
   }
-  err = launch_combine(y, slot_of, a.weights, a.multiply_router_weight, a.out, a.out_dt, a.M,
+  err = launch_combine(y, slot_of, weights, a.multiply_router_weight, a.out, a.out_dt, a.M,
                        a.top_k, a.K, stream, a.out_rows.base ? &a.out_rows : nullptr,
                        a.done.counter ? &a.done : nullptr);
   if (err != cudaSuccess) { *why = "combine"; return err; }

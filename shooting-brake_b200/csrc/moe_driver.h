@@ -51,6 +51,19 @@ struct MoeArgs {
   SplitRows hidden_rows{nullptr, 1};
   SplitRows out_rows{nullptr, 1};
   PeerSignal done{nullptr, nullptr, nullptr, 0};
+  // routing from router logits [M, E] (logits_dt): the plan writes top-k ids
+  // into `routed_ids` and softmax weights into `routed_weights`, which the
+  // rest of the forward then uses in place of ids / weights
+  // activation terms: kSplitTerms (W4A16 results) or 1 (W4A4: one NVFP4
+  // quantisation of the activations, dynamic per row unless a13_gscale is
+  // set, in which case a13/a2_gscale quantise and alpha13/alpha2 scale)
+  int act_terms = kSplitTerms;
+  const float *a13_gscale = nullptr, *a2_gscale = nullptr;
+  const float *alpha13 = nullptr, *alpha2 = nullptr;
+  const void* router_logits = nullptr;
+  int logits_dt = 0;
+  int32_t* routed_ids = nullptr;
+  float* routed_weights = nullptr;
 };
 
 int validate_shape(size_t M, size_t E, size_t top_k, size_t K, size_t I, int act_dt, int out_dt,

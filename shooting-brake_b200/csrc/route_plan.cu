@@ -28,6 +28,82 @@ constexpr int kWarps = kThreads / 32;
 
 __device__ __forceinline__ bool valid_id(int32_t e, int E) { return e >= 0 && e < E; }
 
+// Top-k routing of token t by one warp (the reference's moe_route_topk,
+// src/QuixiCore-XPU/kernels/moe/moe_route/variants/xpu_sycl/
+// moe_route.sycl.cpp:16-50): k rounds of argmax over the untaken experts with
+// a strict '>' (the lowest index wins ties, NaN is never chosen, and a round
+// that finds nothing above -inf picks expert 0), then a softmax over the k
+// chosen logits, summed in selection order. Lane l holds logits l + 32 j
+// (E <= 512); the chosen ids and logits of round i live in lane i % 32.
+__device__ void topk_token_warp(const void* __restrict__ logits, int dt, int64_t t, int E, int k,
+                                int32_t* ids, float* weights) {
+  const int lane = threadIdx.x & 31;
+  constexpr int kPer = kMaxExperts / 32;
+  float v[kPer];
+#pragma unroll
+  for (int j = 0; j < kPer; ++j) {
+    const int e = lane + 32 * j;
+    v[j] = e < E ? load_act(logits, static_cast<size_t>(t) * E + e, dt) : 0.0f;
+  }
+  uint32_t taken = 0;  // bit j: expert lane + 32 j chosen
+  int32_t my_sel[2] = {0, 0};
+  float my_val[2] = {0.0f, 0.0f};
+  for (int i = 0; i < k; ++i) {
+    float best = -INFINITY;
+    int bi = 0x7fffffff;
+#pragma unroll
+    for (int j = 0; j < kPer; ++j) {
+      const int e = lane + 32 * j;
+      if (e < E && !((taken >> j) & 1u) && v[j] > best) {
+        best = v[j];
+        bi = e;
+      }
+    }
+#pragma unroll
+    for (int d = 16; d > 0; d >>= 1) {
+      const float ob = __shfl_xor_sync(0xffffffffu, best, d);
+      const int oi = __shfl_xor_sync(0xffffffffu, bi, d);
+      if (ob > best || (ob == best && oi < bi)) {
+        best = ob;
+        bi = oi;
+      }
+    }
+    if (bi == 0x7fffffff) bi = 0;  // nothing above -inf: expert 0, as the reference
+    if ((bi & 31) == lane) taken |= 1u << (bi >> 5);
+    if ((i & 31) == lane) {
+      my_sel[i >> 5] = bi;
+      my_val[i >> 5] = best;
+    }
+  }
+  // softmax over the chosen logits; max is order-free, the sum follows i
+  float m = -INFINITY;
+  for (int i = 0; i < k; ++i) m = fmaxf(m, __shfl_sync(0xffffffffu, my_val[i >> 5], i & 31));
+  float ex[2] = {0.0f, 0.0f};
+  for (int h = 0; h < 2; ++h)
+    if (lane + 32 * h < k) ex[h] = expf(my_val[h] - m);
+  float sum = 0.0f;
+  for (int i = 0; i < k; ++i) sum += __shfl_sync(0xffffffffu, ex[i >> 5], i & 31);
+  const float inv = 1.0f / sum;
+  for (int h = 0; h < 2; ++h) {
+    const int i = lane + 32 * h;
+    if (i < k) {
+      ids[t * k + i] = my_sel[h];
+      weights[t * k + i] = ex[h] * inv;
+    }
+  }
+}
+
+// One token per warp.
+__global__ void __launch_bounds__(256) router_topk_kernel(const void* __restrict__ logits, int dt,
+                                                          int64_t M, int E, int k,
+                                                          int32_t* __restrict__ ids,
+                                                          float* __restrict__ weights) {
+  pdl_wait();
+  pdl_trigger();
+  const int64_t t = blockIdx.x * 8ll + (threadIdx.x >> 5);
+  if (t < M) topk_token_warp(logits, dt, t, E, k, ids, weights);
+}
+
 __global__ void __launch_bounds__(kThreads) route_hist_kernel(
     const int32_t* __restrict__ ids, int64_t R, int E, int32_t* __restrict__ chunk_counts,
     uint32_t* __restrict__ status) {
@@ -55,11 +131,15 @@ __global__ void __launch_bounds__(kThreads) route_hist_kernel(
 
 // Shared memory: base[E] (chunk base, then running cursor), offs[E + 1],
 // warp_cnt[kWarps * E].
+// With `logits` (single chunk only) the CTA first routes its tokens itself
+// (one warp per token, ids and weights written to `ids`/`weights`), so
+// routing from router logits costs no extra launch.
 __global__ void __launch_bounds__(kThreads) route_scatter_kernel(
-    const int32_t* __restrict__ ids, int64_t R, int E, int nchunks,
+    const int32_t* ids, int64_t R, int E, int nchunks,
     const int32_t* __restrict__ chunk_counts, int32_t* __restrict__ counts,
     int32_t* __restrict__ offsets, int32_t* __restrict__ sorted,
-    int32_t* __restrict__ slot_of, uint32_t* __restrict__ status) {
+    int32_t* __restrict__ slot_of, uint32_t* __restrict__ status, const void* logits,
+    int logits_dt, int top_k, float* weights) {
   extern __shared__ int32_t smem[];
   int32_t* s_base = smem;                // [E]
   int32_t* s_offs = s_base + E;          // [E + 1]
@@ -72,6 +152,12 @@ __global__ void __launch_bounds__(kThreads) route_scatter_kernel(
   const int64_t end = min(begin + (int64_t)kRouteChunk, R);
   pdl_wait();
   pdl_trigger();
+  if (logits) {
+    const int64_t M = R / top_k;
+    for (int64_t t = warp; t < M; t += kWarps)
+      topk_token_warp(logits, logits_dt, t, E, top_k, const_cast<int32_t*>(ids), weights);
+    __syncthreads();  // the CTA's own global writes are visible to it after the barrier
+  }
 
   // 1. per-expert totals and this chunk's base.
   if (nchunks == 1) {
@@ -167,7 +253,8 @@ size_t route_scatter_smem(int E) { return sizeof(int32_t) * ((size_t)E + (E + 1)
 
 cudaError_t launch_route_plan(const int32_t* ids, int64_t R, int E, int32_t* chunk_counts,
                               int32_t* counts, int32_t* offsets, int32_t* sorted,
-                              int32_t* slot_of, uint32_t* status, cudaStream_t stream) {
+                              int32_t* slot_of, uint32_t* status, cudaStream_t stream,
+                              const void* logits, int logits_dt, int top_k, float* weights) {
   const int nchunks = (int)route_plan_chunks(R);
   if (nchunks == 0) {
     // No routes: counts and offsets are all zero.
@@ -186,16 +273,38 @@ cudaError_t launch_route_plan(const int32_t* ids, int64_t R, int E, int32_t* chu
     if (err != cudaSuccess) return err;
     attr_set[dev] = true;
   }
-  // the first launch of the plan waits for everything before it; the
-  // scatter overlaps the histogram's tail
+  // the first launch of the plan waits for everything before it; later ones
+  // overlap their predecessor's tail
+  bool pdl = false;
+  const void* fused_logits = nullptr;
+  if (logits) {
+    if (nchunks == 1) {
+      fused_logits = logits;
+    } else {
+      const int64_t M = R / top_k;
+      err = launch_kernel(false, router_topk_kernel, dim3((unsigned)((M + 7) / 8)), dim3(256), 0,
+                          stream, logits, logits_dt, M, E, top_k, const_cast<int32_t*>(ids),
+                          weights);
+      if (err != cudaSuccess) return err;
+      pdl = true;
+    }
+  }
   if (nchunks > 1) {
-    err = launch_kernel(false, route_hist_kernel, dim3(nchunks), dim3(kThreads),
+    err = launch_kernel(pdl, route_hist_kernel, dim3(nchunks), dim3(kThreads),
                         sizeof(int32_t) * E, stream, ids, R, E, chunk_counts, status);
     if (err != cudaSuccess) return err;
+    pdl = true;
   }
-  return launch_kernel(nchunks > 1, route_scatter_kernel, dim3(nchunks), dim3(kThreads), smem,
-                       stream, ids, R, E, nchunks, static_cast<const int32_t*>(chunk_counts),
-                       counts, offsets, sorted, slot_of, status);
+  return launch_kernel(pdl, route_scatter_kernel, dim3(nchunks), dim3(kThreads), smem, stream,
+                       ids, R, E, nchunks, static_cast<const int32_t*>(chunk_counts), counts,
+                       offsets, sorted, slot_of, status, fused_logits, logits_dt, top_k, weights);
+}
+
+cudaError_t launch_router_topk(const void* logits, int dt, int64_t M, int E, int k, int32_t* ids,
+                               float* weights, cudaStream_t stream) {
+  if (M == 0) return cudaSuccess;
+  return launch_kernel(false, router_topk_kernel, dim3((unsigned)((M + 7) / 8)), dim3(256), 0,
+                       stream, logits, dt, M, E, k, ids, weights);
 }
 
 }  // namespace sbb
