@@ -262,6 +262,41 @@ int sbb200_health(sbb200_provider_t* p, sbb200_health_t* health, char* last_erro
                   size_t last_error_size);
 
 /* ---------------------------------------------------------------------------
+ * SBEXP001 expert bank (the reference's on-disk NVFP4 bank: writer
+ * src/phase1/extract_experts.py:51-128, 234-281; C++ reader
+ * src/phase1/b70_provider.cpp:194-246, 866-934). Opened read-only by mmap and
+ * validated like the reference (magic, reserved field, geometry, file size);
+ * the INT4 bank (SBINT401) is not part of this path and is rejected.
+ * ------------------------------------------------------------------------- */
+
+typedef struct sbb200_bank sbb200_bank_t;
+
+/* NULL on failure (sbb200_last_error says why). */
+sbb200_bank_t* sbb200_bank_open(const char* path);
+
+int sbb200_bank_info(sbb200_bank_t* bank, size_t* layers, size_t* experts, size_t* hidden,
+                     size_t* intermediate);
+
+/* One expert's planes into HOST buffers (any pointer may be NULL to skip):
+ * w13 [2I, H/2] (gate rows then up rows), w13_scales [2I, H/16], w2 [H, I/2],
+ * w2_scales [H, I/16], and the two fp32 dequant multipliers. */
+int sbb200_bank_read_expert(sbb200_bank_t* bank, size_t layer, size_t expert, void* w13,
+                            void* w13_scales, float* w13_global_scale, void* w2,
+                            void* w2_scales, float* w2_global_scale);
+
+/* Experts [expert_begin, expert_begin + expert_count) of `layer` into DEVICE
+ * planes in the layout of sbb200_nvfp4_moe (row i = expert expert_begin + i):
+ * w13 [n, 2I, H/2], w13_scales [n, 2I, H/16], w13_global_scales fp32 [n], w2
+ * [n, H, I/2], w2_scales [n, H, I/16], w2_global_scales fp32 [n]. Copies on
+ * `stream` through pinned staging and returns when they are complete. */
+int sbb200_bank_load(sbb200_bank_t* bank, void* stream, size_t layer, size_t expert_begin,
+                     size_t expert_count, void* w13, void* w13_scales,
+                     float* w13_global_scales, void* w2, void* w2_scales,
+                     float* w2_global_scales);
+
+void sbb200_bank_close(sbb200_bank_t* bank);
+
+/* ---------------------------------------------------------------------------
  * Expert parallelism over NVLink: one process per GPU of one node, the E
  * routed experts sharded contiguously (the first E % world ranks hold one
  * extra), tokens kept by the rank that owns them. Replaces the reference's

@@ -13,7 +13,8 @@ this module reaches it through ctypes and exposes:
 * :class:`Provider` -- registered layers with an owned workspace
   (the device-resident replacement of the B70 provider C-ABI);
 * :mod:`.plugin` -- the vLLM ``RoutedExperts`` hook adapter;
-* :mod:`.ep` -- expert parallelism over NVLink (one process per GPU).
+* :mod:`.ep` -- expert parallelism over NVLink (one process per GPU);
+* :mod:`.bank` -- the reference's SBEXP001 expert-bank files.
 
 There is no CPU fallback: every entry point raises if the CUDA library is
 missing or the tensors are not on a CUDA device.
@@ -102,6 +103,16 @@ def lib() -> ctypes.CDLL:
         L.sbb200_nvfp4_moe_from_logits.restype = I
         L.sbb200_nvfp4_moe_from_logits.argtypes = [P, P, P, I, P, P, P, P, P, P, P, P, P, S, P, I,
                                                    S, S, S, S, S, I, I]
+        L.sbb200_bank_open.restype = P
+        L.sbb200_bank_open.argtypes = [ctypes.c_char_p]
+        L.sbb200_bank_info.restype = I
+        L.sbb200_bank_info.argtypes = [P, P, P, P, P]
+        L.sbb200_bank_read_expert.restype = I
+        L.sbb200_bank_read_expert.argtypes = [P, S, S, P, P, P, P, P, P]
+        L.sbb200_bank_load.restype = I
+        L.sbb200_bank_load.argtypes = [P, P, S, S, S, P, P, P, P, P, P]
+        L.sbb200_bank_close.restype = None
+        L.sbb200_bank_close.argtypes = [P]
         L.sbb200_ep_shard.restype = I
         L.sbb200_ep_shard.argtypes = [S, I, I, P, P]
         L.sbb200_ep_create.restype = P
