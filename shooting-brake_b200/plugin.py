@@ -49,7 +49,7 @@ class RoutedExpertsB200:
     def __init__(self, w13: torch.Tensor, w13_scale: torch.Tensor, w13_global: torch.Tensor,
                  w2: torch.Tensor, w2_scale: torch.Tensor, w2_global: torch.Tensor, *,
                  w13_is_up_gate: bool = False, expert_map: torch.Tensor | None = None,
-                 multiply_router_weight: bool = True):
+                 multiply_router_weight: bool = True, shared: tuple | None = None):
         if w13.dim() != 3 or w13.size(1) % 2:
             raise ValueError("sbb200: w13 must be uint8 [E,2I,d/2]")
         if w13_is_up_gate:
@@ -66,6 +66,44 @@ class RoutedExpertsB200:
                 raise ValueError("sbb200: expert map must be int32 [n_global]")
         self.expert_map = expert_map
         self.multiply_router_weight = multiply_router_weight
+        self.num_routed = self.w13.size(0)
+        self.shared_chunks = 0
+        if shared is not None:
+            self._append_shared(*shared)
+
+    def _append_shared(self, w13, w13_scale, w13_global, w2, w2_scale, w2_global) -> None:
+        """Fuse one NVFP4 shared expert (w13 [2Is, d/2] gate rows then up
+        rows, w2 [d, Is/2], with their scales and scalar globals) into the
+        routed weights. SwiGLU is elementwise over the intermediate dimension,
+        so with Is = n * I the shared expert is exactly n experts of
+        intermediate I (gate/up row blocks, down column blocks on 16-element
+        scale boundaries); they are appended after the routed experts and
+        every token routes to all n with weight 1 (or its shared gate)."""
+        I = self.w13.size(1) // 2
+        Is = w13.size(0) // 2
+        if Is % I:
+            raise ValueError(f"sbb200: shared intermediate {Is} is not a multiple of {I}")
+        n = Is // I
+        dev = self.w13.device
+        g13 = w13_global.reshape(-1)[:1].float().to(dev)
+        g2 = w2_global.reshape(-1)[:1].float().to(dev)
+        cw13, cs13, cw2, cs2 = [], [], [], []
+        for c in range(n):
+            rows = slice(c * I, (c + 1) * I)
+            up = slice(Is + c * I, Is + (c + 1) * I)
+            cw13.append(torch.cat([w13[rows], w13[up]]).to(dev))
+            cs13.append(torch.cat([w13_scale[rows], w13_scale[up]]).to(dev))
+            cw2.append(w2[:, c * (I // 2):(c + 1) * (I // 2)].to(dev))
+            cs2.append(w2_scale[:, c * (I // 16):(c + 1) * (I // 16)].to(dev))
+        self.w13 = torch.cat([self.w13, torch.stack(cw13)]).contiguous()
+        self.w13_scale = torch.cat([self.w13_scale, torch.stack(cs13)]).contiguous()
+        self.w2 = torch.cat([self.w2, torch.stack(cw2)]).contiguous()
+        self.w2_scale = torch.cat([self.w2_scale, torch.stack(cs2)]).contiguous()
+        self.w13_global = torch.cat([self.w13_global, g13.expand(n)]).contiguous()
+        self.w2_global = torch.cat([self.w2_global, g2.expand(n)]).contiguous()
+        self.shared_chunks = n
+        self._shared_ids = torch.arange(self.num_routed, self.num_routed + n, dtype=torch.int32,
+                                        device=dev)
 
     @classmethod
     def from_layer(cls, layer, **kw) -> "RoutedExpertsB200":
@@ -86,20 +124,29 @@ class RoutedExpertsB200:
 
     @property
     def num_experts(self) -> int:
-        return self.w13.size(0)
+        return self.num_routed
 
     def forward_modular(self, x: torch.Tensor, topk_weights: torch.Tensor,
                         topk_ids: torch.Tensor, shared_experts=None,
-                        shared_experts_input: torch.Tensor | None = None) -> torch.Tensor:
-        """Routed-expert output [M, d] in x's dtype, plus the shared experts'
-        output when a shared-expert module is given (the hook's
-        ``Y_local + Y_routed`` sum, ``routed_experts.py:2517-2531``)."""
+                        shared_experts_input: torch.Tensor | None = None,
+                        shared_gate: torch.Tensor | None = None) -> torch.Tensor:
+        """Routed-expert output [M, d] in x's dtype, plus the shared expert's:
+        a fused NVFP4 shared expert (``shared=`` at construction) runs inside
+        the same grouped call, weighted by ``shared_gate`` [M] (1 if None); a
+        shared-expert module given here is run beside it and added (the
+        hook's ``Y_local + Y_routed`` sum, ``routed_experts.py:2517-2531``)."""
         ids = topk_ids if topk_ids.dtype == torch.int32 else topk_ids.to(torch.int32)
         if self.expert_map is not None:
             valid = (ids >= 0) & (ids < self.expert_map.numel())
             ids = torch.where(valid, self.expert_map[ids.clamp(0, self.expert_map.numel() - 1)],
                               torch.full_like(ids, -1))
         w = topk_weights if topk_weights.dtype == torch.float32 else topk_weights.float()
+        if self.shared_chunks:
+            M, n = ids.shape[0], self.shared_chunks
+            ids = torch.cat([ids, self._shared_ids.expand(M, n)], dim=1)
+            sw = (torch.ones((M, 1), dtype=torch.float32, device=w.device) if shared_gate is None
+                  else shared_gate.reshape(M, 1).float())
+            w = torch.cat([w, sw.expand(M, n)], dim=1)
         y = nvfp4_moe(x, ids.contiguous(), w.contiguous(), self.w13, self.w13_scale,
                       self.w13_global, self.w2, self.w2_scale, self.w2_global,
                       multiply_router_weight=self.multiply_router_weight, out_dtype=x.dtype)

@@ -122,3 +122,53 @@ def test_expert_map_shard_and_shared_experts(plugin, oracle, cuda):
     local = np.where((ids >= lo) & (ids < hi), ids - lo, -1).astype(np.int32)
     want = oracle.moe_forward(hidden, local, w, shard) + 0.25
     _check(y.float().cpu().numpy(), want)
+
+
+def _shared_layer(oracle, K, Is, seed):
+    S = oracle.make_layer(1, K, Is, seed=seed)
+    return S
+
+
+def test_shared_expert_split_is_exact(plugin, oracle):
+    """The n chunk experts of a fused shared expert dequantise to exactly the
+    shared expert's gate/up row blocks and down column blocks."""
+    import torch
+    E, K, I = 4, 256, 128
+    L, ts = _layer_tensors(oracle, "cpu", E, K, I, seed=31)
+    S = _shared_layer(oracle, K, 3 * I, seed=32)
+    sh = [torch.from_numpy(np.ascontiguousarray(x[0] if x.ndim == 3 else x)) for x in
+          (S.w13, S.s13, S.g13, S.w2, S.s2, S.g2)]
+    ex = plugin.RoutedExpertsB200(*ts, shared=tuple(sh))
+    assert ex.shared_chunks == 3 and ex.num_experts == E and ex.w13.size(0) == E + 3
+    full13 = oracle.dequant(S.w13[0], S.s13[0], float(S.g13[0]))
+    full2 = oracle.dequant(S.w2[0], S.s2[0], float(S.g2[0]))
+    Is = 3 * I
+    for c in range(3):
+        w13 = oracle.dequant(ex.w13[E + c].numpy(), ex.w13_scale[E + c].numpy(), float(ex.w13_global[E + c]))
+        assert np.array_equal(w13[:I], full13[c * I:(c + 1) * I])
+        assert np.array_equal(w13[I:], full13[Is + c * I:Is + (c + 1) * I])
+        w2 = oracle.dequant(ex.w2[E + c].numpy(), ex.w2_scale[E + c].numpy(), float(ex.w2_global[E + c]))
+        assert np.array_equal(w2, full2[:, c * I:(c + 1) * I])
+
+
+@pytest.mark.gpu
+def test_fused_shared_expert_matches_oracle(plugin, oracle, cuda):
+    """Routed experts plus a shared expert of twice the intermediate size in
+    one grouped call, gated per token, against the oracle's two results."""
+    import torch
+    E, K, I, T, top_k = 12, 512, 256, 30, 4
+    L, ts = _layer_tensors(oracle, cuda, E, K, I, seed=41)
+    S = _shared_layer(oracle, K, 2 * I, seed=42)
+    sh = tuple(torch.from_numpy(np.ascontiguousarray(x[0] if x.ndim == 3 else x)).to(cuda)
+               for x in (S.w13, S.s13, S.g13, S.w2, S.s2, S.g2))
+    hidden = oracle.make_hidden(T, K, seed=43)
+    ids, w = oracle.route_logits(T, E, top_k, seed=44)
+    gate = np.random.default_rng(45).uniform(0.2, 1.0, T).astype(np.float32)
+    ex = plugin.RoutedExpertsB200(*ts, shared=sh)
+    x = torch.from_numpy(hidden).to(cuda).view(torch.bfloat16)
+    y = ex.forward_modular(x, torch.from_numpy(w).to(cuda), torch.from_numpy(ids).to(cuda),
+                           shared_gate=torch.from_numpy(gate).to(cuda))
+    routed = oracle.moe_forward(hidden, ids, w, L)
+    shared = oracle.moe_forward(hidden, np.zeros((T, 1), np.int32), np.ones((T, 1), np.float32), S)
+    want = routed + gate[:, None] * shared
+    _check(y.float().cpu().numpy(), want)
