@@ -385,13 +385,15 @@ def run_expert_parallel(args, sbb, rank, world, local):
     # identical full layers and global batches on every rank; each keeps its
     # expert shard and its slice of the tokens
     ep = ep_mod.ExpertParallel(rank=rank, world=world, device=local, max_tokens=Tr, top_k=TOP_K,
-                               E=E, K=D, I=I)
+                               E=E, K=D, I=I, w4a4=args.w4a4)
+    routing = args.routing or ("uniform" if T < 1024 else "biased")
     layers = []
     for lw in make_layers(device, N_LAYERS, seed=1000):
         layers.append(tuple(ep.local_experts(t).contiguous() for t in lw))
         del lw
     torch.cuda.empty_cache()
-    gbatches = [make_batch(device, T, seed=2000 + 17 * i) for i in range(N_LAYERS)]
+    gbatches = [make_batch(device, T, seed=2000 + 17 * i, routing=routing)
+                for i in range(N_LAYERS)]
     batches = [tuple(x[rank * Tr:(rank + 1) * Tr].contiguous() for x in b) for b in gbatches]
     out = torch.empty((Tr, D), dtype=torch.bfloat16, device=device)
     stream = torch.cuda.current_stream(device)
@@ -474,6 +476,12 @@ def run_expert_parallel(args, sbb, rank, world, local):
     hbm_peak = float(peaks.get("hbm_gbs", 6650.0))
     peak_src = "measured" if "hbm_gbs" in peaks else "fallback"
     per_gpu = avg_bytes / world / (ms * 1e-3) / 1e9
+    # routes each rank's shard serves per step (load imbalance across ranks)
+    shard_routes = []
+    for r in range(world):
+        b, c = ep_mod.expert_shard(E, world, r)
+        shard_routes.append(sum(int(((x >= b) & (x < b + c)).sum()) for x in ids_all) / len(ids_all))
+    mean_routes = sum(shard_routes) / world
     # publish + gather + the shard's MoE kernels + the final sum
     launches = 2 + sbb.kernels_per_call(world * Tr, ep.expert_count, TOP_K, D, I) + 1
     del graphs
@@ -482,11 +490,15 @@ def run_expert_parallel(args, sbb, rank, world, local):
             "metric": METRIC, "value": T / (ms * 1e-3), "unit": "tokens/s", "n_gpus": world,
             "steps": args.steps, "warmup": args.warmup, "ms_per_step": ms,
             "higher_is_better": True, "scaling": "strong", "vs_baseline": None,
-            "dtype": "nvfp4 W4A16: e2m1 weights x 4-term e2m1 activation split, mxf4nvf4 MMA, "
+            "dtype": ("nvfp4 W4A4: e2m1 weights x e2m1 activations (dynamic per-row globals), "
+                      "mxf4nvf4 MMA, fp32 accumulate") if args.w4a4 else
+                     "nvfp4 W4A16: e2m1 weights x 4-term e2m1 activation split, mxf4nvf4 MMA, "
                      "fp32 accumulate",
             "data": "synthetic",
-            "config": {"workload": f"config1-decode E={E} d={D} I={I} top{TOP_K} T={T}, "
-                                   f"experts sharded over {world} GPUs",
+            "config": {"workload": ("config4-skewed-w4a4" if args.w4a4 else
+                                    "config1-decode" if T <= 64 else "config2-prefill" if T >= 8192
+                                    else "layer") + f" E={E} d={D} I={I} top{TOP_K} T={T} "
+                                   f"routing={routing}, experts sharded over {world} GPUs",
                        "global_batch": T, "tokens_per_gpu": Tr, "parallelism": f"ep{world}",
                        "exchange": "NVLink peer loads/stores (CUDA IPC), no NCCL on the data path",
                        "l2": f"inputs larger than L2: {N_LAYERS} rotating layers of "
@@ -505,6 +517,8 @@ def run_expert_parallel(args, sbb, rank, world, local):
                     "h2d_bytes_per_step": Tr * D * 2 + Tr * TOP_K * 8,
                     "d2h_bytes_per_step": Tr * D * 2, "ms_per_step": e2e_ms},
             "gpu_launches": launches * args.steps,
+            "load_imbalance": {"routes_per_rank": shard_routes,
+                               "max_over_mean": max(shard_routes) / mean_routes if mean_routes else None},
             "device_errors": errors,
             "clocks": clocks,
         }

@@ -116,7 +116,7 @@ def lib() -> ctypes.CDLL:
         L.sbb200_ep_shard.restype = I
         L.sbb200_ep_shard.argtypes = [S, I, I, P, P]
         L.sbb200_ep_create.restype = P
-        L.sbb200_ep_create.argtypes = [I, I, I, S, S, S, S, S, I]
+        L.sbb200_ep_create.argtypes = [I, I, I, S, S, S, S, S, I, I]
         L.sbb200_ep_ipc_handle.restype = I
         L.sbb200_ep_ipc_handle.argtypes = [P, P, S]
         L.sbb200_ep_connect.restype = I

@@ -278,7 +278,7 @@ void ep_shard(size_t E, int world, int rank, size_t* begin, size_t* count) {
 }  // namespace sbb
 
 struct sbb200_ep {
-  int device = 0, rank = 0, world = 1, act_dt = SBB200_BF16;
+  int device = 0, rank = 0, world = 1, act_dt = SBB200_BF16, act_terms = sbb::kSplitTerms;
   size_t max_tokens = 0, top_k = 0, E = 0, K = 0, I = 0, e_begin = 0, e_count = 0;
   sbb::ExLayout lay{};
   char* ex = nullptr;                 // this rank's exchange buffer (IPC-exported)
@@ -336,7 +336,7 @@ int sbb200_ep_shard(size_t E, int world, int rank, size_t* begin, size_t* count)
 }
 
 sbb200_ep_t* sbb200_ep_create(int device, int rank, int world, size_t max_tokens, size_t top_k,
-                              size_t E, size_t K, size_t I, int act_dt) {
+                              size_t E, size_t K, size_t I, int act_dt, int w4a4) {
   try {
     std::string why;
     if (world < 1 || world > sbb::kMaxWorld || rank < 0 || rank >= world) {
@@ -358,6 +358,7 @@ sbb200_ep_t* sbb200_ep_create(int device, int rank, int world, size_t max_tokens
     p->rank = rank;
     p->world = world;
     p->act_dt = act_dt;
+    p->act_terms = w4a4 ? 1 : sbb::kSplitTerms;
     p->max_tokens = max_tokens;
     p->top_k = top_k;
     p->E = E;
@@ -531,6 +532,7 @@ int sbb200_ep_forward_staged(sbb200_ep_t* p, void* stream, const void* hidden,
       a.g2 = w2_global_scales;
       a.out = nullptr;
       a.out_dt = SBB200_F32;
+      a.act_terms = p->act_terms;
       a.M = vt;
       a.E = static_cast<int>(p->e_count);
       a.top_k = static_cast<int>(p->top_k);

@@ -56,14 +56,16 @@ class ExpertParallel:
     (collectively: the constructor swaps handles)."""
 
     def __init__(self, *, rank: int, world: int, device: int, max_tokens: int, top_k: int,
-                 E: int, K: int, I: int, act_dtype: torch.dtype = torch.bfloat16, group=None):
+                 E: int, K: int, I: int, act_dtype: torch.dtype = torch.bfloat16, group=None,
+                 w4a4: bool = False):
         self.rank, self.world, self.E = rank, world, E
         self.max_tokens, self.top_k, self.K, self.I = max_tokens, top_k, K, I
         self.device = torch.device("cuda", device)
         self.act_dtype = act_dtype
         self.expert_begin, self.expert_count = expert_shard(E, world, rank)
+        self.w4a4 = bool(w4a4)
         self.h = lib().sbb200_ep_create(device, rank, world, max_tokens, top_k, E, K, I,
-                                        DTYPE_CODE[act_dtype])
+                                        DTYPE_CODE[act_dtype], int(self.w4a4))
         if not self.h:
             raise Sbb200Error(-1, last_error())
         buf = ctypes.create_string_buffer(HANDLE_BYTES)

@@ -39,7 +39,7 @@ def handles_worker(rank: int, world: int, port: int, q):
         q.put((rank, traceback.format_exc()))
 
 
-def ep_forward_worker(rank: int, world: int, port: int, shape: tuple, steps: list, q):
+def ep_forward_worker(rank: int, world: int, port: int, shape: tuple, steps: list, w4a4: bool, q):
     """Expert-parallel forward on GPU `rank` vs the oracle, several steps."""
     try:
         dist = _init(rank, world, port)
@@ -56,7 +56,7 @@ def ep_forward_worker(rank: int, world: int, port: int, shape: tuple, steps: lis
         E, K, I, top_k, max_tokens = shape
         L = O.make_layer(E, K, I, seed=500)
         ep = ep_mod.ExpertParallel(rank=rank, world=world, device=rank, max_tokens=max_tokens,
-                                   top_k=top_k, E=E, K=K, I=I)
+                                   top_k=top_k, E=E, K=K, I=I, w4a4=w4a4)
         dev = torch.device("cuda", rank)
         b, c = ep.expert_begin, ep.expert_count
         ws = [torch.from_numpy(np.ascontiguousarray(x[b:b + c])).to(dev)
@@ -77,7 +77,8 @@ def ep_forward_worker(rank: int, world: int, port: int, shape: tuple, steps: lis
             torch.cuda.synchronize()
             got = out.cpu().numpy()
             if T:
-                want = O.moe_forward(hidden, ids, w, L)
+                want = (O.moe_forward_w4a4(hidden, ids, w, L) if w4a4
+                        else O.moe_forward(hidden, ids, w, L))
                 results.append((T, rel_err(got, want), cosine(got, want)))
             else:
                 results.append((0, 0.0, 1.0))

@@ -47,11 +47,11 @@ def test_shard_and_create_reject_bad_arguments(sbb, ep):
     with pytest.raises(sbb.Sbb200Error):
         ep.expert_shard(4, 8, 0)  # fewer experts than ranks
     L = sbb.lib()
-    assert not L.sbb200_ep_create(0, 2, 2, 64, 8, 170, 4096, 1280, 2)  # rank >= world
+    assert not L.sbb200_ep_create(0, 2, 2, 64, 8, 170, 4096, 1280, 2, 0)  # rank >= world
     assert "rank" in sbb.last_error()
-    assert not L.sbb200_ep_create(0, 0, 2, 64, 8, 170, 4096 + 32, 1280, 2)  # K % 256
+    assert not L.sbb200_ep_create(0, 0, 2, 64, 8, 170, 4096 + 32, 1280, 2, 0)  # K % 256
     assert "256" in sbb.last_error()
-    assert not L.sbb200_ep_create(0, 0, 2, 0, 8, 170, 4096, 1280, 2)
+    assert not L.sbb200_ep_create(0, 0, 2, 0, 8, 170, 4096, 1280, 2, 0)
     assert "max_tokens" in sbb.last_error()
 
 

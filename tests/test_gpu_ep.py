@@ -25,12 +25,13 @@ def _free_port() -> int:
         return s.getsockname()[1]
 
 
-def _run(world, shape, steps):
+def _run(world, shape, steps, w4a4=False):
     import ep_worker
     ctx = mp.get_context("spawn")
     q = ctx.Queue()
     port = _free_port()
-    procs = [ctx.Process(target=ep_worker.ep_forward_worker, args=(r, world, port, shape, steps, q))
+    procs = [ctx.Process(target=ep_worker.ep_forward_worker,
+                         args=(r, world, port, shape, steps, w4a4, q))
              for r in range(world)]
     for p in procs:
         p.start()
@@ -47,12 +48,24 @@ def _run(world, shape, steps):
     return got
 
 
-@pytest.mark.skipif(torch.cuda.device_count() < 2, reason="needs two GPUs")
-@pytest.mark.parametrize("shape", [(16, 512, 256, 4, 24), (34, 1024, 512, 8, 64)])
-def test_ep_two_ranks_match_oracle(cuda, shape):
-    steps = [(shape[4], shape[4] // 2), (5, 0), (1, shape[4])]
-    got = _run(2, shape, steps)
-    for r in range(2):
+def _steps(world, max_tokens):
+    """Token counts per rank for three steps: ragged, one rank idle, full."""
+    return [tuple(max_tokens - (r * 7) % max_tokens for r in range(world)),
+            tuple(0 if r % 2 else 5 for r in range(world)),
+            tuple(max_tokens for _ in range(world))]
+
+
+@pytest.mark.parametrize("world", [2, 4, 8])
+@pytest.mark.parametrize("shape,w4a4", [((16, 512, 256, 4, 24), False),
+                                        ((34, 1024, 512, 8, 64), False),
+                                        ((34, 1024, 512, 8, 32), True)])
+def test_ep_ranks_match_oracle(cuda, world, shape, w4a4):
+    if torch.cuda.device_count() < world:
+        pytest.skip(f"needs {world} GPUs")
+    if shape[0] < world:
+        pytest.skip("fewer experts than ranks")
+    got = _run(world, shape, _steps(world, shape[4]), w4a4)
+    for r in range(world):
         v = got[r]
         assert isinstance(v, dict), v
         assert v["errors"] == 0
