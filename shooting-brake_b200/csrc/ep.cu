@@ -149,11 +149,9 @@ __global__ void __launch_bounds__(kEpThreads) ep_publish_kernel(
   // last one stores the new one (the store happens after all increments)
   const unsigned long long next = dev->epoch + 1ull;
   __shared__ unsigned int s_last;
+  __threadfence_system();  // each thread's own copies
   __syncthreads();
-  if (threadIdx.x == 0) {
-    __threadfence_system();  // cumulative over the CTA's copies (barrier above)
-    s_last = atomicAdd(&dev->publish_ctr, 1u) == gridDim.x - 1u;
-  }
+  if (threadIdx.x == 0) s_last = atomicAdd(&dev->publish_ctr, 1u) == gridDim.x - 1u;
   __syncthreads();
   if (s_last) {
     __threadfence_system();

@@ -78,3 +78,29 @@ def test_w4a4_zipf_prefill_shape(sbb, oracle, cuda):
     want = oracle.moe_forward_w4a4(hidden[pick], ids[pick], w[pick], L)
     g = got.cpu().numpy()[pick]
     assert rel_err(g, want) <= REL_TOL and cosine(g, want) >= COS_TOL
+
+
+@pytest.mark.gpu
+@pytest.mark.parametrize("w4a4", [False, True])
+def test_sparse_routes_after_dense_call(sbb, oracle, cuda, w4a4):
+    """The shape an expert-parallel shard sees: many rows, few of them routed
+    here (the rest -1), right after a call whose routes filled the
+    workspace. Both calls against the oracle."""
+    import torch
+    from gpu_util import dev, layer_to
+    E, K, I, M, k = 5, 1024, 512, 256, 4
+    L = oracle.make_layer(E, K, I, seed=61)
+    ws = layer_to(L, cuda)
+    hidden = oracle.make_hidden(M, K, seed=62)
+    ids, w = oracle.route_logits(M, E, k, seed=63)
+    sparse = ids.copy()
+    sparse[5:] = -1
+    for case in (ids, sparse):
+        fn = sbb.nvfp4_moe_w4a4 if w4a4 else sbb.nvfp4_moe
+        got = fn(dev(hidden, cuda, torch.bfloat16), dev(case, cuda), dev(w, cuda), *ws)
+        torch.cuda.synchronize()
+        want = (oracle.moe_forward_w4a4(hidden[:8], case[:8], w[:8], L) if w4a4
+                else oracle.moe_forward(hidden[:8], case[:8], w[:8], L))
+        g = got.cpu().numpy()[:8]
+        assert rel_err(g, want) <= REL_TOL, (case is sparse, rel_err(g, want))
+        assert cosine(g, want) >= COS_TOL
