@@ -518,14 +518,20 @@ __device__ __forceinline__ float2 e2m1x2_to_float2(uint32_t byte) {
 constexpr int kSplitThreads = 64;
 constexpr int kSplitChunk = 16 * kSplitThreads;
 
+// CG: read through L2 only. Rows on another GPU are rewritten every step by
+// their owner; an L1 line left from an earlier step on this SM would be
+// stale, so they are never read through L1.
+template <bool CG = false>
 __device__ __forceinline__ void load8(const void* src, int src_dt, int64_t at, float* v) {
   if (src_dt == kF32) {
-    const float4 a = *reinterpret_cast<const float4*>(static_cast<const float*>(src) + at);
-    const float4 b = *reinterpret_cast<const float4*>(static_cast<const float*>(src) + at + 4);
+    const float4* p = reinterpret_cast<const float4*>(static_cast<const float*>(src) + at);
+    const float4 a = CG ? __ldcg(p) : p[0];
+    const float4 b = CG ? __ldcg(p + 1) : p[1];
     v[0] = a.x; v[1] = a.y; v[2] = a.z; v[3] = a.w;
     v[4] = b.x; v[5] = b.y; v[6] = b.z; v[7] = b.w;
   } else {
-    const uint4 w = *reinterpret_cast<const uint4*>(static_cast<const uint16_t*>(src) + at);
+    const uint4* p = reinterpret_cast<const uint4*>(static_cast<const uint16_t*>(src) + at);
+    const uint4 w = CG ? __ldcg(p) : p[0];
     const uint32_t u[4] = {w.x, w.y, w.z, w.w};
 #pragma unroll
     for (int i = 0; i < 4; ++i) {
@@ -613,8 +619,13 @@ __global__ void __launch_bounds__(1024) split_nvfp4_kernel(
   const bool active = blk * 16 < K;
   float v[16];
   if (active) {
-    load8(rsrc, src_dt, rbase + blk * 16, v);
-    load8(rsrc, src_dt, rbase + blk * 16 + 8, v + 8);
+    if (rows.base) {
+      load8<true>(rsrc, src_dt, rbase + blk * 16, v);
+      load8<true>(rsrc, src_dt, rbase + blk * 16 + 8, v + 8);
+    } else {
+      load8(rsrc, src_dt, rbase + blk * 16, v);
+      load8(rsrc, src_dt, rbase + blk * 16 + 8, v + 8);
+    }
   }
   if (gstatic) {
     for (int d = 0; d < ndst; ++d) {
