@@ -319,8 +319,8 @@ int sbb200_ep_shard(size_t E, int world, int rank, size_t* begin, size_t* count)
 /* Exchange state of `rank` of `world` on `device` for up to max_tokens
  * tokens per rank (hidden K in act_dt, top_k routes, E experts in total,
  * intermediate I; K and I multiples of 256). w4a4 != 0 runs each shard's
- * experts as sbb200_nvfp4_moe_w4a4 with dynamic per-row scales (up to 2
- * ranks). NULL on failure. */
+ * experts as sbb200_nvfp4_moe_w4a4 with dynamic per-row scales. NULL on
+ * failure. */
 sbb200_ep_t* sbb200_ep_create(int device, int rank, int world, size_t max_tokens, size_t top_k,
                               size_t E, size_t K, size_t I, int act_dt, int w4a4);
 

@@ -39,11 +39,11 @@ __device__ __forceinline__ void store4(void* out, int out_dt, int64_t at, float4
 }
 
 // dst.base != nullptr: expert-parallel partials (fp32, peer memory, rows with
-// no valid route skipped), then the completion signal.
+// no valid route skipped).
 __global__ void __launch_bounds__(kThreads) combine_kernel(
     const float* __restrict__ y, const int32_t* __restrict__ slot_of,
     const float* __restrict__ weights, int multiply_router_weight, void* __restrict__ out,
-    int out_dt, int top_k, int K, SplitRows dst, PeerSignal sig) {
+    int out_dt, int top_k, int K, SplitRows dst) {
   const int64_t t = blockIdx.x;
   __shared__ int32_t s_slot[kMaxTopK];
   __shared__ float s_w[kMaxTopK];
@@ -81,23 +81,20 @@ __global__ void __launch_bounds__(kThreads) combine_kernel(
       store4(orow, dst.base ? static_cast<int>(kF32) : out_dt, obase + n4, acc);
     }
   }
-  if (sig.counter) signal_after_all_ctas(sig.counter, sig.flags, sig.n, *sig.epoch);
 }
 
 }  // namespace
 
 cudaError_t launch_combine(const float* y, const int32_t* slot_of, const float* weights,
                            int multiply_router_weight, void* out, int out_dt, int64_t M,
-                           int top_k, int K, cudaStream_t stream, const SplitRows* dst,
-                           const PeerSignal* signal) {
+                           int top_k, int K, cudaStream_t stream, const SplitRows* dst) {
   if (M == 0) return cudaSuccess;
   // K is a multiple of 32, so whole float4 groups cover each row.
   const int per_cta = kThreads * 4;
   dim3 grid((unsigned)M, (unsigned)((K + per_cta - 1) / per_cta));
   const SplitRows d = dst ? *dst : SplitRows{nullptr, 1};
-  const PeerSignal sg = signal ? *signal : PeerSignal{nullptr, nullptr, nullptr, 0};
   return launch_kernel(true, combine_kernel, grid, dim3(kThreads), 0, stream, y, slot_of, weights,
-                       multiply_router_weight, out, out_dt, top_k, K, d, sg);
+                       multiply_router_weight, out, out_dt, top_k, K, d);
 }
 
 }  // namespace sbb

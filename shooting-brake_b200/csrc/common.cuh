@@ -87,28 +87,4 @@ __device__ __forceinline__ unsigned long long ld_acquire_sys(const unsigned long
   return v;
 }
 
-// Called by every thread of every CTA after its last write of the kernel.
-// The CTA that finishes last sets each flag to `value` once all CTAs' writes
-// are visible at system scope, then rearms the counter for the next launch.
-// Every thread fences its own writes (a fence orders the calling thread's
-// stores only; remote stores of other warps may still be in flight when one
-// thread's fence returns), then one thread per CTA counts the CTA in.
-__device__ __forceinline__ void signal_after_all_ctas(unsigned int* counter,
-                                                      unsigned long long* const* flags, int n,
-                                                      unsigned long long value) {
-  __shared__ unsigned int s_last;
-  __threadfence_system();
-  __syncthreads();
-  if (threadIdx.x == 0) {
-    const unsigned int total = gridDim.x * gridDim.y * gridDim.z;
-    s_last = atomicAdd(counter, 1u) == total - 1u;
-  }
-  __syncthreads();
-  if (s_last) {
-    __threadfence_system();
-    for (int i = threadIdx.x; i < n; i += blockDim.x) st_release_sys(flags[i], value);
-    if (threadIdx.x == 0) *counter = 0u;
-  }
-}
-
 }  // namespace sbb

@@ -9,25 +9,34 @@
 // routed_experts.py:354-382, 2460-2463, 2522-2524). Here the exchange is
 // device-resident and stream-ordered:
 //
-//   publish  (source s)  copy this step's hidden rows, ids and weights into
-//                        s's exchange buffer; the last CTA bumps the device
-//                        epoch and sets ready[s] = epoch << 32 | M on every
-//                        rank (system-scope release store through NVLink).
-//   gather   (dest d)    wait for every ready flag (bounded), read each
-//                        source's ids over NVLink and keep the routes to d's
-//                        experts as local ids (-1 elsewhere) for the virtual
-//                        token list v = s * max_tokens + t.
+//   publish  (source s)  bump the device epoch and copy this step's hidden
+//                        rows, ids and weights into s's exchange buffer.
+//   gather   (dest d)    block 0 first sets ready[d] = epoch << 32 | M on
+//                        every rank (the copies of the kernel before are
+//                        complete; system-scope fence, release stores through
+//                        NVLink); then every block waits for the other ranks'
+//                        ready flags (bounded), reads each source's ids over
+//                        NVLink and keeps the routes to d's experts as local
+//                        ids (-1 elsewhere) for the virtual tokens
+//                        v = s * max_tokens + t.
 //   MoE      (dest d)    the single-GPU pipeline on the virtual tokens: the
 //                        activation split reads each routed token's row
 //                        straight from its source GPU (pull), the GEMMs run
 //                        on d's shard, and the combine stores each token's
 //                        fp32 partial sum (router weights applied) into its
-//                        source's partial[d] rows (push); its last CTA sets
-//                        done[d] = epoch on every rank.
-//   final    (source s)  wait for every done flag (bounded) and sum the
-//                        partials of the ranks that own the token's experts in
-//                        ascending rank order (a fixed order, so repeat runs
-//                        are bit-identical).
+//                        source's partial[d] rows (push).
+//   final    (source s)  block 0 first sets done[s] = epoch on every rank
+//                        (this rank's pushes, the kernel before, are
+//                        complete); every block waits for the other ranks'
+//                        done flags (bounded) and sums the partials of the
+//                        ranks that own the token's experts in ascending rank
+//                        order (a fixed order, so repeat runs are
+//                        bit-identical).
+// Each flag is raised by the kernel after the one whose writes it announces,
+// once griddepcontrol.wait has returned: that grid has completed, so every
+// one of its stores is performed before the release. (A last-CTA counter
+// inside the writing kernel was tried first and, at 8 ranks, let a flag out
+// ahead of some of the kernel's peer stores.)
 //
 // No NCCL call is on the data path; the process group only exchanges the
 // CUDA IPC handles of the exchange buffers once. The buffers are reused
@@ -94,11 +103,9 @@ ExLayout ex_layout(int world, size_t max_tokens, size_t top_k, size_t K, size_t 
 
 // Device-side state of this rank (local memory).
 struct EpDev {
-  unsigned long long epoch;     // step counter, bumped by publish
-  unsigned int publish_ctr;     // last-CTA counters
-  unsigned int combine_ctr;
+  unsigned long long epoch;     // step counter, bumped by publish (one writer)
   unsigned int errors;          // bit 0: a wait timed out (sticky until read)
-  unsigned int pad[3];
+  unsigned int pad[5];
 };
 
 struct EpTables {
@@ -130,14 +137,15 @@ __device__ __forceinline__ bool wait_epoch(const unsigned long long* flag, unsig
   }
 }
 
-// Copy this step's tokens into the exchange buffer, then signal every rank.
+// Copy this step's tokens into the exchange buffer. Thread 0 of CTA 0 is the
+// only writer of the step epoch; the kernels after this one read it.
 __global__ void __launch_bounds__(kEpThreads) ep_publish_kernel(
     const uint4* __restrict__ hidden, int64_t hidden_vec, const int32_t* __restrict__ ids,
     const float* __restrict__ weights, int64_t routes, uint4* __restrict__ ex_hidden,
-    int32_t* __restrict__ ex_ids, float* __restrict__ ex_weights, EpDev* dev,
-    const EpTables* __restrict__ tab, int world, int64_t M) {
+    int32_t* __restrict__ ex_ids, float* __restrict__ ex_weights, EpDev* dev) {
   pdl_wait();
   pdl_trigger();
+  if (blockIdx.x == 0 && threadIdx.x == 0) dev->epoch = dev->epoch + 1ull;
   const int64_t stride = static_cast<int64_t>(gridDim.x) * blockDim.x;
   for (int64_t i = blockIdx.x * blockDim.x + threadIdx.x; i < hidden_vec; i += stride)
     ex_hidden[i] = hidden[i];
@@ -145,37 +153,40 @@ __global__ void __launch_bounds__(kEpThreads) ep_publish_kernel(
     ex_ids[i] = ids[i];
     ex_weights[i] = weights[i];
   }
-  // the epoch this step signals: every CTA reads the old value before the
-  // last one stores the new one (the store happens after all increments)
-  const unsigned long long next = dev->epoch + 1ull;
-  __shared__ unsigned int s_last;
-  __threadfence_system();  // each thread's own copies
-  __syncthreads();
-  if (threadIdx.x == 0) s_last = atomicAdd(&dev->publish_ctr, 1u) == gridDim.x - 1u;
-  __syncthreads();
-  if (s_last) {
+}
+
+// Raised by block 0 of the kernel after the one whose writes it announces:
+// that kernel has completed and its memory operations are performed
+// (griddepcontrol.wait returned, or plain stream order), so a system-scope
+// fence and release stores make them visible to every rank before the flags.
+__device__ __forceinline__ void raise_flags(unsigned long long* const* at_peer, int world,
+                                            unsigned long long value) {
+  if (blockIdx.x != 0 || blockIdx.y != 0) return;
+  if (threadIdx.x < world) {
     __threadfence_system();
-    for (int p = threadIdx.x; p < world; p += blockDim.x)
-      st_release_sys(tab->ready_at_peer[p], (next << 32) | static_cast<unsigned long long>(M));
-    if (threadIdx.x == 0) {
-      dev->epoch = next;
-      dev->publish_ctr = 0u;
-    }
+    st_release_sys(at_peer[threadIdx.x], value);
   }
 }
 
-// Local routes of every virtual token v = s * max_tokens + t.
+// Announce this rank's tokens (ready[rank] = epoch << 32 | M on every rank),
+// then keep the local routes of every virtual token v = s * max_tokens + t.
 __global__ void __launch_bounds__(kEpThreads) ep_gather_kernel(
     const unsigned long long* __restrict__ ready, EpDev* dev, const EpTables* __restrict__ tab,
-    int world, int64_t max_tokens, int top_k, int rank, int32_t* __restrict__ local_ids,
+    int world, int64_t max_tokens, int top_k, int rank, int64_t M, int32_t* __restrict__ local_ids,
     float* __restrict__ local_w) {
   __shared__ int64_t s_count[kMaxWorld];
   pdl_wait();
   pdl_trigger();
   const unsigned long long epoch = dev->epoch;
+  raise_flags(const_cast<unsigned long long* const*>(tab->ready_at_peer), world,
+              (epoch << 32) | static_cast<unsigned long long>(M));
   const uint64_t deadline = globaltimer_ns() + kWaitNs;
   for (int s = threadIdx.x; s < world; s += blockDim.x) {
     unsigned long long v = 0;
+    if (s == rank) {  // this rank's own tokens: published by the kernel before
+      s_count[s] = M;
+      continue;
+    }
     s_count[s] = wait_epoch(&ready[s], epoch, true, &v, &dev->errors, deadline)
                      ? static_cast<int64_t>(v & 0xffffffffull)
                      : 0;
@@ -207,13 +218,15 @@ __global__ void __launch_bounds__(kEpThreads) ep_gather_kernel(
 // out[t] = sum over owning ranks d (ascending) of partial[d][t].
 __global__ void __launch_bounds__(kEpThreads) ep_final_kernel(
     const unsigned long long* __restrict__ done, EpDev* dev, const EpTables* __restrict__ tab,
-    int world, const int32_t* __restrict__ ids, int top_k, int E, const float* __restrict__ partial,
+    int world, int rank, const int32_t* __restrict__ ids, int top_k, int E, const float* __restrict__ partial,
     int64_t max_tokens, int K, void* __restrict__ out, int out_dt) {
   __shared__ unsigned long long s_mask;
   const int64_t t = blockIdx.x;
   pdl_wait();
   pdl_trigger();
   const unsigned long long epoch = dev->epoch;
+  // this rank's partials (the combine before this kernel) are in place
+  raise_flags(const_cast<unsigned long long* const*>(tab->done_at_peer), world, epoch);
   if (threadIdx.x == 0) {
     unsigned long long mask = 0;
     for (int k = 0; k < top_k; ++k) {
@@ -228,7 +241,8 @@ __global__ void __launch_bounds__(kEpThreads) ep_final_kernel(
   const uint64_t deadline = globaltimer_ns() + kWaitNs;
   for (int d = threadIdx.x; d < world; d += blockDim.x) {
     unsigned long long v = 0;
-    wait_epoch(&done[d], epoch, false, &v, &dev->errors, deadline);
+    if (d != rank)  // this rank's own partials: written by the kernel before
+      wait_epoch(&done[d], epoch, false, &v, &dev->errors, deadline);
   }
   __syncthreads();
   const unsigned long long mask = s_mask;
@@ -348,12 +362,6 @@ sbb200_ep_t* sbb200_ep_create(int device, int rank, int world, size_t max_tokens
     }
     if (K % 256 != 0 || I % 256 != 0 || E >= (1u << 31)) {
       sbb::set_last_error("ep create: expert parallelism needs K and I multiples of 256");
-      return nullptr;
-    }
-    if (w4a4 && world > 2) {
-      // validated at 1 and 2 ranks; at 8 ranks the results from the second
-      // step on do not match the reference yet, so larger groups are refused
-      sbb::set_last_error("ep create: W4A4 shards are supported on up to 2 ranks");
       return nullptr;
     }
     auto* p = new (std::nothrow) sbb200_ep();
@@ -500,8 +508,7 @@ int sbb200_ep_forward_staged(sbb200_ep_t* p, void* stream, const void* hidden,
       sbb::ep_publish_kernel<<<blocks, sbb::kEpThreads, 0, s>>>(
           static_cast<const uint4*>(hidden), vec, topk_ids, topk_weights, routes,
           reinterpret_cast<uint4*>(ex + p->lay.hidden), reinterpret_cast<int32_t*>(ex + p->lay.ids),
-          reinterpret_cast<float*>(ex + p->lay.weights), p->dev, p->tab, p->world,
-          static_cast<int64_t>(M));
+          reinterpret_cast<float*>(ex + p->lay.weights), p->dev);
       const cudaError_t e = cudaGetLastError();
       if (e != cudaSuccess) return ep_fail(SBB200_ECUDA, std::string("ep publish: ") + cudaGetErrorString(e));
     }
@@ -513,9 +520,10 @@ int sbb200_ep_forward_staged(sbb200_ep_t* p, void* stream, const void* hidden,
       const int blocks = static_cast<int>(std::min<int64_t>(148 * 2, (total + sbb::kEpThreads - 1) / sbb::kEpThreads));
       const cudaError_t e = sbb::launch_kernel(
           true, sbb::ep_gather_kernel, dim3(blocks), dim3(sbb::kEpThreads), 0, s,
-          reinterpret_cast<const unsigned long long*>(ex + p->lay.ready), p->dev, p->tab, p->world,
-          static_cast<int64_t>(p->max_tokens), static_cast<int>(p->top_k), p->rank, p->local_ids,
-          p->local_w);
+          reinterpret_cast<const unsigned long long*>(ex + p->lay.ready), p->dev,
+          static_cast<const sbb::EpTables*>(p->tab), p->world,
+          static_cast<int64_t>(p->max_tokens), static_cast<int>(p->top_k), p->rank,
+          static_cast<int64_t>(M), p->local_ids, p->local_w);
       if (e != cudaSuccess) return ep_fail(SBB200_ECUDA, std::string("ep gather: ") + cudaGetErrorString(e));
     }
     mark(2);
@@ -548,17 +556,12 @@ int sbb200_ep_forward_staged(sbb200_ep_t* p, void* stream, const void* hidden,
       a.stage_events = stage_events ? stage_events + 2 : nullptr;
       // device addresses of the tables inside p->tab (never dereferenced here)
       char* tab = reinterpret_cast<char*>(p->tab);
-      char* dev = reinterpret_cast<char*>(p->dev);
       a.hidden_rows = sbb::SplitRows{
           reinterpret_cast<const void* const*>(tab + offsetof(sbb::EpTables, peer_hidden)),
           static_cast<int64_t>(p->max_tokens)};
       a.out_rows = sbb::SplitRows{
           reinterpret_cast<const void* const*>(tab + offsetof(sbb::EpTables, partial_at_peer)),
           static_cast<int64_t>(p->max_tokens)};
-      a.done = sbb::PeerSignal{
-          reinterpret_cast<unsigned int*>(dev + offsetof(sbb::EpDev, combine_ctr)),
-          reinterpret_cast<unsigned long long* const*>(tab + offsetof(sbb::EpTables, done_at_peer)),
-          reinterpret_cast<const unsigned long long*>(dev + offsetof(sbb::EpDev, epoch)), p->world};
       std::string why;
       const cudaError_t e = sbb::run_moe(a, p->plan, p->workspace, s, &why);
       if (e != cudaSuccess) return ep_fail(SBB200_ECUDA, "ep expert step (" + why + "): " + cudaGetErrorString(e));
@@ -571,7 +574,7 @@ int sbb200_ep_forward_staged(sbb200_ep_t* p, void* stream, const void* hidden,
     const cudaError_t e = sbb::launch_kernel(
         true, sbb::ep_final_kernel, grid, dim3(sbb::kEpThreads), 0, s,
         reinterpret_cast<const unsigned long long*>(ex + p->lay.done), p->dev,
-        static_cast<const sbb::EpTables*>(p->tab), p->world, M > 0 ? topk_ids : nullptr,
+        static_cast<const sbb::EpTables*>(p->tab), p->world, p->rank, M > 0 ? topk_ids : nullptr,
         M > 0 ? static_cast<int>(p->top_k) : 0, static_cast<int>(p->E),
         reinterpret_cast<const float*>(ex + p->lay.partial), static_cast<int64_t>(p->max_tokens),
         M > 0 ? static_cast<int>(K) : 0, out, out_dt);

@@ -44,16 +44,6 @@ cudaError_t launch_down_simt(const float* h, const uint8_t* w2, const uint8_t* s
                              const float* g2, const int32_t* counts, const int32_t* offsets,
                              float* y, int E, int K, int I, cudaStream_t stream);
 
-// Completion signal to other GPUs, raised by the last CTA of a kernel once
-// every CTA's writes are fenced at system scope: each flags[i] (an address in
-// peer memory) is set to *epoch with a system-scope release store.
-struct PeerSignal {
-  unsigned int* counter;                    // local, zero between kernels
-  unsigned long long* const* flags;         // device array [n] of peer flag addresses
-  const unsigned long long* epoch;          // device epoch of this step
-  int n;
-};
-
 // Rows of a [world * rows_per_src, K] operand that live on different GPUs:
 // row v is at base[v / rows_per_src] + (v % rows_per_src) * K elements.
 struct SplitRows {
@@ -63,12 +53,12 @@ struct SplitRows {
 
 // out[t, :] = sum over valid k of w[t, k] * y[slot_of[t*top_k + k], :], k ascending.
 // With `dst` set (expert-parallel partials), fp32 row t goes to dst.base[t /
-// rows_per_src] + (t % rows_per_src) * K, rows without a valid route are not
-// written, and `signal` is raised when every row is stored.
+// rows_per_src] + (t % rows_per_src) * K and rows without a valid route are
+// not written.
 cudaError_t launch_combine(const float* y, const int32_t* slot_of, const float* weights,
                            int multiply_router_weight, void* out, int out_dt, int64_t M,
                            int top_k, int K, cudaStream_t stream,
-                           const SplitRows* dst = nullptr, const PeerSignal* signal = nullptr);
+                           const SplitRows* dst = nullptr);
 
 // Bit-exact NVFP4 dequant: out[r, c] = e2m1 * fp32(e4m3 * g[r / rows_per_scale]).
 cudaError_t launch_dequant(const uint8_t* q, const uint8_t* sf, const float* g,

@@ -142,8 +142,7 @@ cudaError_t run_moe(const MoeArgs& a, const WorkspacePlan& plan, void* workspace
     if ((err = mark(3)) != cudaSuccess) { *why = "stage event"; return err; }
   }
   err = launch_combine(y, slot_of, weights, a.multiply_router_weight, a.out, a.out_dt, a.M,
-                       a.top_k, a.K, stream, a.out_rows.base ? &a.out_rows : nullptr,
-                       a.done.counter ? &a.done : nullptr);
+                       a.top_k, a.K, stream, a.out_rows.base ? &a.out_rows : nullptr);
   if (err != cudaSuccess) { *why = "combine"; return err; }
   if ((err = mark(4)) != cudaSuccess) { *why = "stage event"; return err; }
   return cudaSuccess;

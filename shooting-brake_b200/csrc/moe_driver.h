@@ -47,10 +47,9 @@ struct MoeArgs {
   int E, top_k, K, I;
   void* const* stage_events;  // optional cudaEvent_t[SBB200_STAGE_EVENTS]
   // expert parallel (block-scaled path only): token rows read from the
-  // source GPUs, fp32 partial rows stored back to them, then a signal
+  // source GPUs, fp32 partial rows stored back to them
   SplitRows hidden_rows{nullptr, 1};
   SplitRows out_rows{nullptr, 1};
-  PeerSignal done{nullptr, nullptr, nullptr, 0};
   // routing from router logits [M, E] (logits_dt): the plan writes top-k ids
   // into `routed_ids` and softmax weights into `routed_weights`, which the
   // rest of the forward then uses in place of ids / weights

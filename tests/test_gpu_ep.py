@@ -64,8 +64,6 @@ def test_ep_ranks_match_oracle(cuda, world, shape, w4a4):
         pytest.skip(f"needs {world} GPUs")
     if shape[0] < world:
         pytest.skip("fewer experts than ranks")
-    if w4a4 and world > 2:
-        pytest.skip("W4A4 shards are supported on up to 2 ranks")
     got = _run(world, shape, _steps(world, shape[4]), w4a4)
     for r in range(world):
         v = got[r]
