@@ -53,6 +53,8 @@ def parse():
                     help="routing (default: uniform for decode sizes, biased from 1024 tokens)")
     ap.add_argument("--w4a4", action="store_true",
                     help="quantise activations once (W4A4, dynamic per-row globals)")
+    ap.add_argument("--stack", type=int, default=0,
+                    help="run the layer stack of BASELINE config 3 (e.g. 46 layers) per step")
     ap.add_argument("--replicas", action="store_true",
                     help="with N > 1, run N independent single-GPU replicas instead of "
                          "expert parallelism")
@@ -529,6 +531,187 @@ def run_expert_parallel(args, sbb, rank, world, local):
     dist.destroy_process_group()
 
 
+def run_stack(args, sbb, rank, world, local):
+    """a stack of args.stack routed-expert layers (46 ->
+    69.2 GB of NVFP4 weights, independent seeded layers) run back to back per
+    step on T tokens (the attention blocks between the MoE layers are outside
+    this path, so every layer reads the same hidden rows), routing per layer
+    from its own seeded logits. One GPU holds every layer; with N GPUs each
+    layer's experts are sharded (expert parallel, strong scaling: the T
+    tokens split over the ranks). value = T / step time; one CUDA graph per
+    step holds all layers."""
+    import importlib
+
+    import torch
+    device = torch.device("cuda", local)
+    T, Ls = args.tokens, args.stack
+    if T % world:
+        raise SystemExit(f"--tokens {T} must divide evenly over {world} ranks")
+    Tr = T // world
+    routing = args.routing or ("uniform" if T < 1024 else "biased")
+    ep = None
+    if world > 1:
+        ep_mod = importlib.import_module(sbb.__name__ + ".ep")
+        ep = ep_mod.ExpertParallel(rank=rank, world=world, device=local, max_tokens=Tr,
+                                   top_k=TOP_K, E=E, K=D, I=I, w4a4=args.w4a4)
+    layers = []
+    for l in range(Ls):
+        lw = make_layers(device, 1, seed=5000 + l)[0]
+        layers.append(tuple(ep.local_experts(t).contiguous() for t in lw) if ep else lw)
+        del lw
+    torch.cuda.empty_cache()
+    routes, gids = [], []
+    for l in range(Ls):
+        h, ids, w = make_batch(device, T, seed=7000 + l, routing=routing)
+        gids.append(ids.cpu().numpy())
+        routes.append((ids[rank * Tr:(rank + 1) * Tr].contiguous(),
+                       w[rank * Tr:(rank + 1) * Tr].contiguous()))
+        if l == 0:
+            hidden = h[rank * Tr:(rank + 1) * Tr].contiguous()
+    out = torch.empty((Tr, D), dtype=torch.bfloat16, device=device)
+    stream = torch.cuda.current_stream(device)
+
+    def layer(l, x, o):
+        ids, w = routes[l]
+        if ep is not None:
+            return ep.forward(x, ids, w, *layers[l], out=o)
+        if args.w4a4:
+            return sbb.nvfp4_moe_w4a4(x, ids, w, *layers[l], out=o)
+        return sbb._nvfp4_moe_impl(x, ids, w, *layers[l], True, torch.bfloat16, out=o)
+
+    def stack_step():
+        for l in range(Ls):
+            layer(l, hidden, out)
+
+    for _ in range(max(args.warmup, 3)):
+        stack_step()
+    torch.cuda.synchronize()
+    barrier(world)
+    graph = None
+    if not args.eager:
+        cap = torch.cuda.Stream(device)
+        cap.wait_stream(stream)
+        with torch.cuda.stream(cap):
+            stack_step()  # the capture stream's workspace exists before capture
+        torch.cuda.synchronize()
+        barrier(world)
+        graph = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(graph, stream=cap):
+            stack_step()
+        torch.cuda.synchronize()
+        barrier(world)
+        graph.replay()
+    run = graph.replay if graph is not None else stack_step
+    torch.cuda.synchronize()
+    barrier(world)
+    torch.cuda.synchronize()
+    ev0 = torch.cuda.Event(enable_timing=True)
+    ev1 = torch.cuda.Event(enable_timing=True)
+    clk = ClockSampler(local)
+    clk.__enter__()
+    clk.wait_first_sample()
+    ev0.record(stream)
+    for _ in range(args.steps):
+        run()
+    ev1.record(stream)
+    torch.cuda.synchronize()
+    clk.__exit__(None, None, None)
+    barrier(world)
+    ms = max_over_ranks(ev0.elapsed_time(ev1), world) / args.steps
+
+    # end to end: this rank's hidden rows and every layer's routing in from
+    # pinned host memory, the last layer's output back
+    host_h = hidden.cpu().pin_memory()
+    host_r = [(i.cpu().pin_memory(), w.cpu().pin_memory()) for i, w in routes]
+    host_out = torch.empty((Tr, D), dtype=torch.bfloat16).pin_memory()
+    dh = torch.empty_like(hidden)
+    dr = [(torch.empty_like(i), torch.empty_like(w)) for i, w in routes]
+
+    def e2e_step():
+        dh.copy_(host_h, non_blocking=True)
+        for (di, dw), (hi, hw) in zip(dr, host_r):
+            di.copy_(hi, non_blocking=True)
+            dw.copy_(hw, non_blocking=True)
+        for l in range(Ls):
+            ids, w = dr[l]
+            if ep is not None:
+                o = ep.forward(dh, ids, w, *layers[l], out_dtype=torch.bfloat16)
+            elif args.w4a4:
+                o = sbb.nvfp4_moe_w4a4(dh, ids, w, *layers[l], out_dtype=torch.bfloat16)
+            else:
+                o = sbb.nvfp4_moe(dh, ids, w, *layers[l], out_dtype=torch.bfloat16)
+        host_out.copy_(o, non_blocking=True)
+
+    e2e_step()
+    torch.cuda.synchronize()
+    barrier(world)
+    e0 = torch.cuda.Event(enable_timing=True)
+    e1 = torch.cuda.Event(enable_timing=True)
+    e0.record(stream)
+    n_e2e = max(1, args.steps // 2)
+    for _ in range(n_e2e):
+        e2e_step()
+    e1.record(stream)
+    torch.cuda.synchronize()
+    e2e_ms = max_over_ranks(e0.elapsed_time(e1), world) / n_e2e
+    errors = ep.device_errors() if ep is not None else 0
+
+    peaks = {}
+    try:
+        peaks = json.loads((ROOT / "MEASURED_PEAKS.json").read_text())
+    except Exception:
+        pass
+    hbm_peak = float(peaks.get("hbm_gbs", 6650.0))
+    byts = sum(algorithmic_bytes(g, T)[0] for g in gids)
+    per_gpu_gbs = byts / world / (ms * 1e-3) / 1e9
+    fl = 2.0 * T * TOP_K * 3 * I * D * Ls
+    tf_peak = float(peaks.get("bf16_tflops_sustained", 1400.0))
+    tflops = fl / world / (ms * 1e-3) / 1e12
+    roofline = ({"bound": "hbm", "achieved": per_gpu_gbs, "peak": hbm_peak, "unit": "GB/s",
+                 "frac": per_gpu_gbs / hbm_peak} if T < 1024 else
+                {"bound": "tensor", "achieved": tflops, "peak": tf_peak, "unit": "TFLOP/s",
+                 "frac": tflops / tf_peak})
+    roofline.update({"traffic": None, "kernel": f"whole {Ls}-layer stack per GPU",
+                     "peak_source": "measured" if peaks else "fallback"})
+    if ep is not None:
+        per_layer = 2 + sbb.kernels_per_call(world * Tr, ep.expert_count, TOP_K, D, I) + 1
+        ep.close()
+    else:
+        per_layer = sbb.kernels_per_call(T, E, TOP_K, D, I)
+    if rank == 0:
+        line = {
+            "metric": METRIC, "value": T / (ms * 1e-3), "unit": "tokens/s", "n_gpus": world,
+            "steps": args.steps, "warmup": args.warmup, "ms_per_step": ms,
+            "higher_is_better": True, "scaling": "strong" if world > 1 else "weak",
+            "vs_baseline": None,
+            "dtype": "nvfp4 W4A4 (dynamic per-row activation globals)" if args.w4a4 else
+                     "nvfp4 W4A16: e2m1 weights x 4-term e2m1 activation split, mxf4nvf4 MMA, "
+                     "fp32 accumulate",
+            "data": "synthetic",
+            "config": {"workload": f"config3-stack {Ls} layers E={E} d={D} I={I} top{TOP_K} "
+                                   f"T={T} routing={routing}",
+                       "global_batch": T, "tokens_per_gpu": Tr,
+                       "parallelism": f"ep{world}" if world > 1 else "single",
+                       "weights_gb": Ls * E * EXPERT_BYTES / 1e9,
+                       "l2": "inputs larger than L2: every layer's weights are read each step"},
+            "timing": "CUDA graph replay (one graph per stack step)" if graph is not None
+                      else "eager calls",
+            "ms_per_layer": ms / Ls,
+            "roofline": roofline, "cpu_baseline": None,
+            "e2e": {"value": T / (e2e_ms * 1e-3), "unit": "tokens/s",
+                    "h2d_bytes_per_step": Tr * D * 2 + Ls * Tr * TOP_K * 8,
+                    "d2h_bytes_per_step": Tr * D * 2, "ms_per_step": e2e_ms},
+            "gpu_launches": per_layer * Ls * args.steps, "device_errors": errors,
+            "clocks": clk.summary(),
+        }
+        print(json.dumps(line), flush=True)
+    del graph
+    if world > 1:
+        import torch.distributed as dist
+        dist.barrier()
+        dist.destroy_process_group()
+
+
 def main():
     args = parse()
     if args.impl == "reference":
@@ -543,6 +726,9 @@ def main():
     torch.cuda.set_device(device)
     sbb = g.load_package()
     T = args.tokens
+    if args.stack:
+        run_stack(args, sbb, rank, world, local)
+        return
     if world > 1 and not args.replicas:
         run_expert_parallel(args, sbb, rank, world, local)
         return
