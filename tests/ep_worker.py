@@ -61,7 +61,10 @@ def ep_forward_worker(rank: int, world: int, port: int, shape: tuple, steps: lis
         b, c = ep.expert_begin, ep.expert_count
         ws = [torch.from_numpy(np.ascontiguousarray(x[b:b + c])).to(dev)
               for x in (L.w13, L.s13, L.g13, L.w2, L.s2, L.g2)]
-        results = []
+        # every step first, back to back like a serving engine's layers; the
+        # oracle runs afterwards, so host work between steps cannot hold one
+        # rank past another's bounded waits
+        runs = []
         for i, counts in enumerate(steps):
             T = counts[rank]
             seed = 1000 * i + 10 * rank
@@ -74,7 +77,10 @@ def ep_forward_worker(rank: int, world: int, port: int, shape: tuple, steps: lis
             h = torch.from_numpy(np.ascontiguousarray(hidden)).to(dev).view(torch.bfloat16)
             out = ep.forward(h, torch.from_numpy(ids).to(dev), torch.from_numpy(w).to(dev), *ws,
                              out_dtype=torch.float32)
-            torch.cuda.synchronize()
+            runs.append((T, hidden, ids, w, out))
+        torch.cuda.synchronize()
+        results = []
+        for T, hidden, ids, w, out in runs:
             got = out.cpu().numpy()
             if T:
                 want = (O.moe_forward_w4a4(hidden, ids, w, L) if w4a4

@@ -66,9 +66,12 @@ def test_ep_ranks_match_oracle(cuda, world, shape, w4a4):
         pytest.skip("fewer experts than ranks")
     got = _run(world, shape, _steps(world, shape[4]), w4a4)
     for r in range(world):
+        assert isinstance(got[r], dict), got[r]
+    # a rank whose bounded wait gave up computes nothing for the late ranks:
+    # report that first, for every rank
+    assert all(got[r]["errors"] == 0 for r in range(world)), {r: got[r]["errors"] for r in range(world)}
+    for r in range(world):
         v = got[r]
-        assert isinstance(v, dict), v
-        assert v["errors"] == 0
         for T, err, cos in v["results"]:
             if T:
                 assert err <= REL_TOL, (r, T, err)
