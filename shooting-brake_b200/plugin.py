@@ -168,9 +168,15 @@ def register() -> bool:
     global _registered
     try:
         from vllm.model_executor.custom_op import PluggableLayer, op_registry_oot
-        from vllm.model_executor.layers.fused_moe import RoutedExperts  # type: ignore
     except ImportError:
         return False
+    try:  # the module the reference imports it from (routed_experts.py:13)
+        from vllm.model_executor.layers.fused_moe.routed_experts import RoutedExperts
+    except ImportError:
+        try:
+            from vllm.model_executor.layers.fused_moe import RoutedExperts  # type: ignore
+        except ImportError:
+            return False
     if not hasattr(RoutedExperts, "forward_modular"):
         # older vLLM (e.g. 0.22): RoutedExperts is FusedMoE without the
         # modular forward the hook overrides
