@@ -95,3 +95,51 @@ def ep_forward_worker(rank: int, world: int, port: int, shape: tuple, steps: lis
         q.put((rank, {"results": results, "errors": errs}))
     except Exception:
         q.put((rank, traceback.format_exc()))
+
+
+def ep_skip_worker(rank: int, world: int, port: int, q):
+    """One step together, then rank 1 skips a step: rank 0's waits for it
+    must give up after their deadline, raise the error bit and return; the
+    context stays usable (a host synchronise and a device read follow).
+    Rank 1 stays in the group (its memory stays mapped) until rank 0 is done."""
+    try:
+        dist = _init(rank, world, port)
+        import time
+        import numpy as np
+        import torch
+        import __graft_entry__ as g
+        from oracle import nvfp4 as O
+
+        torch.cuda.set_device(rank)
+        sbb = g.load_package()
+        import importlib
+        ep_mod = importlib.import_module(sbb.__name__ + ".ep")
+        E, K, I, top_k, T = 8, 512, 256, 4, 8
+        L = O.make_layer(E, K, I, seed=77)
+        ep = ep_mod.ExpertParallel(rank=rank, world=world, device=rank, max_tokens=T,
+                                   top_k=top_k, E=E, K=K, I=I)
+        dev = torch.device("cuda", rank)
+        b, c = ep.expert_begin, ep.expert_count
+        ws = [torch.from_numpy(np.ascontiguousarray(x[b:b + c])).to(dev)
+              for x in (L.w13, L.s13, L.g13, L.w2, L.s2, L.g2)]
+        hidden = torch.from_numpy(O.make_hidden(T, K, seed=rank)).to(dev).view(torch.bfloat16)
+        ids, w = O.route_logits(T, E, top_k, seed=10 + rank)
+        ids, w = torch.from_numpy(ids).to(dev), torch.from_numpy(w).to(dev)
+        ep.forward(hidden, ids, w, *ws)
+        torch.cuda.synchronize()
+        first = ep.device_errors()
+        dist.barrier()
+        result = {"first": first}
+        if rank == 0:
+            t0 = time.time()
+            ep.forward(hidden, ids, w, *ws)  # rank 1 does not take part
+            torch.cuda.synchronize()
+            result["seconds"] = time.time() - t0
+            result["errors"] = ep.device_errors()
+            result["after"] = float(torch.ones(4, device=dev).sum().item())  # context alive
+        dist.barrier()  # rank 1 leaves only after rank 0's step has ended
+        ep.close()
+        dist.destroy_process_group()
+        q.put((rank, result))
+    except Exception:
+        q.put((rank, traceback.format_exc()))

@@ -76,3 +76,33 @@ def test_ep_ranks_match_oracle(cuda, world, shape, w4a4):
             if T:
                 assert err <= REL_TOL, (r, T, err)
                 assert cos >= COS_TOL, (r, T, cos)
+
+
+@pytest.mark.skipif(torch.cuda.device_count() < 2, reason="needs two GPUs")
+def test_wait_gives_up_when_a_rank_skips_a_step(cuda):
+    """Failure detection without a GPU fault: a rank that skips a step makes
+    the other rank's bounded waits expire; it reports the error bit and its
+    context keeps working."""
+    import ep_worker
+    ctx = mp.get_context("spawn")
+    q = ctx.Queue()
+    port = _free_port()
+    procs = [ctx.Process(target=ep_worker.ep_skip_worker, args=(r, 2, port, q)) for r in range(2)]
+    for p in procs:
+        p.start()
+    got = {}
+    try:
+        for _ in range(2):
+            r, v = q.get(timeout=300)
+            got[r] = v
+    finally:
+        for p in procs:
+            p.join(timeout=60)
+            if p.is_alive():
+                p.kill()
+    for r in range(2):
+        assert isinstance(got[r], dict), got[r]
+        assert got[r]["first"] == 0
+    assert got[0]["errors"] & 1, got[0]
+    assert 1.5 < got[0]["seconds"] < 30, got[0]
+    assert got[0]["after"] == 4.0
