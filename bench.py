@@ -1,6 +1,6 @@
 """Benchmark of the routed-expert NVFP4 MoE layer on B200.
 
-Headline workload (decode-shaped full layer): E=170 routed
+Headline workload (config 1: decode-shaped full layer): E=170 routed
 experts, hidden d=4096, expert intermediate I=1280, top-8, T=64 tokens, NVFP4
 weights (bf16 N(0, 0.02) quantised with per-tensor global amax/(448*6)),
 bf16 N(0, 1) activations, uniform-random top-8 routing with softmax-
@@ -54,7 +54,7 @@ def parse():
     ap.add_argument("--w4a4", action="store_true",
                     help="quantise activations once (W4A4, dynamic per-row globals)")
     ap.add_argument("--stack", type=int, default=0,
-                    help="run the layer stack of BASELINE config 3 (e.g. 46 layers) per step")
+                    help="run a stack of this many layers per step (config 3: 46 layers)")
     ap.add_argument("--replicas", action="store_true",
                     help="with N > 1, run N independent single-GPU replicas instead of "
                          "expert parallelism")
@@ -532,7 +532,7 @@ def run_expert_parallel(args, sbb, rank, world, local):
 
 
 def run_stack(args, sbb, rank, world, local):
-    """a stack of args.stack routed-expert layers (46 ->
+    """Config 3: a stack of args.stack routed-expert layers (46 ->
     69.2 GB of NVFP4 weights, independent seeded layers) run back to back per
     step on T tokens (the attention blocks between the MoE layers are outside
     this path, so every layer reads the same hidden rows), routing per layer

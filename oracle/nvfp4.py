@@ -11,10 +11,10 @@ Contents
   CPU expert tier, ``src/phase7/cpu_expert_capi.h:70-135`` of the reference,
   compiled from its source by ``oracle/Makefile``).
 * A numpy restatement of the NVFP4 quantiser the reference's tests and the
-  BASELINE configs use: vLLM ``ref_nvfp4_quant`` / ``cast_to_fp4``
+  benchmark configurations use: vLLM ``ref_nvfp4_quant`` / ``cast_to_fp4``
   (``vllm/model_executor/layers/quantization/utils/nvfp4_emulation_utils.py``,
   the library the reference's fixtures call, ``src/phase7/nvfp4_testutil.py:53-71``).
-* Seeded generators for the BASELINE configs (weights bf16 N(0, 0.02) quantised
+* Seeded generators for the benchmark configurations (weights bf16 N(0, 0.02) quantised
   with a per-tensor global multiplier ``amax / (448 * 6)``; activations bf16
   N(0, 1); softmax top-k routing renormalised over the selected k).
 * The deterministic known-answer fixture of the reference's device test
@@ -269,7 +269,7 @@ def _quantize_plane(w: np.ndarray) -> tuple[np.ndarray, np.ndarray, np.float32]:
 
 
 def make_layer(E: int, K: int, I: int, seed: int, std: float = 0.02) -> Layer:
-    """BASELINE weights: bf16 N(0, std) per expert gate/up [2I, K] and down
+    """Benchmark weights: bf16 N(0, std) per expert gate/up [2I, K] and down
     [K, I], quantised to NVFP4 with one global per w13 and one per w2."""
     rng = np.random.default_rng(seed)
     w13 = np.empty((E, 2 * I, K // 2), np.uint8)

@@ -6,7 +6,7 @@
 // trust, src/phase7/nvfp4_testutil.py:53-71).
 //
 // Quantise: vLLM ref_nvfp4_quant, the quantiser behind the reference's
-// fixtures and the BASELINE weights. Per 16-element block with quantisation
+// fixtures and the benchmark weights. Per 16-element block with quantisation
 // global G (= 448*6/amax):
 //   scale = clamp(G * (amax_block * fp32(1/6)), -448, 448) -> e4m3 (nearest even)
 //   inv   = 1 / (fp32(e4m3) * (1 / G))

@@ -14,7 +14,7 @@ from the reference's code, never from this repository's oracle:
   device test (src/QuixiCore-XPU/tests/xpu_ops_smoke.cpp:2260-2304 and
   :2454-2510), outputs of the reference's CPU expert tier (sb_cpu_moe_forward)
   and of the test's own fp32 loop (xpu_ops_smoke.cpp:2316-2348, restated).
-* c0.npz -- BASELINE config 0 (E=16, d=1024, I=512, top-2, T=64, seed 0)
+* c0.npz -- benchmark config 0 (E=16, d=1024, I=512, top-2, T=64, seed 0)
   through sb_cpu_moe_forward.
 * expert_planes.npz -- random-byte NVFP4 planes in the style of
   src/phase7/nvfp4_testutil.py:33-51 (all 16 nibble codes, scale exponents

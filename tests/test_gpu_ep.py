@@ -1,6 +1,6 @@
 """Expert parallelism over NVLink on two GPUs: each rank's tokens through the
 sharded layer vs the oracle's single-layer result (tolerance of the
-north_star bar: normwise relative error <= 1e-2, cosine >= 0.9999), over
+parity bar: normwise relative error <= 1e-2, cosine >= 0.9999), over
 several steps with ragged token counts (one rank with none) so the exchange
 buffers are reused. Child processes, one per GPU, gloo for the handle swap
 only; skipped with fewer than two GPUs."""

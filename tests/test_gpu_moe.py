@@ -1,6 +1,6 @@
 """Routed-expert forward on the B200 vs the reference's expert path.
 
-Tolerance: max relative error <= 1e-2, measured as
+Tolerance (the parity bar of this port): max relative error <= 1e-2, measured as
 max|got - want| / max|want|, and cosine >= 0.9999 against the fp32-accumulated
 reference result."""
 

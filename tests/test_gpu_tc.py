@@ -1,4 +1,4 @@
-"""The tcgen05 path at the BASELINE shapes (E=170, d=4096, I=1280, top-8),
+"""The tcgen05 path at the benchmark shapes (E=170, d=4096, I=1280, top-8),
 checked against the CPU oracle on sampled tokens: a token's output depends
 only on its own routes, so a sample checks a full-size batch exactly.
 

@@ -1,6 +1,6 @@
 """W4A4 (activations quantised once to NVFP4 and fed to the block-scaled
 MMA): vLLM's static per-expert a1/a2_gscale + g1/g2_alphas convention, and
-dynamic per-row quantisation, against the oracle's W4A4
+dynamic per-row quantisation (benchmark config 4), against the oracle's W4A4
 path built on the vLLM-pinned quantiser. Bar: normwise relative error <= 1e-2
 and cosine >= 0.9999 against the oracle's W4A4 result."""
 
