@@ -45,6 +45,7 @@
 #include <cudaTypedefs.h>
 #include <cuda_fp8.h>
 
+#include <atomic>
 #include <mutex>
 
 #include "common.cuh"
@@ -728,11 +729,12 @@ cudaError_t launch_gemm(const CUtensorMap& a, const CUtensorMap& sa, const CUten
   int dev = 0;
   cudaError_t err = cudaGetDevice(&dev);
   if (err != cudaSuccess) return err;
-  static bool attr[64] = {};
-  if (dev >= 0 && dev < 64 && !attr[dev]) {
+  // once per device and instantiation; a repeat from a racing thread is harmless
+  static std::atomic<bool> attr[64] = {};
+  if (dev < 0 || dev >= 64 || !attr[dev].load(std::memory_order_acquire)) {
     err = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, C::kSmem);
     if (err != cudaSuccess) return err;
-    attr[dev] = true;
+    if (dev >= 0 && dev < 64) attr[dev].store(true, std::memory_order_release);
   }
   return launch_kernel(true, kern, dim3(grid), dim3(kThreads), C::kSmem, stream, a, sa, b, sb, p);
 }

@@ -15,6 +15,8 @@
 // expert's global offset and the chunk's base within the expert from those
 // rows, then ranks its routes in order with warp match masks. With a single
 // chunk, pass 2 computes the histogram itself and pass 1 is skipped.
+#include <atomic>
+
 #include "common.cuh"
 #include "kernels.h"
 #include "launch.cuh"
@@ -266,12 +268,13 @@ cudaError_t launch_route_plan(const int32_t* ids, int64_t R, int E, int32_t* chu
   int dev = 0;
   cudaError_t err = cudaGetDevice(&dev);
   if (err != cudaSuccess) return err;
-  static bool attr_set[64] = {};
-  if (dev >= 0 && dev < 64 && !attr_set[dev]) {
+  // once per device; a repeat from a racing thread is harmless
+  static std::atomic<bool> attr_set[64] = {};
+  if (dev < 0 || dev >= 64 || !attr_set[dev].load(std::memory_order_acquire)) {
     err = cudaFuncSetAttribute(route_scatter_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                (int)route_scatter_smem(kMaxExperts));
     if (err != cudaSuccess) return err;
-    attr_set[dev] = true;
+    if (dev >= 0 && dev < 64) attr_set[dev].store(true, std::memory_order_release);
   }
   // the first launch of the plan waits for everything before it; later ones
   // overlap their predecessor's tail
