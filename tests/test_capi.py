@@ -95,3 +95,41 @@ def test_codec_validation(sbb):
 
 def test_health_rejects_null(sbb):
     assert sbb.lib().sbb200_health(None, None, None, 0) == -1
+
+
+def test_router_topk_validation(sbb):
+    L = sbb.lib()
+    assert L.sbb200_router_topk(None, None, 7, 4, 8, 2, None, None) == -1  # dtype
+    assert "dtype" in sbb.last_error()
+    assert L.sbb200_router_topk(None, None, 0, 4, 8, 9, None, None) == -1  # top_k > E
+    assert "top_k" in sbb.last_error()
+    assert L.sbb200_router_topk(None, None, 0, 4, 600, 2, None, None) == -1  # E > 512
+    assert L.sbb200_router_topk(None, None, 0, 0, 8, 2, None, None) == 0    # no tokens: no work
+    assert L.sbb200_router_topk(None, None, 0, 4, 8, 2, None, None) == -1  # null pointers
+    assert "null" in sbb.last_error()
+
+
+def test_w4a4_static_scales_come_together(sbb):
+    import ctypes
+    L = sbb.lib()
+    dummy = ctypes.c_void_p(16)
+    args = [None, dummy, dummy, dummy, dummy, dummy, dummy, dummy, dummy, dummy,
+            dummy, None, None, None,   # a13_gscale only: incomplete static set
+            dummy, 1 << 30, dummy, 2, 4, 8, 2, 512, 256, 2, 1, None, 0]
+    assert L.sbb200_nvfp4_moe_w4a4(*args) == -1
+    assert "together" in sbb.last_error()
+
+
+def test_from_logits_validation(sbb):
+    import ctypes
+    L = sbb.lib()
+    d = ctypes.c_void_p(16)
+    base = [None, d, d, 2, d, d, d, d, d, d, d, d, d, 1 << 30, d, 2, 4, 8, 2, 512, 256, 2, 1]
+    bad_dt = list(base)
+    bad_dt[3] = 9
+    assert L.sbb200_nvfp4_moe_from_logits(*bad_dt) == -1
+    assert "dtype" in sbb.last_error()
+    big_k = list(base)
+    big_k[18] = 9  # top_k > E
+    assert L.sbb200_nvfp4_moe_from_logits(*big_k) == -1
+    assert "top_k" in sbb.last_error()
