@@ -198,17 +198,20 @@ def unpack_fp4(packed: np.ndarray) -> np.ndarray:
     return out
 
 
-def quantize_nvfp4(w: np.ndarray, global_quant_scale: float) -> tuple[np.ndarray, np.ndarray]:
+def quantize_nvfp4(w: np.ndarray, global_quant_scale) -> tuple[np.ndarray, np.ndarray]:
     """Restatement of vLLM ``ref_nvfp4_quant`` for a [rows, cols] fp32 matrix.
 
     ``global_quant_scale`` is the checkpoint's ``weight_global_scale``
     (448*6/amax); the dequant multiplier stored beside the weights is its
-    inverse, amax/(448*6). Returns (packed e2m1 [rows, cols/2],
+    inverse, amax/(448*6). A [rows] array gives each row its own global (the
+    same arithmetic per row). Returns (packed e2m1 [rows, cols/2],
     e4m3 block scales [rows, cols/16]) as uint8.
     """
     rows, cols = w.shape
     assert cols % BLOCK == 0
-    G = np.float32(global_quant_scale)
+    G = np.asarray(global_quant_scale, dtype=np.float32)
+    if G.ndim == 1:
+        G = G.reshape(rows, 1, 1)
     x = np.asarray(w, dtype=np.float32).reshape(rows, cols // BLOCK, BLOCK)
     vec_max = np.max(np.abs(x), axis=-1, keepdims=True).astype(np.float32)
     scale = (G * (vec_max * np.float32(1.0 / 6.0))).astype(np.float32)
@@ -456,11 +459,8 @@ def moe_forward_w4a4(hidden_bf16: np.ndarray, ids: np.ndarray, weights: np.ndarr
     out = np.zeros((T, K), np.float64)
 
     def quant_rows(rows: np.ndarray, G: np.ndarray):
-        deq = np.empty_like(rows, dtype=np.float64)
-        for i in range(rows.shape[0]):
-            q, sf = quantize_nvfp4(rows[i:i + 1], float(G[i]))
-            deq[i] = dequant(q, sf, 1.0)[0]
-        return deq
+        q, sf = quantize_nvfp4(rows, G)
+        return dequant(q, sf, 1.0).astype(np.float64)
 
     def dyn_g(rows: np.ndarray) -> np.ndarray:
         amax = np.abs(rows).max(axis=1).astype(np.float32)
