@@ -496,7 +496,7 @@ def run_expert_parallel(args, sbb, rank, world, local):
         shard_routes.append(sum(int(((x >= b) & (x < b + c)).sum()) for x in ids_all) / len(ids_all))
     mean_routes = sum(shard_routes) / world
     # publish + gather + the shard's MoE kernels + the final sum
-    launches = 2 + sbb.kernels_per_call(world * Tr, ep.expert_count, TOP_K, D, I) + 1
+    launches = ep.kernels_per_step()
     del graphs
     if rank == 0:
         line = {
@@ -683,7 +683,7 @@ def run_stack(args, sbb, rank, world, local):
     roofline.update({"traffic": None, "kernel": f"whole {Ls}-layer stack per GPU",
                      "peak_source": "measured" if peaks else "fallback"})
     if ep is not None:
-        per_layer = 2 + sbb.kernels_per_call(world * Tr, ep.expert_count, TOP_K, D, I) + 1
+        per_layer = ep.kernels_per_step()
         ep.close()
     else:
         per_layer = sbb.kernels_per_call(T, E, TOP_K, D, I)

@@ -360,6 +360,11 @@ int sbb200_ep_forward_staged(sbb200_ep_t* ep, void* stream, const void* hidden,
  * another rank passed its 2 s deadline); reads, clears, synchronises. */
 int sbb200_ep_device_errors(sbb200_ep_t* ep, void* stream, uint32_t* errors);
 
+/* Number of kernels one sbb200_ep_forward step launches on its stream
+ * (publish, gather, the shard's expert step, final sum), or -1 for a null
+ * handle. No counterpart in the reference. */
+int sbb200_ep_launches(const sbb200_ep_t* ep);
+
 void sbb200_ep_destroy(sbb200_ep_t* ep);
 
 #ifdef __cplusplus

@@ -127,6 +127,8 @@ def lib() -> ctypes.CDLL:
         L.sbb200_ep_forward_staged.argtypes = [P, P, P, P, P, S, P, P, P, P, P, P, P, I, I, P, S]
         L.sbb200_ep_device_errors.restype = I
         L.sbb200_ep_device_errors.argtypes = [P, P, P]
+        L.sbb200_ep_launches.restype = I
+        L.sbb200_ep_launches.argtypes = [P]
         L.sbb200_ep_destroy.restype = None
         L.sbb200_ep_destroy.argtypes = [P]
         _lib = L
@@ -266,7 +268,8 @@ def kernels_per_call(M: int, E: int, top_k: int, K: int, I: int,
                      act_dtype: torch.dtype = torch.bfloat16) -> int:
     """Kernels of this library one nvfp4_moe call of this shape launches (the
     driver's own count: route plan, activation split, gate/up, SwiGLU split,
-    down, combine on the block-scaled path)."""
+    down, combine on the block-scaled path; up to 1,024 routes the split
+    computes the route plan itself)."""
     return int(lib().sbb200_nvfp4_moe_launches(M, E, top_k, K, I, DTYPE_CODE[act_dtype]))
 
 

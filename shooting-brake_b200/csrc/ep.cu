@@ -596,6 +596,15 @@ int sbb200_ep_forward(sbb200_ep_t* p, void* stream, const void* hidden, const in
                                   multiply_router_weight, nullptr, SBB200_EP_STAGE_EVENTS);
 }
 
+int sbb200_ep_launches(const sbb200_ep_t* p) {
+  if (!p) return -1;
+  // publish + gather, the expert step on world * max_tokens virtual tokens
+  // (rows read from peers, so the route plan is its own kernel), final
+  const int64_t vt = static_cast<int64_t>(p->world) * p->max_tokens;
+  return 2 + sbb::count_launches(vt, static_cast<int>(p->top_k), static_cast<int>(p->K),
+                                 static_cast<int>(p->I), false) + 1;
+}
+
 int sbb200_ep_device_errors(sbb200_ep_t* p, void* stream, uint32_t* errors) {
   if (!p || !errors) return ep_fail(SBB200_EINVAL, "ep errors: null argument");
   DeviceGuard g(p->device);

@@ -11,6 +11,9 @@
 namespace sbb {
 
 constexpr int kRouteChunk = 4096;  // routes per CTA in the route plan
+// Up to this many routes (M * top_k) on the block-scaled path with token rows
+// on this GPU, the activation split computes the route plan itself.
+constexpr int kInlinePlanRoutes = 1024;
 
 // Sets the calling thread's message returned by sbb200_last_error.
 void set_last_error(const std::string& msg);
@@ -84,10 +87,13 @@ struct BsLaunch {
   // static W4A4 (a13_gscale != nullptr): activation quantisation globals and
   // output scales per expert, vLLM's a1/a2_gscale and g1/g2_alphas
   const float *a13_gscale, *a2_gscale, *alpha13, *alpha2;
-  const int32_t* counts;
-  const int32_t* offsets;
-  const int32_t* sorted;
-  const int32_t* slot_of;  // [M*top_k] sorted slot of each route, -1 if dropped
+  int32_t* counts;
+  int32_t* offsets;
+  int32_t* sorted;
+  int32_t* slot_of;  // [M*top_k] sorted slot of each route, -1 if dropped
+  // true: no route plan ran; the activation split writes counts, offsets,
+  // sorted, slot_of and the bad-id count (status[0]) itself
+  bool inline_plan;
   const uint8_t *w13, *s13, *w2, *s2;
   const float *g13, *g2;
   uint8_t* xq;   // [R*NT, K/2]

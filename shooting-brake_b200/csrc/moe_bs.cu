@@ -513,7 +513,8 @@ __device__ __forceinline__ float2 e2m1x2_to_float2(uint32_t byte) {
 // written to output rows i*NT + t; with slot_of (token mode) source row i is
 // token i and its terms go to every route slot the token feeds
 // (slot_of[i*top_k + k], -1 skipped), so a token is split once however many
-// experts it visits, and a token with no slot is not read at all.
+// experts it visits, and a token with no slot is not read at all. In token
+// mode with an InlinePlan the slots are computed here instead of read.
 // Outputs: packed e2m1 [row*NT + t, K/2], e4m3 scales [row*NT + t, K/16] and
 // the dequant global g [row*NT + t].
 constexpr int kSplitThreads = 64;
@@ -578,6 +579,103 @@ __device__ __forceinline__ void quant_block(float* v, float G, float g, uint32_t
   *scale_byte = static_cast<uint8_t>(s8);
 }
 
+// Route plan of a small call (R = gridDim.x * top_k <= kInlinePlanRoutes
+// routes, blockDim = kSplitThreads) computed inside the token-mode split, so
+// no separate plan kernel runs ahead of it. Every CTA histograms all route
+// ids in shared memory and scans the counts into expert offsets; the slot of
+// its token's route r = row * top_k + i with expert e is then offsets[e] +
+// #{r' < r : ids[r'] == e}, the stable (token, k) order of the separate plan
+// (route_scatter_kernel). The CTAs of source chunk 0 write their token's
+// slot_of and sorted entries, CTA (0, 0) also counts, offsets and the
+// number of ids outside [0, E) other than -1.
+struct InlinePlan {
+  const int32_t* ids;  // nullptr: the route plan ran and the split reads its slot_of
+  int E;
+  int32_t* counts;
+  int32_t* offsets;
+  int32_t* sorted;
+  int32_t* slot_of;
+  uint32_t* status;
+};
+constexpr int kInlinePer = kInlinePlanRoutes / kSplitThreads;  // route ids per thread
+
+// s_off: kMaxExperts + 1 entries; s_rank, s_exp, s_dst: top_k entries.
+// Ends with every s_dst entry written and visible to the CTA.
+__device__ __forceinline__ void inline_route_slots(const InlinePlan& plan, int64_t row, int top_k,
+                                                   int32_t* s_off, int32_t* s_rank, int32_t* s_exp,
+                                                   int32_t* s_dst) {
+  const int tid = threadIdx.x;
+  const int lane = tid & 31;
+  const int E = plan.E;
+  const int R = static_cast<int>(gridDim.x) * top_k;
+  const int r0 = static_cast<int>(row) * top_k;
+  for (int e = tid; e <= E; e += blockDim.x) s_off[e] = 0;
+  for (int i = tid; i < top_k; i += blockDim.x) {
+    s_rank[i] = 0;
+    s_exp[i] = plan.ids[r0 + i];
+  }
+  __syncthreads();
+  int32_t mine[kInlinePer];
+  uint32_t bad = 0;
+#pragma unroll
+  for (int j = 0; j < kInlinePer; ++j) {
+    const int r = tid + j * static_cast<int>(blockDim.x);
+    const int32_t e = r < R ? plan.ids[r] : -1;
+    mine[j] = e;
+    if (e >= 0 && e < E) atomicAdd(&s_off[e], 1);
+    else if (e != -1) ++bad;
+  }
+  if (bad && blockIdx.x == 0 && blockIdx.y == 0) atomicAdd(plan.status, bad);
+  // rank of each of the token's routes among the earlier routes of its expert
+  for (int i = 0; i < top_k; ++i) {
+    const int32_t e = s_exp[i];  // the same for every thread of the CTA
+    if (e < 0 || e >= E) continue;
+    int c = 0;
+#pragma unroll
+    for (int j = 0; j < kInlinePer; ++j)
+      c += (mine[j] == e && tid + j * static_cast<int>(blockDim.x) < r0 + i) ? 1 : 0;
+#pragma unroll
+    for (int d = 16; d > 0; d >>= 1) c += __shfl_xor_sync(0xffffffffu, c, d);
+    if (lane == 0 && c) atomicAdd(&s_rank[i], c);
+  }
+  __syncthreads();
+  // exclusive scan of the counts in place: s_off[e] = first slot of expert e,
+  // s_off[E] = valid routes
+  if (tid < 32) {
+    int32_t carry = 0;
+    for (int e0 = 0; e0 <= E; e0 += 32) {
+      const int e = e0 + lane;
+      const int32_t v = e < E ? s_off[e] : 0;
+      int32_t incl = v;
+#pragma unroll
+      for (int d = 1; d < 32; d <<= 1) {
+        const int32_t n = __shfl_up_sync(0xffffffffu, incl, d);
+        if (lane >= d) incl += n;
+      }
+      if (e <= E) s_off[e] = carry + incl - v;
+      carry += __shfl_sync(0xffffffffu, incl, 31);
+    }
+  }
+  __syncthreads();
+  for (int i = tid; i < top_k; i += blockDim.x) {
+    const int32_t e = s_exp[i];
+    const int32_t slot = (e >= 0 && e < E) ? s_off[e] + s_rank[i] : -1;
+    s_dst[i] = slot;
+    if (blockIdx.y == 0) {
+      plan.slot_of[r0 + i] = slot;
+      if (slot >= 0) plan.sorted[slot] = r0 + i;
+    }
+  }
+  if (blockIdx.x == 0 && blockIdx.y == 0) {
+    for (int e = tid; e < E; e += blockDim.x) {
+      plan.counts[e] = s_off[e + 1] - s_off[e];
+      plan.offsets[e] = s_off[e];
+    }
+    if (tid == 0) plan.offsets[E] = s_off[E];
+  }
+  __syncthreads();
+}
+
 // gstatic != nullptr (W4A4 with static activation globals, NT = 1): the
 // block of each destination slot is quantised under gstatic[e] of that
 // slot's expert e (token mode: eids[row * top_k + k]; row mode:
@@ -588,9 +686,12 @@ __global__ void __launch_bounds__(1024) split_nvfp4_kernel(
     const void* __restrict__ src, int src_dt, SplitRows rows, const int32_t* __restrict__ slot_of,
     int top_k, const int32_t* __restrict__ n_rows_dev, int K, int NT, uint8_t* __restrict__ q,
     uint8_t* __restrict__ sf, float* __restrict__ gout, const float* __restrict__ gstatic,
-    const int32_t* __restrict__ eids, const int32_t* __restrict__ sorted) {
+    const int32_t* __restrict__ eids, const int32_t* __restrict__ sorted, const InlinePlan plan) {
   __shared__ float s_max[32];
   __shared__ int32_t s_dst[kMaxTopK];
+  __shared__ int32_t s_off[kMaxExperts + 1];
+  __shared__ int32_t s_rank[kMaxTopK];
+  __shared__ int32_t s_exp[kMaxTopK];
   __shared__ int s_any;
   const int64_t row = blockIdx.x;
   pdl_wait();
@@ -599,12 +700,19 @@ __global__ void __launch_bounds__(1024) split_nvfp4_kernel(
   const int tid = threadIdx.x;
   const int nwarps = blockDim.x >> 5;
   int ndst = 1;
-  if (slot_of) {
+  const bool token = slot_of != nullptr || plan.ids != nullptr;  // token mode
+  if (token) {
     if (tid == 0) s_any = 0;
-    __syncthreads();
-    for (int i = tid; i < top_k; i += blockDim.x) {
-      s_dst[i] = slot_of[row * top_k + i];
-      if (s_dst[i] >= 0) s_any = 1;
+    if (plan.ids) {
+      inline_route_slots(plan, row, top_k, s_off, s_rank, s_exp, s_dst);
+      for (int i = tid; i < top_k; i += blockDim.x)
+        if (s_dst[i] >= 0) s_any = 1;
+    } else {
+      __syncthreads();
+      for (int i = tid; i < top_k; i += blockDim.x) {
+        s_dst[i] = slot_of[row * top_k + i];
+        if (s_dst[i] >= 0) s_any = 1;
+      }
     }
     __syncthreads();
     if (!s_any) return;  // the whole CTA leaves together
@@ -630,9 +738,9 @@ __global__ void __launch_bounds__(1024) split_nvfp4_kernel(
   }
   if (gstatic) {
     for (int d = 0; d < ndst; ++d) {
-      const int64_t dst = slot_of ? static_cast<int64_t>(s_dst[d]) : row;
+      const int64_t dst = token ? static_cast<int64_t>(s_dst[d]) : row;
       if (dst < 0) continue;
-      const int32_t e = slot_of ? eids[row * top_k + d] : eids[sorted[row]];
+      const int32_t e = token ? eids[row * top_k + d] : eids[sorted[row]];
       const float G = gstatic[e];
       if (blockIdx.y == 0 && tid == 0) gout[dst] = 1.0f;
       if (!active) continue;
@@ -670,7 +778,7 @@ __global__ void __launch_bounds__(1024) split_nvfp4_kernel(
   const float G0 = amax > 0.0f ? __fdiv_rn(2688.0f, amax) : 1.0f;
   const float g0 = __fdiv_rn(1.0f, G0);
   if (blockIdx.y == 0 && tid < ndst) {
-    const int64_t dst = slot_of ? static_cast<int64_t>(s_dst[tid]) : row;
+    const int64_t dst = token ? static_cast<int64_t>(s_dst[tid]) : row;
     if (dst >= 0)
       for (int t = 0; t < NT; ++t) gout[dst * NT + t] = ldexpf(g0, -2 * t);
   }
@@ -681,7 +789,7 @@ __global__ void __launch_bounds__(1024) split_nvfp4_kernel(
     uint8_t s8;
     quant_block<true>(v, G, g, w, &s8);
     for (int d = 0; d < ndst; ++d) {
-      const int64_t dst = slot_of ? static_cast<int64_t>(s_dst[d]) : row;
+      const int64_t dst = token ? static_cast<int64_t>(s_dst[d]) : row;
       if (dst < 0) continue;
       const int64_t orow = dst * NT + t;
       *reinterpret_cast<uint2*>(q + orow * (K / 2) + blk * 8) = make_uint2(w[0], w[1]);
@@ -772,21 +880,27 @@ int sm_count() {
   return n;
 }
 
-// slot_of != nullptr: token mode (n_rows source tokens, terms scattered to
-// their route slots); otherwise n_rows rows (device count n_rows_dev when
-// given, n_rows an upper bound).
+// slot_of != nullptr or plan->ids != nullptr: token mode (n_rows source
+// tokens, terms scattered to their route slots); otherwise n_rows rows
+// (device count n_rows_dev when given, n_rows an upper bound). The plan
+// (token rows on this GPU, n_rows * top_k <= kInlinePlanRoutes) makes the
+// split the first kernel of the call, so it is launched without PDL.
 cudaError_t launch_split(const void* src, int src_dt, const SplitRows* rows,
                          const int32_t* slot_of, int top_k, const int32_t* n_rows_dev,
                          int64_t n_rows, int K, int nt, uint8_t* q, uint8_t* sf, float* g,
                          const float* gstatic, const int32_t* eids, const int32_t* sorted,
-                         cudaStream_t stream) {
+                         cudaStream_t stream, const InlinePlan* plan = nullptr) {
   if (n_rows <= 0) return cudaSuccess;
   const SplitRows r = rows ? *rows : SplitRows{nullptr, 1};
+  const InlinePlan ip = plan ? *plan : InlinePlan{};
+  if (ip.ids && (r.base || n_rows * top_k > kInlinePlanRoutes || ip.E > kMaxExperts))
+    return cudaErrorInvalidValue;
   // rows on another GPU: one CTA per row, so each element crosses NVLink once
   const int threads = r.base ? K / 16 : kSplitThreads;
   const dim3 grid(static_cast<unsigned>(n_rows), r.base ? 1 : (K + kSplitChunk - 1) / kSplitChunk);
-  return launch_kernel(true, split_nvfp4_kernel, grid, dim3(threads), 0, stream, src, src_dt, r,
-                       slot_of, top_k, n_rows_dev, K, nt, q, sf, g, gstatic, eids, sorted);
+  return launch_kernel(ip.ids == nullptr, split_nvfp4_kernel, grid, dim3(threads), 0, stream, src,
+                       src_dt, r, ip.ids ? nullptr : slot_of, top_k, n_rows_dev, K, nt, q, sf, g,
+                       gstatic, eids, sorted, ip);
 }
 
 }  // namespace
@@ -863,11 +977,14 @@ cudaError_t launch_moe_bs(const BsLaunch& a, cudaStream_t stream, const char** s
   p2.out_ld = a.K;
   p2.stream_weights = R <= static_cast<int64_t>(a.E) * (bnr2 / NT);
 
-  // 1. split each token once; its terms go to all of its route slots
+  // 1. split each token once; its terms go to all of its route slots (for a
+  //    small call the split also computes the route plan)
   *step = "activation split";
+  const InlinePlan plan{a.inline_plan ? a.ids : nullptr, a.E, a.counts, a.offsets, a.sorted,
+                        a.slot_of, a.status};
   cudaError_t err = launch_split(a.hidden, a.act_dt, &a.hidden_rows, a.slot_of, a.top_k, nullptr,
                                  a.M, a.K, NT, a.xq, a.xsf, a.xg, a.a13_gscale, a.ids, a.sorted,
-                                 stream);
+                                 stream, &plan);
   if (err != cudaSuccess) return err;
   if (a.stage_mark) a.stage_mark(a.stage_ctx, 1);
   // 2. gate/up + SwiGLU

@@ -41,9 +41,15 @@ WorkspacePlan plan_workspace(size_t M, size_t E, size_t top_k, size_t K, size_t 
   return p;
 }
 
-int count_launches(int64_t M, int top_k, int K, int I) {
+bool plan_in_split(int64_t R, int K, int I, bool rows_local, bool from_logits) {
+  return rows_local && !from_logits && R > 0 && R <= kInlinePlanRoutes && bs_supported(K, I);
+}
+
+int count_launches(int64_t M, int top_k, int K, int I, bool rows_local) {
   const int64_t R = M * top_k;
-  const int plan = route_plan_chunks(R) > 1 ? 2 : 1;
+  const int plan = plan_in_split(R, K, I, rows_local, false) ? 0
+                   : route_plan_chunks(R) > 1                 ? 2
+                                                              : 1;
   // block-scaled path: activation split, gate/up, SwiGLU split, down;
   // CUDA-core path: gate/up, down. Both end with the combine.
   const int body = bs_supported(K, I) ? 4 : 2;
@@ -73,9 +79,13 @@ cudaError_t run_moe(const MoeArgs& a, const WorkspacePlan& plan, void* workspace
   if (err != cudaSuccess) { *why = "status clear"; return err; }
   const int32_t* ids = a.router_logits ? a.routed_ids : a.ids;
   const float* weights = a.router_logits ? a.routed_weights : a.weights;
-  err = launch_route_plan(ids, R, a.E, chunk_counts, counts, offsets, sorted, slot_of, status,
-                          stream, a.router_logits, a.logits_dt, a.top_k, a.routed_weights);
-  if (err != cudaSuccess) { *why = "route plan"; return err; }
+  const bool inline_plan = plan_in_split(R, a.K, a.I, a.hidden_rows.base == nullptr,
+                                         a.router_logits != nullptr);
+  if (!inline_plan) {
+    err = launch_route_plan(ids, R, a.E, chunk_counts, counts, offsets, sorted, slot_of, status,
+                            stream, a.router_logits, a.logits_dt, a.top_k, a.routed_weights);
+    if (err != cudaSuccess) { *why = "route plan"; return err; }
+  }
   if (bs_supported(a.K, a.I)) {
     BsLaunch t{};
     t.hidden = a.hidden;
@@ -91,6 +101,7 @@ cudaError_t run_moe(const MoeArgs& a, const WorkspacePlan& plan, void* workspace
     t.offsets = offsets;
     t.sorted = sorted;
     t.slot_of = slot_of;
+    t.inline_plan = inline_plan;
     t.w13 = a.w13;
     t.s13 = a.s13;
     t.w2 = a.w2;

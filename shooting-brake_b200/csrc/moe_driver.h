@@ -68,8 +68,15 @@ struct MoeArgs {
 int validate_shape(size_t M, size_t E, size_t top_k, size_t K, size_t I, int act_dt, int out_dt,
                    std::string* why);
 
-// Kernels (excluding the status memset) one run_moe call enqueues.
-int count_launches(int64_t M, int top_k, int K, int I);
+// True when the activation split computes the route plan itself (no plan
+// kernel): a small call (R = M * top_k routes, at most kInlinePlanRoutes) on
+// the block-scaled path, token rows on this GPU, ids given rather than routed
+// from logits.
+bool plan_in_split(int64_t R, int K, int I, bool rows_local, bool from_logits);
+
+// Kernels (excluding the status memset) one run_moe call enqueues when ids
+// are given; rows_local is false for expert-parallel rows read from peers.
+int count_launches(int64_t M, int top_k, int K, int I, bool rows_local = true);
 
 // Enqueue the whole forward on `stream`. On failure returns the CUDA error and
 // names the failing step in *why.

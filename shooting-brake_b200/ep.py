@@ -114,6 +114,14 @@ class ExpertParallel:
             _check(lib().sbb200_ep_forward_staged(*args, arr, STAGE_EVENTS))
         return out
 
+    def kernels_per_step(self) -> int:
+        """Kernels one forward step launches on this rank (the library's own
+        count: publish, gather, the shard's expert step, final sum)."""
+        n = int(lib().sbb200_ep_launches(self.h))
+        if n < 0:
+            raise RuntimeError("expert-parallel handle is closed")
+        return n
+
     def device_errors(self) -> int:
         """Error bits since the last read (bit 0: a wait for another rank
         timed out); synchronises the current stream."""

@@ -53,6 +53,7 @@ def test_shard_and_create_reject_bad_arguments(sbb, ep):
     assert "256" in sbb.last_error()
     assert not L.sbb200_ep_create(0, 0, 2, 0, 8, 170, 4096, 1280, 2, 0)
     assert "max_tokens" in sbb.last_error()
+    assert L.sbb200_ep_launches(None) == -1
 
 
 def test_handle_exchange_gloo_world2():

@@ -94,16 +94,30 @@ def test_duplicate_experts_and_empty_tokens(sbb, oracle, cuda, K, I):
     assert np.all(got[4:8] == 0)
 
 
-def test_out_of_range_ids_are_dropped_and_counted(sbb, oracle, cuda):
-    E, K, I, T, top_k = 8, 256, 64, 6, 2
+# (256, 64): CUDA-core path; (512, 256): block-scaled path with the route plan
+# computed inside the activation split (up to 1,024 routes) or by its own
+# kernels (1,200 routes)
+@pytest.mark.parametrize("K,I,T", [(256, 64, 6), (512, 256, 6), (512, 256, 300)])
+def test_out_of_range_ids_are_dropped_and_counted(sbb, oracle, cuda, K, I, T):
+    E, top_k = 8, 4
     L = oracle.make_layer(E, K, I, seed=51)
     hidden = oracle.make_hidden(T, K, seed=52)
     ids, w = oracle.route_logits(T, E, top_k, seed=53)
     ids[1, 0] = E
     ids[2, 1] = -4
+    ids[T - 1, 3] = -1  # dropped, not counted
     got = run_moe(sbb, hidden, ids, w, L, cuda)
     check(got, oracle.moe_forward(hidden, ids, w, L))
     assert sbb.nvfp4_moe_bad_ids(cuda) == 2
+
+
+def test_launch_count(sbb, cuda):
+    # block-scaled path: split (+ route plan above 1,024 routes), gate/up,
+    # SwiGLU split, down, combine
+    assert sbb.kernels_per_call(64, 170, 8, 4096, 1280) == 5
+    assert sbb.kernels_per_call(128, 170, 8, 4096, 1280) == 5
+    assert sbb.kernels_per_call(129, 170, 8, 4096, 1280) == 6
+    assert sbb.kernels_per_call(8192, 170, 8, 4096, 1280) == 7  # 16 route-plan chunks
 
 
 def test_custom_op_and_validation(sbb, oracle, cuda):
