@@ -45,6 +45,7 @@
 #include <cudaTypedefs.h>
 #include <cuda_fp8.h>
 
+#include <algorithm>
 #include <atomic>
 #include <mutex>
 
@@ -504,12 +505,11 @@ __device__ __forceinline__ float2 e2m1x2_to_float2(uint32_t byte) {
 }
 
 
-// Splits rows into NT NVFP4 terms. Grid (rows, chunks): each CTA takes
-// 16 * blockDim elements of one source row, one 16-element block per thread,
-// so block maxima need no shuffles and a thread's packed block is one 8-byte
-// store. With several chunks per row every CTA reduces the whole row for the
-// row maximum (re-read from L2); with one chunk (rows read from another GPU,
-// blockDim = K / 16) each element is read once. Without slot_of, row i is
+// Splits rows into NT NVFP4 terms. One CTA per source row, one 16-element
+// block per thread (blockDim: K / 16 rounded up to whole warps, at least
+// kSplitThreads), so block maxima need no shuffles, the row maximum is one
+// CTA reduction of values already in registers, every element is read once
+// and a thread's packed block is one 8-byte store. Without slot_of, row i is
 // written to output rows i*NT + t; with slot_of (token mode) source row i is
 // token i and its terms go to every route slot the token feeds
 // (slot_of[i*top_k + k], -1 skipped), so a token is split once however many
@@ -518,7 +518,6 @@ __device__ __forceinline__ float2 e2m1x2_to_float2(uint32_t byte) {
 // Outputs: packed e2m1 [row*NT + t, K/2], e4m3 scales [row*NT + t, K/16] and
 // the dequant global g [row*NT + t].
 constexpr int kSplitThreads = 64;
-constexpr int kSplitChunk = 16 * kSplitThreads;
 
 // CG: read through L2 only. Rows on another GPU are rewritten every step by
 // their owner; an L1 line left from an earlier step on this SM would be
@@ -580,14 +579,14 @@ __device__ __forceinline__ void quant_block(float* v, float G, float g, uint32_t
 }
 
 // Route plan of a small call (R = gridDim.x * top_k <= kInlinePlanRoutes
-// routes, blockDim = kSplitThreads) computed inside the token-mode split, so
+// routes, blockDim >= kSplitThreads) computed inside the token-mode split, so
 // no separate plan kernel runs ahead of it. Every CTA histograms all route
 // ids in shared memory and scans the counts into expert offsets; the slot of
 // its token's route r = row * top_k + i with expert e is then offsets[e] +
 // #{r' < r : ids[r'] == e}, the stable (token, k) order of the separate plan
-// (route_scatter_kernel). The CTAs of source chunk 0 write their token's
-// slot_of and sorted entries, CTA (0, 0) also counts, offsets and the
-// number of ids outside [0, E) other than -1.
+// (route_scatter_kernel). Each CTA writes its token's slot_of and sorted
+// entries, CTA 0 also counts, offsets and the number of ids outside [0, E)
+// other than -1.
 struct InlinePlan {
   const int32_t* ids;  // nullptr: the route plan ran and the split reads its slot_of
   int E;
@@ -625,7 +624,7 @@ __device__ __forceinline__ void inline_route_slots(const InlinePlan& plan, int64
     if (e >= 0 && e < E) atomicAdd(&s_off[e], 1);
     else if (e != -1) ++bad;
   }
-  if (bad && blockIdx.x == 0 && blockIdx.y == 0) atomicAdd(plan.status, bad);
+  if (bad && blockIdx.x == 0) atomicAdd(plan.status, bad);
   // rank of each of the token's routes among the earlier routes of its expert
   for (int i = 0; i < top_k; ++i) {
     const int32_t e = s_exp[i];  // the same for every thread of the CTA
@@ -661,12 +660,10 @@ __device__ __forceinline__ void inline_route_slots(const InlinePlan& plan, int64
     const int32_t e = s_exp[i];
     const int32_t slot = (e >= 0 && e < E) ? s_off[e] + s_rank[i] : -1;
     s_dst[i] = slot;
-    if (blockIdx.y == 0) {
-      plan.slot_of[r0 + i] = slot;
-      if (slot >= 0) plan.sorted[slot] = r0 + i;
-    }
+    plan.slot_of[r0 + i] = slot;
+    if (slot >= 0) plan.sorted[slot] = r0 + i;
   }
-  if (blockIdx.x == 0 && blockIdx.y == 0) {
+  if (blockIdx.x == 0) {
     for (int e = tid; e < E; e += blockDim.x) {
       plan.counts[e] = s_off[e + 1] - s_off[e];
       plan.offsets[e] = s_off[e];
@@ -724,7 +721,7 @@ __global__ void __launch_bounds__(1024) split_nvfp4_kernel(
     rsrc = rows.base[row / rows.rows_per_src];
     rbase = (row % rows.rows_per_src) * K;
   }
-  const int blk = blockIdx.y * blockDim.x + tid;  // this thread's 16-element block
+  const int blk = tid;  // this thread's 16-element block
   const bool active = blk * 16 < K;
   float v[16];
   if (active) {
@@ -742,7 +739,7 @@ __global__ void __launch_bounds__(1024) split_nvfp4_kernel(
       if (dst < 0) continue;
       const int32_t e = token ? eids[row * top_k + d] : eids[sorted[row]];
       const float G = gstatic[e];
-      if (blockIdx.y == 0 && tid == 0) gout[dst] = 1.0f;
+      if (tid == 0) gout[dst] = 1.0f;
       if (!active) continue;
       float x[16];
 #pragma unroll
@@ -756,18 +753,9 @@ __global__ void __launch_bounds__(1024) split_nvfp4_kernel(
     return;
   }
   float amax = 0.0f;
-  if (gridDim.y == 1) {
-    if (active) {
+  if (active) {
 #pragma unroll
-      for (int i = 0; i < 16; ++i) amax = fmaxf(amax, fabsf(v[i]));
-    }
-  } else {
-    for (int k = tid * 8; k < K; k += blockDim.x * 8) {
-      float v8[8];
-      load8(rsrc, src_dt, rbase + k, v8);
-#pragma unroll
-      for (int i = 0; i < 8; ++i) amax = fmaxf(amax, fabsf(v8[i]));
-    }
+    for (int i = 0; i < 16; ++i) amax = fmaxf(amax, fabsf(v[i]));
   }
 #pragma unroll
   for (int d = 16; d > 0; d >>= 1) amax = fmaxf(amax, __shfl_xor_sync(0xffffffffu, amax, d));
@@ -777,7 +765,7 @@ __global__ void __launch_bounds__(1024) split_nvfp4_kernel(
   for (int w = 1; w < nwarps; ++w) amax = fmaxf(amax, s_max[w]);
   const float G0 = amax > 0.0f ? __fdiv_rn(2688.0f, amax) : 1.0f;
   const float g0 = __fdiv_rn(1.0f, G0);
-  if (blockIdx.y == 0 && tid < ndst) {
+  if (tid < ndst) {
     const int64_t dst = token ? static_cast<int64_t>(s_dst[tid]) : row;
     if (dst >= 0)
       for (int t = 0; t < NT; ++t) gout[dst * NT + t] = ldexpf(g0, -2 * t);
@@ -895,9 +883,10 @@ cudaError_t launch_split(const void* src, int src_dt, const SplitRows* rows,
   const InlinePlan ip = plan ? *plan : InlinePlan{};
   if (ip.ids && (r.base || n_rows * top_k > kInlinePlanRoutes || ip.E > kMaxExperts))
     return cudaErrorInvalidValue;
-  // rows on another GPU: one CTA per row, so each element crosses NVLink once
-  const int threads = r.base ? K / 16 : kSplitThreads;
-  const dim3 grid(static_cast<unsigned>(n_rows), r.base ? 1 : (K + kSplitChunk - 1) / kSplitChunk);
+  if (K % 16 != 0 || K / 16 > 1024) return cudaErrorInvalidValue;
+  // one CTA per row (rows on another GPU then cross NVLink once)
+  const int threads = std::max(kSplitThreads, (K / 16 + 31) / 32 * 32);
+  const dim3 grid(static_cast<unsigned>(n_rows));
   return launch_kernel(ip.ids == nullptr, split_nvfp4_kernel, grid, dim3(threads), 0, stream, src,
                        src_dt, r, ip.ids ? nullptr : slot_of, top_k, n_rows_dev, K, nt, q, sf, g,
                        gstatic, eids, sorted, ip);
