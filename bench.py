@@ -13,6 +13,22 @@ one captured CUDA graph per (layer, batch), as a serving engine replays its
 decode step; the eager time of the same calls is reported beside it, and the
 end-to-end number goes through the public op with host buffers.
 
+Timing: every K-step loop is bracketed by synchronize + barrier +
+synchronize, and starts with one untimed step whose cross-GPU waits (expert
+parallel) line the ranks up on the device, so the first event records after
+every rank has arrived; the loop is repeated enough times to cover about a
+second of device time with nvidia-smi clock samples (the sampler is started
+before the first barrier), the per-rank median is taken, then the maximum
+over ranks.
+
+With one GPU the default run also measures, in the same process, the other
+single-GPU workloads of the benchmark configurations (T = 1, 8, 32 decode;
+T = 8192 prefill; T = 4096 Zipf routing, W4A16 and W4A4), each under
+"workloads" with its own roofline. With N > 1 GPUs it runs expert
+parallelism (170 experts sharded, the T tokens split over the ranks, strong
+scaling) and checks the step's output against this library's single-GPU
+path on the full layer.
+
     python bench.py [--gpus N] [--steps K] [--warmup W] [--tokens T]
     python bench.py --impl reference ...   # the reference's CPU expert tier
 
@@ -23,6 +39,7 @@ from __future__ import annotations
 
 import argparse
 import json
+import math
 import os
 import statistics
 import subprocess
@@ -35,13 +52,15 @@ sys.path.insert(0, str(ROOT))
 
 E, D, I, TOP_K = 170, 4096, 1280, 8
 EXPERT_BYTES = 2 * I * D // 2 + 2 * I * D // 16 + D * I // 2 + D * I // 16 + 8
+W13_EXPERT_BYTES = 2 * I * D // 2 + 2 * I * D // 16 + 4
+W2_EXPERT_BYTES = D * I // 2 + D * I // 16 + 4
 METRIC = "routed-expert tokens/s"
 
 
 def parse():
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
-    ap.add_argument("--steps", type=int, default=2000)
+    ap.add_argument("--steps", type=int, default=50)
     ap.add_argument("--warmup", type=int, default=5)
     ap.add_argument("--tokens", type=int, default=64)
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
@@ -60,6 +79,10 @@ def parse():
                          "expert parallelism")
     ap.add_argument("--layers", type=int, default=4,
                     help="independent layers rotated across steps (>= 2 keeps weights out of L2)")
+    ap.add_argument("--no-extras", action="store_true",
+                    help="single GPU: measure the headline workload only")
+    ap.add_argument("--min-timed-s", type=float, default=1.0,
+                    help="device seconds the repeated K-step loops of the headline cover")
     return ap.parse_args()
 
 
@@ -87,22 +110,23 @@ def barrier(world):
         dist.barrier()
 
 
-def max_over_ranks(v: float, world: int) -> float:
+def reduce_over_ranks(v: float, world: int, op: str = "max") -> float:
     if world == 1:
         return v
     import torch
     import torch.distributed as dist
     t = torch.tensor([v], dtype=torch.float64, device="cuda")
-    dist.all_reduce(t, op=dist.ReduceOp.MAX)
+    dist.all_reduce(t, op=dist.ReduceOp.MAX if op == "max" else dist.ReduceOp.MIN)
     return float(t.item())
+
+
+def max_over_ranks(v: float, world: int) -> float:
+    return reduce_over_ranks(v, world, "max")
 
 
 # --------------------------------------------------------------------------
 # synthetic inputs
 # --------------------------------------------------------------------------
-
-_E2M1_THRESH = None
-
 
 def quantize_plane_torch(w, G):
     """NVFP4 quantisation of a [rows, cols] plane with plain torch ops (vLLM
@@ -213,6 +237,38 @@ def algorithmic_bytes(ids_cpu, T):
     return distinct * EXPERT_BYTES + T * D * 2 + T * TOP_K * 8 + T * D * 2, distinct
 
 
+def default_routing(T):
+    return "uniform" if T < 1024 else "biased"
+
+
+def workload_name(T, routing, w4a4):
+    """The config name both arms print for a single-layer workload."""
+    if T >= 4096 and routing == "zipf":
+        kind = "config4-skewed-w4a4" if w4a4 else "config4-skewed-w4a16"
+    elif T <= 64:
+        kind = "config1-decode"
+    elif T >= 8192:
+        kind = "config2-prefill"
+    else:
+        kind = "layer"
+    if w4a4 and not kind.endswith("w4a4"):
+        kind += "-w4a4"
+    return f"{kind} E={E} d={D} I={I} top{TOP_K} T={T} routing={routing}"
+
+
+def single_config(T, routing, w4a4):
+    """`config` of a single-GPU line; the reference arm prints the same dict."""
+    return {"workload": workload_name(T, routing, w4a4), "global_batch": T,
+            "parallelism": "single", "l2": "inputs larger than L2 (rotating 1.5 GB layers)"}
+
+
+def load_peaks():
+    try:
+        return json.loads((ROOT / "MEASURED_PEAKS.json").read_text())
+    except Exception:
+        return {}
+
+
 # --------------------------------------------------------------------------
 # clocks
 # --------------------------------------------------------------------------
@@ -225,8 +281,11 @@ class ClockSampler:
     def __init__(self, gpu_index: int):
         self.gpu = gpu_index
         self.proc = None
+        self.lines = []
 
-    def __enter__(self):
+    def start(self):
+        """Start nvidia-smi and block until it has printed its first line, so
+        the samples that follow cover what runs next."""
         try:
             self.proc = subprocess.Popen(
                 ["nvidia-smi", "-i", str(self.gpu), f"--query-gpu={self.FIELDS}",
@@ -234,20 +293,14 @@ class ClockSampler:
                 stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True)
         except (FileNotFoundError, OSError):
             self.proc = None
-        return self
-
-    def wait_first_sample(self, timeout=3.0):
-        """Block until nvidia-smi has printed its first line, so the samples
-        that follow cover the timed region."""
-        if self.proc is None or self.proc.stdout is None:
-            return
+            return self
         import select
-        r, _, _ = select.select([self.proc.stdout], [], [], timeout)
+        r, _, _ = select.select([self.proc.stdout], [], [], 3.0)
         if r:
             self.proc.stdout.readline()
+        return self
 
-    def __exit__(self, *exc):
-        self.lines = []
+    def stop(self):
         if self.proc is not None:
             self.proc.terminate()
             try:
@@ -256,6 +309,7 @@ class ClockSampler:
                 self.proc.kill()
                 out, _ = self.proc.communicate()
             self.lines = [ln for ln in out.splitlines() if ln.strip()]
+            self.proc = None
 
     def summary(self):
         sm, smax, reasons = [], None, set()
@@ -276,6 +330,50 @@ class ClockSampler:
             return None
         return {"sm_mhz": statistics.median(sm), "sm_max_mhz": smax, "reasons": sorted(reasons),
                 "samples": len(sm)}
+
+
+# --------------------------------------------------------------------------
+# timing
+# --------------------------------------------------------------------------
+
+class StepTimer:
+    """Device time per step of K-step loops on one stream.
+
+    Each loop: synchronize, barrier, synchronize; one untimed step (in the
+    expert-parallel step its cross-GPU waits hold every rank until all have
+    arrived, so the ranks start the timed steps together on the device);
+    event; K steps; event. Loops are repeated, the per-rank median kept and
+    the maximum over ranks reported. Every rank runs the same number of
+    loops (the count is agreed over the ranks first)."""
+
+    def __init__(self, stream, world):
+        self.stream = stream
+        self.world = world
+
+    def loop_ms(self, run_one, steps):
+        import torch
+        torch.cuda.synchronize()
+        barrier(self.world)
+        torch.cuda.synchronize()
+        ev0 = torch.cuda.Event(enable_timing=True)
+        ev1 = torch.cuda.Event(enable_timing=True)
+        run_one(0)
+        ev0.record(self.stream)
+        for i in range(steps):
+            run_one(i + 1)
+        ev1.record(self.stream)
+        torch.cuda.synchronize()
+        return ev0.elapsed_time(ev1) / steps
+
+    def repeats_for(self, est_ms, steps, seconds, lo=3, hi=200):
+        n = math.ceil(seconds * 1e3 / max(est_ms * steps, 1e-3)) if seconds > 0 else lo
+        return int(max_over_ranks(float(min(hi, max(lo, n))), self.world))
+
+    def run(self, run_one, steps, repeats):
+        per = [self.loop_ms(run_one, steps) for _ in range(repeats)]
+        med = statistics.median(per)
+        return max_over_ranks(med, self.world), {"repeats": repeats, "min_ms": min(per),
+                                                 "max_ms": max(per)}
 
 
 # --------------------------------------------------------------------------
@@ -306,6 +404,14 @@ def cpu_reference_run(layer_host, hidden_bits, ids, w, seconds, max_calls=500, w
                           f"batch each) on one 170-expert layer"), threads, per_call, len(times)
 
 
+def cpu_isa():
+    try:
+        from oracle import nvfp4 as O
+        return O.reference_isa()
+    except Exception:
+        return None
+
+
 def profiled_traffic(T):
     """dram__bytes_read.sum + dram__bytes_write.sum of one gate/up launch,
     from the committed ncu summary of this workload, or None."""
@@ -318,13 +424,6 @@ def profiled_traffic(T):
     return int(m.group(1)) if m else None
 
 
-def workload_name(args, T, routing):
-    """The config name both arms print for a single-layer workload."""
-    kind = ("config4-skewed-w4a4" if args.w4a4 else "config1-decode" if T <= 64 else
-            "config2-prefill" if T >= 8192 else "layer")
-    return f"{kind} E={E} d={D} I={I} top{TOP_K} T={T} routing={routing}"
-
-
 def host_batch(batch):
     """(bf16 bits, ids, weights) numpy copies of a device batch."""
     import torch
@@ -334,7 +433,7 @@ def host_batch(batch):
 
 
 # --------------------------------------------------------------------------
-# main
+# reference arm
 # --------------------------------------------------------------------------
 
 def run_reference_arm(args):
@@ -356,35 +455,54 @@ def run_reference_arm(args):
     device = torch.device("cuda", 0) if torch.cuda.is_available() else torch.device("cpu")
     # the same seeded layer 0 and batch 0 as the B200 arm
     layer_host = layer_to_host(make_layers(device, 1, seed=1000)[0])
-    routing = args.routing or ("uniform" if T < 1024 else "biased")
+    routing = args.routing or default_routing(T)
     hb, ids, w = host_batch(make_batch(device, T, seed=2000, routing=routing))
     # K timed whole-batch calls after W warm-up calls, bounded to a few
     # minutes of host time (the step count actually timed is reported).
     tps, sample, threads, per_call, n = cpu_reference_run(
         layer_host, hb, ids, w, seconds=150.0, max_calls=args.steps, warmup=args.warmup)
+    world = args.gpus
+    config = (single_config(T, routing, args.w4a4) if world == 1 or args.replicas else
+              ep_config(T, routing, args.w4a4, world))
     line = {
         "impl": "reference", "metric": METRIC, "value": tps, "unit": "tokens/s",
         "n_gpus": args.gpus, "steps": n, "steps_requested": args.steps, "warmup": args.warmup,
-        "ms_per_step": per_call * 1e3, "higher_is_better": True, "scaling": "weak",
+        "ms_per_step": per_call * 1e3, "higher_is_better": True,
+        "scaling": "weak" if world == 1 or args.replicas else "strong",
         "vs_baseline": None, "dtype": "f32", "data": "synthetic",
-        "config": {"workload": workload_name(args, T, routing),
-                   "global_batch": T, "parallelism": "host threads"},
+        "config": config,
         "cpu_baseline": {"value": tps, "unit": "tokens/s", "cores": threads,
-                         "kind": "reference", "sample": sample},
+                         "kind": "reference", "sample": sample, "isa": cpu_isa()},
         "e2e": {"value": tps, "unit": "tokens/s", "h2d_bytes_per_step": 0,
                 "d2h_bytes_per_step": 0},
     }
+    if world > 1:
+        line["note"] = ("the reference CPU expert tier on this host's cores runs the whole "
+                        "global batch through all 170 experts")
     if args.w4a4:
         line["note"] = ("the reference CPU expert tier keeps activations in f32 (it has no "
                         "activation quantisation); it is timed on the same layer and routes")
     print(json.dumps(line), flush=True)
 
 
+# --------------------------------------------------------------------------
+# expert parallel
+# --------------------------------------------------------------------------
+
+def ep_config(T, routing, w4a4, world):
+    return {"workload": workload_name(T, routing, w4a4) + f", experts sharded over {world} GPUs",
+            "global_batch": T, "parallelism": f"ep{world}",
+            "l2": "inputs larger than L2 (rotating 1.5 GB layers, sharded)"}
+
+
 def run_expert_parallel(args, sbb, rank, world, local):
     """Expert parallelism over NVLink, strong scaling: the global batch of T
     tokens (config 1) is split evenly over the ranks, the 170 experts are
     sharded contiguously, and every step runs one sbb200_ep_forward per rank.
-    `value` = T / (max over ranks of the per-step time)."""
+    `value` = T / (max over ranks of the per-step time). The output of one
+    step is checked against this library's single-GPU forward of the full
+    layer on the same tokens (itself checked against the CPU oracle by the
+    GPU tests)."""
     import importlib
 
     import torch
@@ -395,14 +513,14 @@ def run_expert_parallel(args, sbb, rank, world, local):
         raise SystemExit(f"--tokens {T} must divide evenly over {world} ranks")
     Tr = T // world
     N_LAYERS = args.layers
-    # identical full layers and global batches on every rank; each keeps its
-    # expert shard and its slice of the tokens
     ep = ep_mod.ExpertParallel(rank=rank, world=world, device=local, max_tokens=Tr, top_k=TOP_K,
                                E=E, K=D, I=I, w4a4=args.w4a4)
-    routing = args.routing or ("uniform" if T < 1024 else "biased")
-    layers = []
-    for lw in make_layers(device, N_LAYERS, seed=1000):
+    routing = args.routing or default_routing(T)
+    layers, full0 = [], None
+    for li, lw in enumerate(make_layers(device, N_LAYERS, seed=1000)):
         layers.append(tuple(ep.local_experts(t).contiguous() for t in lw))
+        if li == 0:
+            full0 = lw  # kept for the single-GPU parity check
         del lw
     torch.cuda.empty_cache()
     gbatches = [make_batch(device, T, seed=2000 + 17 * i, routing=routing)
@@ -410,34 +528,17 @@ def run_expert_parallel(args, sbb, rank, world, local):
     batches = [tuple(x[rank * Tr:(rank + 1) * Tr].contiguous() for x in b) for b in gbatches]
     out = torch.empty((Tr, D), dtype=torch.bfloat16, device=device)
     stream = torch.cuda.current_stream(device)
+    timer = StepTimer(stream, world)
 
     def step(i):
         h, ids, w = batches[i % N_LAYERS]
         ep.forward(h, ids, w, *layers[i % N_LAYERS], out=out)
 
-    def timed(run_one, use_clocks):
-        torch.cuda.synchronize()
-        barrier(world)
-        torch.cuda.synchronize()
-        ev0 = torch.cuda.Event(enable_timing=True)
-        ev1 = torch.cuda.Event(enable_timing=True)
-        clk = ClockSampler(local) if use_clocks else None
-        if clk is not None:
-            clk.__enter__()
-            clk.wait_first_sample()
-        ev0.record(stream)
-        for i in range(args.steps):
-            run_one(i)
-        ev1.record(stream)
-        torch.cuda.synchronize()
-        if clk is not None:
-            clk.__exit__(None, None, None)
-        barrier(world)
-        return max_over_ranks(ev0.elapsed_time(ev1), world) / args.steps, clk
-
     for i in range(max(args.warmup, 3)):
         step(i)
+    est = timer.loop_ms(step, max(args.warmup, 3))
     graphs = []
+    clk = ClockSampler(local)
     if not args.eager:
         cap = torch.cuda.Stream(device)
         cap.wait_stream(stream)
@@ -451,10 +552,17 @@ def run_expert_parallel(args, sbb, rank, world, local):
         barrier(world)
         for i in range(max(args.warmup, 3)):
             graphs[i % N_LAYERS].replay()
-        ms, clk = timed(lambda i: graphs[i % N_LAYERS].replay(), True)
-        eager_ms, _ = timed(step, False)
+        replay = lambda i: graphs[i % N_LAYERS].replay()  # noqa: E731
+        repeats = timer.repeats_for(est, args.steps, args.min_timed_s)
+        clk.start()
+        ms, spread = timer.run(replay, args.steps, repeats)
+        clk.stop()
+        eager_ms, _ = timer.run(step, args.steps, 3)
     else:
-        ms, clk = timed(step, True)
+        repeats = timer.repeats_for(est, args.steps, args.min_timed_s)
+        clk.start()
+        ms, spread = timer.run(step, args.steps, repeats)
+        clk.stop()
         eager_ms = ms
     clocks = clk.summary()
 
@@ -474,18 +582,33 @@ def run_expert_parallel(args, sbb, rank, world, local):
 
     for i in range(max(args.warmup, 3)):
         e2e_step(i)
-    e2e_ms, _ = timed(e2e_step, False)
-    errors = ep.device_errors()
+    e2e_ms, _ = timer.run(e2e_step, args.steps, 3)
+    errors = ep.device_errors() | sbb.device_errors(device)
+
+    # parity: one eager step (layer 0, batch 0) against the single-GPU path
+    # on the full layer and this rank's tokens; every rank takes part
+    h0, ids0, w0 = batches[0]
+    got = ep.forward(h0, ids0, w0, *layers[0], out_dtype=torch.float32)
+    if args.w4a4:
+        want = sbb.nvfp4_moe_w4a4(h0, ids0, w0, *full0, out_dtype=torch.float32)
+    else:
+        want = sbb._nvfp4_moe_impl(h0, ids0, w0, *full0, True, torch.float32)
+    torch.cuda.synchronize()
+    errors |= ep.device_errors() | sbb.device_errors(device)
+    diff = float((got.double() - want.double()).abs().max())
+    scale = float(want.double().abs().max())
+    cos = float(torch.nn.functional.cosine_similarity(got.double().flatten(),
+                                                      want.double().flatten(), dim=0))
+    max_rel = reduce_over_ranks(diff / max(scale, 1e-30), world, "max")
+    min_cos = reduce_over_ranks(cos, world, "min")
+    all_errors = int(reduce_over_ranks(float(errors), world, "max"))
+    del full0
 
     ids_all = [b[1].cpu().numpy() for b in gbatches]
     byts = [algorithmic_bytes(x, T) for x in ids_all]
     avg_bytes = sum(b for b, _ in byts) / len(byts)
     avg_distinct = sum(d for _, d in byts) / len(byts)
-    peaks = {}
-    try:
-        peaks = json.loads((ROOT / "MEASURED_PEAKS.json").read_text())
-    except Exception:
-        pass
+    peaks = load_peaks()
     hbm_peak = float(peaks.get("hbm_gbs", 6650.0))
     peak_src = "measured" if "hbm_gbs" in peaks else "fallback"
     per_gpu = avg_bytes / world / (ms * 1e-3) / 1e9
@@ -495,28 +618,27 @@ def run_expert_parallel(args, sbb, rank, world, local):
         b, c = ep_mod.expert_shard(E, world, r)
         shard_routes.append(sum(int(((x >= b) & (x < b + c)).sum()) for x in ids_all) / len(ids_all))
     mean_routes = sum(shard_routes) / world
-    # publish + gather + the shard's MoE kernels + the final sum
     launches = ep.kernels_per_step()
     del graphs
     if rank == 0:
+        valid = all_errors == 0 and max_rel <= 1e-2 and min_cos >= 0.9999
         line = {
-            "metric": METRIC, "value": T / (ms * 1e-3), "unit": "tokens/s", "n_gpus": world,
-            "steps": args.steps, "warmup": args.warmup, "ms_per_step": ms,
+            "metric": METRIC, "value": T / (ms * 1e-3) if valid else None, "unit": "tokens/s",
+            "n_gpus": world, "steps": args.steps, "warmup": args.warmup, "ms_per_step": ms,
             "higher_is_better": True, "scaling": "strong", "vs_baseline": None,
             "dtype": ("nvfp4 W4A4: e2m1 weights x e2m1 activations (dynamic per-row globals), "
                       "mxf4nvf4 MMA, fp32 accumulate") if args.w4a4 else
                      "nvfp4 W4A16: e2m1 weights x 4-term e2m1 activation split, mxf4nvf4 MMA, "
                      "fp32 accumulate",
             "data": "synthetic",
-            "config": {"workload": workload_name(args, T, routing)
-                                   + f", experts sharded over {world} GPUs",
-                       "global_batch": T, "tokens_per_gpu": Tr, "parallelism": f"ep{world}",
-                       "exchange": "NVLink peer loads/stores (CUDA IPC), no NCCL on the data path",
-                       "l2": f"inputs larger than L2: {N_LAYERS} rotating layers of "
-                             f"{E * EXPERT_BYTES / 1e9:.2f} GB sharded",
-                       "distinct_experts_avg": avg_distinct,
-                       "algorithmic_bytes_per_step": avg_bytes},
-            "timing": "CUDA graph replay" if not args.eager else "eager calls",
+            "config": ep_config(T, routing, args.w4a4, world),
+            "tokens_per_gpu": Tr,
+            "exchange": "NVLink peer loads/stores (CUDA IPC), no NCCL on the data path",
+            "distinct_experts_avg": avg_distinct, "algorithmic_bytes_per_step": avg_bytes,
+            "timing": ("CUDA graph replay" if not args.eager else "eager calls")
+                      + f"; median of {spread['repeats']} loops of {args.steps} steps, each after "
+                        "one untimed step that lines the ranks up on the device; max over ranks",
+            "loop_spread_ms": spread,
             "eager_ms_per_step": eager_ms,
             "roofline": {"bound": "hbm", "achieved": per_gpu, "peak": hbm_peak, "unit": "GB/s",
                          "frac": per_gpu / hbm_peak, "traffic": None,
@@ -530,15 +652,24 @@ def run_expert_parallel(args, sbb, rank, world, local):
             "gpu_launches": launches * args.steps,
             "load_imbalance": {"routes_per_rank": shard_routes,
                                "max_over_mean": max(shard_routes) / mean_routes if mean_routes else None},
-            "device_errors": errors,
+            "parity": {"vs": "this library's single-GPU forward of the full layer on the same "
+                             "tokens (fp32 out), layer 0 batch 0, every rank",
+                       "max_rel": max_rel, "cos": min_cos, "bar": "max_rel <= 1e-2, cos >= 0.9999"},
+            "device_errors": all_errors,
             "clocks": clocks,
         }
+        if not valid:
+            line["invalid"] = "device error bits set or parity outside the bar; no value reported"
         print(json.dumps(line), flush=True)
     ep.close()
     import torch.distributed as dist
     dist.barrier()
     dist.destroy_process_group()
 
+
+# --------------------------------------------------------------------------
+# config 3: layer stack
+# --------------------------------------------------------------------------
 
 def run_stack(args, sbb, rank, world, local):
     """Config 3: a stack of args.stack routed-expert layers (46 ->
@@ -557,7 +688,7 @@ def run_stack(args, sbb, rank, world, local):
     if T % world:
         raise SystemExit(f"--tokens {T} must divide evenly over {world} ranks")
     Tr = T // world
-    routing = args.routing or ("uniform" if T < 1024 else "biased")
+    routing = args.routing or default_routing(T)
     ep = None
     if world > 1:
         ep_mod = importlib.import_module(sbb.__name__ + ".ep")
@@ -579,6 +710,7 @@ def run_stack(args, sbb, rank, world, local):
             hidden = h[rank * Tr:(rank + 1) * Tr].contiguous()
     out = torch.empty((Tr, D), dtype=torch.bfloat16, device=device)
     stream = torch.cuda.current_stream(device)
+    timer = StepTimer(stream, world)
 
     def layer(l, x, o):
         ids, w = routes[l]
@@ -588,7 +720,7 @@ def run_stack(args, sbb, rank, world, local):
             return sbb.nvfp4_moe_w4a4(x, ids, w, *layers[l], out=o)
         return sbb._nvfp4_moe_impl(x, ids, w, *layers[l], True, torch.bfloat16, out=o)
 
-    def stack_step():
+    def stack_step(_i=0):
         for l in range(Ls):
             layer(l, hidden, out)
 
@@ -610,23 +742,12 @@ def run_stack(args, sbb, rank, world, local):
         torch.cuda.synchronize()
         barrier(world)
         graph.replay()
-    run = graph.replay if graph is not None else stack_step
-    torch.cuda.synchronize()
-    barrier(world)
-    torch.cuda.synchronize()
-    ev0 = torch.cuda.Event(enable_timing=True)
-    ev1 = torch.cuda.Event(enable_timing=True)
-    clk = ClockSampler(local)
-    clk.__enter__()
-    clk.wait_first_sample()
-    ev0.record(stream)
-    for _ in range(args.steps):
-        run()
-    ev1.record(stream)
-    torch.cuda.synchronize()
-    clk.__exit__(None, None, None)
-    barrier(world)
-    ms = max_over_ranks(ev0.elapsed_time(ev1), world) / args.steps
+    run = (lambda _i: graph.replay()) if graph is not None else stack_step
+    est = timer.loop_ms(run, 1)
+    repeats = timer.repeats_for(est, args.steps, 0.0, lo=3, hi=3)
+    clk = ClockSampler(local).start()
+    ms, spread = timer.run(run, args.steps, repeats)
+    clk.stop()
 
     # end to end: this rank's hidden rows and every layer's routing in from
     # pinned host memory, the last layer's output back
@@ -636,7 +757,7 @@ def run_stack(args, sbb, rank, world, local):
     dh = torch.empty_like(hidden)
     dr = [(torch.empty_like(i), torch.empty_like(w)) for i, w in routes]
 
-    def e2e_step():
+    def e2e_step(_i=0):
         dh.copy_(host_h, non_blocking=True)
         for (di, dw), (hi, hw) in zip(dr, host_r):
             di.copy_(hi, non_blocking=True)
@@ -652,24 +773,12 @@ def run_stack(args, sbb, rank, world, local):
         host_out.copy_(o, non_blocking=True)
 
     e2e_step()
-    torch.cuda.synchronize()
-    barrier(world)
-    e0 = torch.cuda.Event(enable_timing=True)
-    e1 = torch.cuda.Event(enable_timing=True)
-    e0.record(stream)
     n_e2e = max(1, args.steps // 2)
-    for _ in range(n_e2e):
-        e2e_step()
-    e1.record(stream)
-    torch.cuda.synchronize()
-    e2e_ms = max_over_ranks(e0.elapsed_time(e1), world) / n_e2e
-    errors = ep.device_errors() if ep is not None else 0
+    e2e_ms, _ = timer.run(e2e_step, n_e2e, 1)
+    errors = (ep.device_errors() if ep is not None else 0) | sbb.device_errors(device)
+    errors = int(reduce_over_ranks(float(errors), world, "max"))
 
-    peaks = {}
-    try:
-        peaks = json.loads((ROOT / "MEASURED_PEAKS.json").read_text())
-    except Exception:
-        pass
+    peaks = load_peaks()
     hbm_peak = float(peaks.get("hbm_gbs", 6650.0))
     byts = sum(algorithmic_bytes(g, T)[0] for g in gids)
     per_gpu_gbs = byts / world / (ms * 1e-3) / 1e9
@@ -689,7 +798,8 @@ def run_stack(args, sbb, rank, world, local):
         per_layer = sbb.kernels_per_call(T, E, TOP_K, D, I)
     if rank == 0:
         line = {
-            "metric": METRIC, "value": T / (ms * 1e-3), "unit": "tokens/s", "n_gpus": world,
+            "metric": METRIC, "value": T / (ms * 1e-3) if errors == 0 else None,
+            "unit": "tokens/s", "n_gpus": world,
             "steps": args.steps, "warmup": args.warmup, "ms_per_step": ms,
             "higher_is_better": True, "scaling": "strong" if world > 1 else "weak",
             "vs_baseline": None,
@@ -699,12 +809,12 @@ def run_stack(args, sbb, rank, world, local):
             "data": "synthetic",
             "config": {"workload": f"config3-stack {Ls} layers E={E} d={D} I={I} top{TOP_K} "
                                    f"T={T} routing={routing}",
-                       "global_batch": T, "tokens_per_gpu": Tr,
+                       "global_batch": T,
                        "parallelism": f"ep{world}" if world > 1 else "single",
-                       "weights_gb": Ls * E * EXPERT_BYTES / 1e9,
                        "l2": "inputs larger than L2: every layer's weights are read each step"},
-            "timing": "CUDA graph replay (one graph per stack step)" if graph is not None
-                      else "eager calls",
+            "tokens_per_gpu": Tr, "weights_gb": Ls * E * EXPERT_BYTES / 1e9,
+            "timing": ("CUDA graph replay (one graph per stack step)" if graph is not None
+                       else "eager calls") + f"; median of {spread['repeats']} loops",
             "ms_per_layer": ms / Ls,
             "roofline": roofline, "cpu_baseline": None,
             "e2e": {"value": T / (e2e_ms * 1e-3), "unit": "tokens/s",
@@ -721,192 +831,192 @@ def run_stack(args, sbb, rank, world, local):
         dist.destroy_process_group()
 
 
-def main():
-    args = parse()
-    if args.impl == "reference":
-        run_reference_arm(args)
-        return
-    import numpy as np
-    import torch
-    import __graft_entry__ as g
+# --------------------------------------------------------------------------
+# single GPU
+# --------------------------------------------------------------------------
 
-    rank, world, local = dist_init()
-    device = torch.device("cuda", local)
-    torch.cuda.set_device(device)
-    sbb = g.load_package()
-    T = args.tokens
-    if args.stack:
-        run_stack(args, sbb, rank, world, local)
-        return
-    if world > 1 and not args.replicas:
-        run_expert_parallel(args, sbb, rank, world, local)
-        return
+class LayerBench:
+    """One single-GPU workload (T tokens, routing, W4A16 or W4A4) over the
+    shared rotating layers: graph replay timing, eager timing, per-stage
+    events for the dominant kernel."""
 
-    N_LAYERS = args.layers
-    routing = args.routing or ("uniform" if T < 1024 else "biased")
-    layers = make_layers(device, N_LAYERS, seed=1000 + rank)
-    batches = [make_batch(device, T, seed=2000 + 17 * i + rank, routing=routing)
-               for i in range(N_LAYERS)]
-    out = torch.empty((T, D), dtype=torch.bfloat16, device=device)
-    stream = torch.cuda.current_stream(device)
+    def __init__(self, sbb, device, layers, T, routing, w4a4, args, seed_base=2000):
+        import torch
+        self.sbb, self.device, self.layers = sbb, device, layers
+        self.T, self.routing, self.w4a4, self.args = T, routing, w4a4, args
+        self.n = len(layers)
+        self.batches = [make_batch(device, T, seed=seed_base + 17 * i, routing=routing)
+                        for i in range(self.n)]
+        self.out = torch.empty((T, D), dtype=torch.bfloat16, device=device)
+        self.stream = torch.cuda.current_stream(device)
+        self.timer = StepTimer(self.stream, 1)
 
-    def forward(h, ids, w, lw, out=None, stage_events=None, out_dtype=torch.bfloat16):
-        if args.w4a4:
-            return sbb.nvfp4_moe_w4a4(h, ids, w, *lw, out_dtype=out_dtype, out=out,
-                                      stage_events=stage_events)
+    def forward(self, h, ids, w, lw, out=None, stage_events=None, out_dtype=None):
+        import torch
+        out_dtype = out_dtype or torch.bfloat16
+        if self.w4a4:
+            return self.sbb.nvfp4_moe_w4a4(h, ids, w, *lw, out_dtype=out_dtype, out=out,
+                                           stage_events=stage_events)
         if out is None and stage_events is None:
-            return sbb.nvfp4_moe(h, ids, w, *lw, out_dtype=out_dtype)  # the public custom op
-        return sbb._nvfp4_moe_impl(h, ids, w, *lw, True, out_dtype, out=out,
-                                   stage_events=stage_events)
+            return self.sbb.nvfp4_moe(h, ids, w, *lw, out_dtype=out_dtype)  # the public op
+        return self.sbb._nvfp4_moe_impl(h, ids, w, *lw, True, out_dtype, out=out,
+                                        stage_events=stage_events)
 
-    def step(i):
-        h, ids, w = batches[i % N_LAYERS]
-        forward(h, ids, w, layers[i % N_LAYERS], out=out)
+    def step(self, i):
+        h, ids, w = self.batches[i % self.n]
+        self.forward(h, ids, w, self.layers[i % self.n], out=self.out)
 
-    def timed(run_one, use_clocks):
-        """Per-step ms of args.steps calls, bracketed by barrier + synchronize,
-        max over ranks; optionally with nvidia-smi clocks sampled throughout."""
-        torch.cuda.synchronize()
-        barrier(world)
-        torch.cuda.synchronize()
-        ev0 = torch.cuda.Event(enable_timing=True)
-        ev1 = torch.cuda.Event(enable_timing=True)
-        clk = ClockSampler(local) if use_clocks else None
+    def measure(self, steps, warmup, seconds, clk=None, eager=False):
+        import torch
+        for i in range(max(warmup, 3)):
+            self.step(i)
+        est = self.timer.loop_ms(self.step, max(warmup, 3))
+        self.graphs = []
+        if not eager:
+            cap = torch.cuda.Stream(self.device)
+            cap.wait_stream(self.stream)
+            with torch.cuda.stream(cap):
+                for i in range(self.n):
+                    self.step(i)  # the capture stream's workspace exists before capture
+            torch.cuda.synchronize()
+            for i in range(self.n):
+                gr = torch.cuda.CUDAGraph()
+                with torch.cuda.graph(gr, stream=cap):
+                    self.step(i)
+                self.graphs.append(gr)
+            for i in range(max(warmup, 3)):
+                self.graphs[i % self.n].replay()
+            run = lambda i: self.graphs[i % self.n].replay()  # noqa: E731
+        else:
+            run = self.step
+        repeats = self.timer.repeats_for(est, steps, seconds)
         if clk is not None:
-            clk.__enter__()
-            clk.wait_first_sample()
-        ev0.record(stream)
-        for i in range(args.steps):
-            run_one(i)
-        ev1.record(stream)
-        torch.cuda.synchronize()
+            clk.start()
+        ms, spread = self.timer.run(run, steps, repeats)
         if clk is not None:
-            clk.__exit__(None, None, None)
-        barrier(world)
-        return max_over_ranks(ev0.elapsed_time(ev1), world) / args.steps, clk
-
-    # ---- device-resident timing: one CUDA graph per (layer, batch) holding
-    # the same kernel launches an eager call makes -------------------------
-    for i in range(max(args.warmup, 3)):
-        step(i)
-    graphs = []
-    if not args.eager:
-        cap = torch.cuda.Stream(device)
-        cap.wait_stream(stream)
-        with torch.cuda.stream(cap):
-            for i in range(N_LAYERS):
-                step(i)  # the capture stream's workspace exists before capture
+            clk.stop()
+        eager_ms = ms if eager else self.timer.run(self.step, steps, 3)[0]
+        self.graphs = []
+        # per-stage timing: the same calls with the C-ABI's stage events
+        # recorded on the launching stream
+        evsets = [self.sbb.stage_events(self.stream) for _ in range(steps)]
         torch.cuda.synchronize()
-        for i in range(N_LAYERS):
-            gr = torch.cuda.CUDAGraph()
-            with torch.cuda.graph(gr, stream=cap):
-                step(i)
-            graphs.append(gr)
-        for i in range(max(args.warmup, 3)):
-            graphs[i % N_LAYERS].replay()
-        ms, clk = timed(lambda i: graphs[i % N_LAYERS].replay(), True)
-        eager_ms, _ = timed(step, False)
-    else:
-        ms, clk = timed(step, True)
-        eager_ms = ms
+        for i in range(steps):
+            h, ids, w = self.batches[i % self.n]
+            self.forward(h, ids, w, self.layers[i % self.n], out=self.out,
+                         stage_events=evsets[i])
+        torch.cuda.synchronize()
+        stage_ms = {name: statistics.mean(evs[j].elapsed_time(evs[j + 1]) for evs in evsets)
+                    for j, name in enumerate(self.sbb.STAGE_NAMES)}
+        return ms, eager_ms, spread, stage_ms
+
+    def roofline(self, ms, stage_ms, peaks):
+        """Dominant-kernel roofline (the gate/up GEMM): HBM for decode sizes,
+        tensor pipe from 1,024 tokens."""
+        T = self.T
+        ids_all = [b[1].cpu().numpy() for b in self.batches]
+        byts = [algorithmic_bytes(x, T) for x in ids_all]
+        avg_bytes = sum(b for b, _ in byts) / len(byts)
+        avg_distinct = sum(d for _, d in byts) / len(byts)
+        hbm_peak = float(peaks.get("hbm_gbs", 6650.0))
+        peak_src = "measured" if "hbm_gbs" in peaks else "fallback"
+        step_gbs = avg_bytes / (ms * 1e-3) / 1e9
+        gu_bytes = avg_distinct * W13_EXPERT_BYTES + T * D * 2
+        dn_bytes = avg_distinct * W2_EXPERT_BYTES
+        gu_gbs = gu_bytes / (stage_ms["gate_up"] * 1e-3) / 1e9
+        dn_gbs = dn_bytes / (stage_ms["h_split+down"] * 1e-3) / 1e9
+        info = {"distinct_experts_avg": avg_distinct, "algorithmic_bytes_per_step": avg_bytes}
+        if T < 1024:
+            traffic = profiled_traffic(T) if not self.w4a4 else None
+            roof = {"bound": "hbm", "achieved": gu_gbs, "peak": hbm_peak, "unit": "GB/s",
+                    "frac": gu_gbs / hbm_peak, "traffic": traffic,
+                    "kernel": "moe_gemm_bs_kernel<gate/up> (w13 weight stream + SwiGLU)",
+                    "algorithmic_bytes_per_launch": gu_bytes,
+                    "launch_ms": stage_ms["gate_up"], "peak_source": f"{peak_src} hbm_gbs",
+                    "stages_ms": stage_ms, "down_gbs": dn_gbs,
+                    "whole_step_gbs": step_gbs, "whole_step_frac": step_gbs / hbm_peak}
+            if traffic is not None:
+                roof["traffic_launch_algorithmic_bytes"] = (
+                    byts[0][1] * W13_EXPERT_BYTES + T * D * 2)
+            return roof, info
+        # prefill sizes: algorithmic FLOPs 2 * routes * 2I * d (gate/up) and
+        # 2 * routes * d * I (down); W4A16 work counts against the measured
+        # bf16 rate, W4A4 against the FP4 rate (4x). The kernels run inside a
+        # seconds-long loop, so the sustained figure applies.
+        routes = sum(int((x >= 0).sum()) for x in ids_all) / len(ids_all)
+        fl_gu = 2.0 * routes * 2 * I * D
+        fl_all = fl_gu * 1.5
+        tf_peak = float(peaks.get("bf16_tflops_sustained", 1400.0)) * (4.0 if self.w4a4 else 1.0)
+        tf_src = ("measured bf16_tflops_sustained" if "bf16_tflops_sustained" in peaks
+                  else "fallback 1.4 PF sustained") + (" x4 (FP4 rate)" if self.w4a4 else "")
+        gu_tf = fl_gu / (stage_ms["gate_up"] * 1e-3) / 1e12
+        dn_tf = fl_gu / 2 / (stage_ms["h_split+down"] * 1e-3) / 1e12
+        step_tf = fl_all / (ms * 1e-3) / 1e12
+        roof = {"bound": "tensor", "achieved": gu_tf, "peak": tf_peak, "unit": "TFLOP/s",
+                "frac": gu_tf / tf_peak, "traffic": None,
+                "kernel": "moe_gemm_bs_kernel<gate/up> (grouped GEMM + SwiGLU)",
+                "algorithmic_flops_per_launch": fl_gu, "launch_ms": stage_ms["gate_up"],
+                "peak_source": tf_src, "stages_ms": stage_ms, "down_tflops": dn_tf,
+                "whole_step_tflops": step_tf, "whole_step_frac": step_tf / tf_peak,
+                "bf16_burst_peak": float(peaks.get("bf16_tflops", 1590.0))}
+        return roof, info
+
+
+def run_single(args, sbb, rank, world, local):
+    import torch
+    device = torch.device("cuda", local)
+    T = args.tokens
+    N_LAYERS = args.layers
+    routing = args.routing or default_routing(T)
+    peaks = load_peaks()
+    layers = make_layers(device, N_LAYERS, seed=1000 + rank)
+    head = LayerBench(sbb, device, layers, T, routing, args.w4a4, args, seed_base=2000 + rank)
+    clk = ClockSampler(local)
+    ms, eager_ms, spread, stage_ms = head.measure(args.steps, args.warmup, args.min_timed_s,
+                                                  clk=clk, eager=args.eager)
     clocks = clk.summary()
-
-    # ---- per-stage timing for the roofline: the same calls with the C-ABI's
-    # stage events recorded on the launching stream ------------------------
-    evsets = [sbb.stage_events(stream) for _ in range(args.steps)]
-    torch.cuda.synchronize()
-    for i in range(args.steps):
-        h, ids, w = batches[i % N_LAYERS]
-        forward(h, ids, w, layers[i % N_LAYERS], out=out, stage_events=evsets[i])
-    torch.cuda.synchronize()
-    stage_ms = {name: statistics.mean(evs[j].elapsed_time(evs[j + 1]) for evs in evsets)
-                for j, name in enumerate(sbb.STAGE_NAMES)}
+    roofline, info = head.roofline(ms, stage_ms, peaks)
 
     # ---- end-to-end through the public op with host buffers ---------------
-    host_in = []
-    for (h, ids, w) in batches:
-        host_in.append((h.cpu().pin_memory(), ids.cpu().pin_memory(), w.cpu().pin_memory()))
+    host_in = [(h.cpu().pin_memory(), ids.cpu().pin_memory(), w.cpu().pin_memory())
+               for (h, ids, w) in head.batches]
     host_out = torch.empty((T, D), dtype=torch.bfloat16).pin_memory()
-    dh = torch.empty_like(batches[0][0])
-    di = torch.empty_like(batches[0][1])
-    dw = torch.empty_like(batches[0][2])
+    dh = torch.empty_like(head.batches[0][0])
+    di = torch.empty_like(head.batches[0][1])
+    dw = torch.empty_like(head.batches[0][2])
 
     def e2e_step(i):
         hh, hi, hw = host_in[i % N_LAYERS]
         dh.copy_(hh, non_blocking=True)
         di.copy_(hi, non_blocking=True)
         dw.copy_(hw, non_blocking=True)
-        o = forward(dh, di, dw, layers[i % N_LAYERS])
+        o = head.forward(dh, di, dw, layers[i % N_LAYERS])
         host_out.copy_(o, non_blocking=True)
 
     for i in range(max(args.warmup, 3)):
         e2e_step(i)
-    torch.cuda.synchronize()
-    barrier(world)
-    e0 = torch.cuda.Event(enable_timing=True)
-    e1 = torch.cuda.Event(enable_timing=True)
-    e0.record(stream)
-    for i in range(args.steps):
-        e2e_step(i)
-    e1.record(stream)
-    torch.cuda.synchronize()
-    e2e_ms = max_over_ranks(e0.elapsed_time(e1), world) / args.steps
+    e2e_ms, _ = head.timer.run(e2e_step, args.steps, 3)
     h2d = T * D * 2 + T * TOP_K * 4 + T * TOP_K * 4
     d2h = T * D * 2
 
-    # ---- algorithmic bytes and roofline -----------------------------------
-    ids_all = [b[1].cpu().numpy() for b in batches]
-    byts = [algorithmic_bytes(x, T) for x in ids_all]
-    avg_bytes = sum(b for b, _ in byts) / len(byts)
-    avg_distinct = sum(d for _, d in byts) / len(byts)
-    peaks = {}
-    try:
-        peaks = json.loads((ROOT / "MEASURED_PEAKS.json").read_text())
-    except Exception:
-        pass
-    hbm_peak = float(peaks.get("hbm_gbs", 6650.0))
-    peak_src = "measured" if "hbm_gbs" in peaks else "fallback"
-    achieved_step = avg_bytes / (ms * 1e-3) / 1e9
-
-    # dominant kernel: gate/up + SwiGLU streams w13 (2/3 of the weight bytes)
-    distinct_bytes_w13 = avg_distinct * (2 * I * D // 2 + 2 * I * D // 16 + 4) + T * D * 2
-    distinct_bytes_w2 = avg_distinct * (D * I // 2 + D * I // 16 + 4)
-    gu_gbs = distinct_bytes_w13 / (stage_ms["gate_up"] * 1e-3) / 1e9
-    dn_gbs = distinct_bytes_w2 / (stage_ms["h_split+down"] * 1e-3) / 1e9
-    # DRAM traffic of one gate/up launch on batch 0 from the committed ncu
-    # summary (same seeds, T and layer shape), beside that launch's own
-    # algorithmic bytes.
-    traffic, traffic_alg = profiled_traffic(T), None
-    if traffic is not None:
-        traffic_alg = byts[0][1] * (2 * I * D // 2 + 2 * I * D // 16 + 4) + T * D * 2
-    roofline = {"bound": "hbm", "achieved": gu_gbs, "peak": hbm_peak, "unit": "GB/s",
-                "frac": gu_gbs / hbm_peak, "traffic": traffic,
-                "traffic_launch_algorithmic_bytes": traffic_alg,
-                "kernel": "moe_gemm_bs_kernel<gate/up> (w13 weight stream + SwiGLU)",
-                "algorithmic_bytes_per_launch": distinct_bytes_w13,
-                "launch_ms": stage_ms["gate_up"], "peak_source": f"{peak_src} hbm_gbs",
-                "stages_ms": stage_ms, "down_gbs": dn_gbs,
-                "whole_step_gbs": achieved_step, "whole_step_frac": achieved_step / hbm_peak}
-    if T >= 1024:
-        # prefill sizes: tensor-bound. Algorithmic FLOPs 2 * routes * 2I * d for
-        # gate/up and 2 * routes * d * I for down (W4A16 work counts as bf16;
-        # W4A4 against the FP4 rate, 4x the measured bf16 figure). The kernels
-        # are timed inside a seconds-long loop, so the sustained figure applies.
-        routes = T * TOP_K
-        fl_gu = 2.0 * routes * 2 * I * D
-        fl_all = fl_gu * 1.5
-        tf_peak = float(peaks.get("bf16_tflops_sustained", 1400.0)) * (4.0 if args.w4a4 else 1.0)
-        tf_src = ("measured bf16_tflops_sustained" if "bf16_tflops_sustained" in peaks
-                  else "fallback 1.4 PF sustained") + (" x4 (FP4 rate)" if args.w4a4 else "")
-        gu_tf = fl_gu / (stage_ms["gate_up"] * 1e-3) / 1e12
-        step_tf = fl_all / (ms * 1e-3) / 1e12
-        roofline = {"bound": "tensor", "achieved": gu_tf, "peak": tf_peak, "unit": "TFLOP/s",
-                    "frac": gu_tf / tf_peak, "traffic": None,
-                    "kernel": "moe_gemm_bs_kernel<gate/up> (grouped GEMM + SwiGLU)",
-                    "algorithmic_flops_per_launch": fl_gu, "launch_ms": stage_ms["gate_up"],
-                    "peak_source": tf_src, "stages_ms": stage_ms,
-                    "whole_step_tflops": step_tf, "whole_step_frac": step_tf / tf_peak,
-                    "bf16_burst_peak": float(peaks.get("bf16_tflops", 1590.0))}
+    # ---- the other single-GPU workloads of the configurations -------------
+    workloads = {}
+    if not args.no_extras and world == 1 and not args.w4a4 and T == 64 and not args.eager:
+        extras = [(1, "uniform", False), (8, "uniform", False), (32, "uniform", False),
+                  (8192, "biased", False), (4096, "zipf", False), (4096, "zipf", True)]
+        for (t, r, w4) in extras:
+            lb = LayerBench(sbb, device, layers, t, r, w4, args, seed_base=3000 + t)
+            xclk = ClockSampler(local)
+            xms, xeager, xspread, xstage = lb.measure(args.steps, args.warmup, 0.25, clk=xclk)
+            xroof, xinfo = lb.roofline(xms, xstage, peaks)
+            workloads[workload_name(t, r, w4)] = {
+                "value": t / (xms * 1e-3), "unit": "tokens/s", "ms_per_step": xms,
+                "eager_ms_per_step": xeager, "loop_spread_ms": xspread,
+                "roofline": xroof, **xinfo, "clocks": xclk.summary(),
+                "gpu_launches": sbb.kernels_per_call(t, E, TOP_K, D, I) * args.steps}
+            del lb
+            torch.cuda.empty_cache()
+    errors = sbb.device_errors(device)
 
     cpu_baseline = None
     if rank == 0 and world == 1 and not args.no_cpu_baseline:
@@ -915,18 +1025,19 @@ def main():
             if not O.reference_available():
                 O.build(ref=True)
             if O.reference_available():
-                hb, hids, hw = host_batch(batches[0])
+                hb, hids, hw = host_batch(head.batches[0])
                 tps, sample, threads, _, _ = cpu_reference_run(
                     layer_to_host(layers[0]), hb, hids, hw, args.cpu_seconds)
                 cpu_baseline = {"value": tps, "unit": "tokens/s", "cores": threads,
-                                "kind": "reference", "sample": sample}
+                                "kind": "reference", "sample": sample, "isa": cpu_isa()}
         except Exception as exc:  # the baseline is reported, never required
             cpu_baseline = {"error": str(exc)[:200]}
 
     launches_per_step = sbb.kernels_per_call(T, E, TOP_K, D, I)
     if rank == 0:
         line = {
-            "metric": METRIC, "value": world * T / (ms * 1e-3), "unit": "tokens/s",
+            "metric": METRIC, "value": world * T / (ms * 1e-3) if errors == 0 else None,
+            "unit": "tokens/s",
             "n_gpus": world, "steps": args.steps, "warmup": args.warmup, "ms_per_step": ms,
             "higher_is_better": True, "scaling": "weak", "vs_baseline": None,
             "dtype": ("nvfp4 W4A4: e2m1 weights x e2m1 activations (dynamic per-row globals), "
@@ -934,28 +1045,52 @@ def main():
                      "nvfp4 W4A16: e2m1 weights x 4-term e2m1 activation split, mxf4nvf4 MMA, "
                      "fp32 accumulate",
             "data": "synthetic",
-            "config": {"workload": workload_name(args, T, routing),
-                       "global_batch": world * T, "tokens_per_gpu": T,
-                       "parallelism": f"replicas x{world}" if world > 1 else "single",
-                       "l2": f"inputs larger than L2: {N_LAYERS} rotating layers of "
-                             f"{E * EXPERT_BYTES / 1e9:.2f} GB",
-                       "distinct_experts_avg": avg_distinct,
-                       "algorithmic_bytes_per_step": avg_bytes},
-            "timing": "CUDA graph replay" if graphs else "eager calls",
+            "config": single_config(T, routing, args.w4a4),
+            "tokens_per_gpu": T,
+            "replicas": world if world > 1 else None,
+            **info,
+            "timing": ("CUDA graph replay" if not args.eager else "eager calls")
+                      + f"; median of {spread['repeats']} loops of {args.steps} steps, each "
+                        "after one untimed step",
+            "loop_spread_ms": spread,
             "eager_ms_per_step": eager_ms,
-            "weight_stream_gbs": achieved_step,
+            "weight_stream_gbs": roofline.get("whole_step_gbs"),
             "roofline": roofline,
             "cpu_baseline": cpu_baseline,
             "e2e": {"value": world * T / (e2e_ms * 1e-3), "unit": "tokens/s",
                     "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": d2h,
                     "ms_per_step": e2e_ms},
             "gpu_launches": launches_per_step * args.steps,
+            "device_errors": errors,
             "clocks": clocks,
+            "workloads": workloads or None,
         }
+        if errors:
+            line["invalid"] = "device error bits set during the run; no value reported"
         print(json.dumps(line), flush=True)
     if world > 1:
         import torch.distributed as dist
         dist.destroy_process_group()
+
+
+def main():
+    args = parse()
+    if args.impl == "reference":
+        run_reference_arm(args)
+        return
+    import torch
+    import __graft_entry__ as g
+
+    rank, world, local = dist_init()
+    device = torch.device("cuda", local)
+    torch.cuda.set_device(device)
+    sbb = g.load_package()
+    if args.stack:
+        run_stack(args, sbb, rank, world, local)
+    elif world > 1 and not args.replicas:
+        run_expert_parallel(args, sbb, rank, world, local)
+    else:
+        run_single(args, sbb, rank, world, local)
 
 
 if __name__ == "__main__":

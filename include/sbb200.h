@@ -118,6 +118,26 @@ int sbb200_nvfp4_moe_bad_ids(void* stream, const void* workspace, uint32_t* coun
  * hanging (src/phase7/b70_capi.h:189-193). */
 int sbb200_nvfp4_moe_device_errors(void* stream, const void* workspace, uint32_t* errors);
 
+/* Limit, in nanoseconds, of every pipeline wait inside the tcgen05 GEMM
+ * kernels launched from now on (0 restores the default of 2 s); returns the
+ * previous limit. A wait that runs out raises bit 0 of the device error word
+ * (sbb200_nvfp4_moe_device_errors) and the kernel abandons its work and
+ * returns, so the context stays usable. The limit is counted from the moment
+ * the previous kernel's results are visible. Captured CUDA graphs keep the
+ * limit in force at capture. Process-wide. The reference's CUDA-side wait
+ * cannot time out (src/phase7/b70_capi.h:189-193); this bound replaces its
+ * poller's failure counting on the device. */
+uint64_t sbb200_set_kernel_wait_ns(uint64_t ns);
+
+/* Error bits raised on the current device by any call of this library since
+ * the last read, whatever workspace or stream it used (bit 0: a tcgen05 GEMM
+ * wait passed its limit and that call's result is not valid). Unlike
+ * sbb200_nvfp4_moe_device_errors, which sees only the last call on one
+ * workspace, this keeps failures across calls and CUDA-graph replays until
+ * read. Reads, clears, synchronises `stream`. No counterpart in the
+ * reference (its poller counts failed dispatches, b70_capi.h:189-193). */
+int sbb200_device_errors(void* stream, uint32_t* errors);
+
 /* ---------------------------------------------------------------------------
  * Building blocks, exported for parity tests and for callers that own the
  * routing step. All stream-ordered.
@@ -185,17 +205,21 @@ int sbb200_route_plan(void* stream, const int32_t* topk_ids, size_t M, size_t to
                       void* scratch, uint32_t* bad_ids);
 
 /* sbb200_route_plan without allocation, for callers that cannot give the
- * library device memory: code inside a CUDA stream capture, engines whose
- * device memory is owned by a pooling allocator, FFI bindings without a
- * device allocator. Same arguments and results as sbb200_route_plan minus
- * the scratch: its scratch is a fixed 128 KB array in the library's device
- * image (held on every device that loads the library until exit), so it
- * handles at most 262144 routes (M * top_k) and E <= 512; larger calls fail
- * with SBB200_EUNSUPPORTED. The first call on a device resolves that array's
- * device address (cudaGetSymbolAddress), so make the first call on each
- * device before any stream capture. All calls share the array: calls that
- * overlap on the GPU (different streams, or several host threads) race and
- * must be serialised by the caller. Has no counterpart in the reference. */
+ * library device memory: serving engines whose device memory is owned by a
+ * pooling allocator sized before the model runs, and FFI bindings (ctypes,
+ * cgo, JNI) that hold only the tensors they were handed and have no device
+ * allocator. Same arguments and results as sbb200_route_plan minus the
+ * scratch: its scratch is a fixed 128 KB array in the library's device image
+ * (held on every device that loads the library until exit), so it handles at
+ * most 262144 routes (M * top_k) and E <= 512; larger calls fail with
+ * SBB200_EUNSUPPORTED. Nothing is allocated by any call. The first call on a
+ * device resolves that array's device address (cudaGetSymbolAddress), so make
+ * the first call on each device before any stream capture; the address is
+ * kept for the life of the process, so the entry point is not usable on a
+ * device after cudaDeviceReset. All calls share the array and each call
+ * overwrites what the previous one left there: calls that overlap on the GPU
+ * (different streams, or several host threads) race and must be serialised
+ * by the caller. Has no counterpart in the reference. */
 int sbb200_route_plan_static(void* stream, const int32_t* topk_ids, size_t M, size_t top_k,
                              size_t E, int32_t* counts, int32_t* offsets, int32_t* sorted,
                              int32_t* slot_of, uint32_t* bad_ids);
@@ -223,7 +247,10 @@ int sbb200_nvfp4_quantize(void* stream, const void* x, int in_dt, const float* g
 typedef struct sbb200_provider sbb200_provider_t;
 
 /* 48-byte POD, field for field the reference's sb_b70_health_t
- * (src/phase7/b70_capi.h:28-41). */
+ * (src/phase7/b70_capi.h:28-41); its `reserved` word carries the device error
+ * word of the provider's last forward here (bit 0: a kernel wait passed its
+ * limit and that forward's result is not valid; bit 31: the word could not
+ * be read). */
 typedef struct sbb200_health {
   uint64_t generation;
   uint64_t dispatches;
@@ -232,7 +259,7 @@ typedef struct sbb200_health {
   uint32_t loaded;
   uint32_t pending;
   uint32_t stopped;
-  uint32_t reserved;
+  uint32_t device_errors;
 } sbb200_health_t;
 
 /* Create a provider on `device` able to serve batches up to max_tokens tokens
@@ -257,7 +284,9 @@ int sbb200_moe_forward(sbb200_provider_t* p, size_t layer, void* stream, const v
 
 /* Health snapshot + last error copy-out (src/phase7/b70_capi.h:159-172):
  * 0 ok, -1 invalid arguments, -2 buffer too small (truncated copy written,
- * last_error_bytes holds the size needed). */
+ * last_error_bytes holds the size needed). After a forward it synchronises
+ * the provider's device to read device_errors, so it is not to be called
+ * inside a stream capture. */
 int sbb200_health(sbb200_provider_t* p, sbb200_health_t* health, char* last_error,
                   size_t last_error_size);
 

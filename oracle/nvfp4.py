@@ -43,11 +43,31 @@ E2M1_VALUES = np.array([0.0, 0.5, 1.0, 1.5, 2.0, 3.0, 4.0, 6.0], dtype=np.float3
 # building / loading
 # --------------------------------------------------------------------------
 
+def reference_dir() -> Path | None:
+    """Root of the reference source tree: ``SBB200_REFERENCE_DIR`` when set,
+    else a directory named ``reference`` beside this repository, else None."""
+    env = os.environ.get("SBB200_REFERENCE_DIR")
+    if env:
+        return Path(env)
+    sibling = HERE.parent.parent / "reference"
+    return sibling if (sibling / "src" / "phase7").is_dir() else None
+
+
 def build(ref: bool = True) -> None:
-    """Compile the C oracle (and, where the reference tree exists, the
+    """Compile the C oracle (and, where the reference tree is found, the
     reference CPU tier) with ``oracle/Makefile``."""
     targets = ["oracle"] + (["ref"] if ref else [])
-    subprocess.run(["make", "-s", "-C", str(HERE)] + targets, check=True)
+    cmd = ["make", "-s", "-C", str(HERE)] + targets
+    rdir = reference_dir() if ref else None
+    if rdir is not None:
+        cmd.append(f"REF={rdir}")
+    subprocess.run(cmd, check=True)
+
+
+def reference_isa() -> str | None:
+    """The -march the reference CPU tier in _ref was compiled for."""
+    f = REF_SO.parent / "isa.txt"
+    return f.read_text().strip() if f.exists() else None
 
 
 _oracle_lib = None

@@ -77,6 +77,10 @@ def lib() -> ctypes.CDLL:
         L.sbb200_nvfp4_moe_bad_ids.argtypes = [P, P, P]
         L.sbb200_nvfp4_moe_device_errors.restype = I
         L.sbb200_nvfp4_moe_device_errors.argtypes = [P, P, P]
+        L.sbb200_device_errors.restype = I
+        L.sbb200_device_errors.argtypes = [P, P]
+        L.sbb200_set_kernel_wait_ns.restype = ctypes.c_uint64
+        L.sbb200_set_kernel_wait_ns.argtypes = [ctypes.c_uint64]
         L.sbb200_route_plan_scratch_bytes.restype = S
         L.sbb200_route_plan_scratch_bytes.argtypes = [S, S]
         L.sbb200_route_plan.restype = I
@@ -289,17 +293,55 @@ def stage_events(stream: torch.cuda.Stream | None = None) -> list:
 _OUT_CODES = {0: torch.float32, 1: torch.float16, 2: torch.bfloat16}
 
 
+def _check_split_scratch(split_scratch, split, topk_ids, w13):
+    """The split-scratch check of tk_xpu_ext.sycl:378-388, same message."""
+    if split and split_scratch is not None:
+        _check_cuda("split scratch", split_scratch)
+        M, top_k = topk_ids.shape
+        I = w13.size(1) // 2
+        if (split_scratch.dtype != torch.float32 or split_scratch.dim() != 2
+                or split_scratch.size(0) != M * top_k or split_scratch.size(1) != 2 * I):
+            raise ValueError("sbb200: split scratch must be float32 [M*top_k,2I]")
+
+
 @torch.library.custom_op("sbb200::nvfp4_moe", mutates_args=())
 def _nvfp4_moe_op(hidden: torch.Tensor, topk_ids: torch.Tensor, topk_weights: torch.Tensor,
                   w13: torch.Tensor, w13_scales: torch.Tensor, w13_global_scales: torch.Tensor,
                   w2: torch.Tensor, w2_scales: torch.Tensor, w2_global_scales: torch.Tensor,
-                  multiply_router_weight: bool, out_dtype_code: int) -> torch.Tensor:
+                  split_scratch: torch.Tensor | None, split: bool,
+                  multiply_router_weight: bool) -> torch.Tensor:
+    """The reference extension's op, argument for argument and in the same
+    order (tk_xpu_ext.sycl:296-302): fp32 [M, K] out. ``split`` and
+    ``split_scratch`` pick a kernel shape on the reference's Arc cards; the
+    B200 driver picks its kernels itself, so they are validated and leave the
+    result unchanged."""
+    _check_split_scratch(split_scratch, split, topk_ids, w13)
+    return _nvfp4_moe_impl(hidden, topk_ids, topk_weights, w13, w13_scales, w13_global_scales,
+                           w2, w2_scales, w2_global_scales, multiply_router_weight,
+                           torch.float32)
+
+
+@_nvfp4_moe_op.register_fake
+def _(hidden, topk_ids, topk_weights, w13, w13_scales, w13_global_scales, w2, w2_scales,
+      w2_global_scales, split_scratch, split, multiply_router_weight):
+    return hidden.new_empty(hidden.shape, dtype=torch.float32)
+
+
+@torch.library.custom_op("sbb200::nvfp4_moe_typed", mutates_args=())
+def _nvfp4_moe_typed_op(hidden: torch.Tensor, topk_ids: torch.Tensor,
+                        topk_weights: torch.Tensor, w13: torch.Tensor, w13_scales: torch.Tensor,
+                        w13_global_scales: torch.Tensor, w2: torch.Tensor,
+                        w2_scales: torch.Tensor, w2_global_scales: torch.Tensor,
+                        multiply_router_weight: bool, out_dtype_code: int) -> torch.Tensor:
+    """sbb200::nvfp4_moe with the output in the model dtype (out_dtype_code
+    0 f32, 1 f16, 2 bf16): the hook's path, which skips the fp32 round trip
+    the reference's plugin makes before casting (routed_experts.py:3004-3007)."""
     return _nvfp4_moe_impl(hidden, topk_ids, topk_weights, w13, w13_scales, w13_global_scales,
                            w2, w2_scales, w2_global_scales, multiply_router_weight,
                            _OUT_CODES[out_dtype_code])
 
 
-@_nvfp4_moe_op.register_fake
+@_nvfp4_moe_typed_op.register_fake
 def _(hidden, topk_ids, topk_weights, w13, w13_scales, w13_global_scales, w2, w2_scales,
       w2_global_scales, multiply_router_weight, out_dtype_code):
     return hidden.new_empty(hidden.shape, dtype=_OUT_CODES[out_dtype_code])
@@ -315,16 +357,18 @@ def nvfp4_moe(hidden: torch.Tensor, topk_ids: torch.Tensor, topk_weights: torch.
     (tk_xpu_ext.sycl:296-302). ``split``/``split_scratch`` select a kernel
     shape on the reference's Arc cards; the B200 driver picks its kernels
     itself, so they are accepted and validated but do not change the result.
-    Returns ``out_dtype`` [M, K] (fp32 like the reference op by default)."""
-    if split and split_scratch is not None:
-        M, top_k = topk_ids.shape
-        I = w13.size(1) // 2
-        if (split_scratch.dtype != torch.float32 or split_scratch.dim() != 2
-                or split_scratch.size(0) != M * top_k or split_scratch.size(1) != 2 * I):
-            raise ValueError("sbb200: split scratch must be float32 [M*top_k,2I]")
-    return torch.ops.sbb200.nvfp4_moe(hidden, topk_ids, topk_weights, w13, w13_scales,
-                                      w13_global_scales, w2, w2_scales, w2_global_scales,
-                                      bool(multiply_router_weight), DTYPE_CODE[out_dtype])
+    Returns ``out_dtype`` [M, K] (fp32 like the reference op by default):
+    fp32 goes through ``torch.ops.sbb200.nvfp4_moe``, other dtypes through
+    ``torch.ops.sbb200.nvfp4_moe_typed``."""
+    if out_dtype == torch.float32:
+        return torch.ops.sbb200.nvfp4_moe(hidden, topk_ids, topk_weights, w13, w13_scales,
+                                          w13_global_scales, w2, w2_scales, w2_global_scales,
+                                          split_scratch, bool(split),
+                                          bool(multiply_router_weight))
+    _check_split_scratch(split_scratch, split, topk_ids, w13)
+    return torch.ops.sbb200.nvfp4_moe_typed(hidden, topk_ids, topk_weights, w13, w13_scales,
+                                            w13_global_scales, w2, w2_scales, w2_global_scales,
+                                            bool(multiply_router_weight), DTYPE_CODE[out_dtype])
 
 
 def nvfp4_moe_bad_ids(device: torch.device | None = None) -> int:
@@ -351,6 +395,27 @@ def nvfp4_moe_device_errors(device: torch.device | None = None) -> int:
     v = ctypes.c_uint32(0)
     _check(lib().sbb200_nvfp4_moe_device_errors(key[1], _p(ws), ctypes.addressof(v)))
     return int(v.value)
+
+
+def device_errors(device: torch.device | None = None) -> int:
+    """Error bits raised on ``device`` by any call of this library since the
+    last read (bit 0: a tcgen05 GEMM wait passed its limit and that call's
+    result is not valid), across workspaces, streams and graph replays.
+    Reads and clears; synchronises the current stream."""
+    device = device or torch.device("cuda", torch.cuda.current_device())
+    v = ctypes.c_uint32(0)
+    with torch.cuda.device(device):
+        _check(lib().sbb200_device_errors(torch.cuda.current_stream(device).cuda_stream,
+                                          ctypes.addressof(v)))
+    return int(v.value)
+
+
+def set_kernel_wait_ns(ns: int) -> int:
+    """Limit of the tcgen05 GEMMs' pipeline waits for later launches (0: the
+    2 s default); returns the previous limit. A wait that runs out makes the
+    kernel abandon its work and raise the device error bit instead of
+    hanging."""
+    return int(lib().sbb200_set_kernel_wait_ns(int(ns)))
 
 
 # --------------------------------------------------------------------------
@@ -493,7 +558,7 @@ class Health(ctypes.Structure):
     _fields_ = [("generation", ctypes.c_uint64), ("dispatches", ctypes.c_uint64),
                 ("allocations", ctypes.c_uint64), ("last_error_bytes", ctypes.c_uint64),
                 ("loaded", ctypes.c_uint32), ("pending", ctypes.c_uint32),
-                ("stopped", ctypes.c_uint32), ("reserved", ctypes.c_uint32)]
+                ("stopped", ctypes.c_uint32), ("device_errors", ctypes.c_uint32)]
 
 
 class Provider:
@@ -530,6 +595,9 @@ class Provider:
         return out
 
     def health(self) -> tuple[dict, str]:
+        """(health fields, last error). ``device_errors`` is the device error
+        word of the last forward (bit 0: a kernel wait passed its limit and
+        that result is not valid); reading it synchronises the device."""
         h = Health()
         buf = ctypes.create_string_buffer(4096)
         lib().sbb200_health(self.h, ctypes.byref(h), buf, 4096)

@@ -62,7 +62,7 @@ int validate_shape(size_t M, size_t E, size_t top_k, size_t K, size_t I, int act
     *why = "top_k above the supported maximum of " + std::to_string(kMaxTopK);
     return SBB200_EUNSUPPORTED;
   }
-  if (M * top_k > (size_t)0x7fffffff || K > 65536 || I > 65536) {
+  if (M > (size_t)0x7fffffff / top_k || K > 65536 || I > 65536) {
     *why = "shape exceeds 32-bit route indexing";
     return SBB200_EUNSUPPORTED;
   }
@@ -318,6 +318,15 @@ int sbb200_nvfp4_moe_device_errors(void* stream, const void* workspace, uint32_t
   return SBB200_OK;
 }
 
+uint64_t sbb200_set_kernel_wait_ns(uint64_t ns) { return sbb::set_kernel_wait_ns(ns); }
+
+int sbb200_device_errors(void* stream, uint32_t* errors) {
+  if (!errors) return fail(SBB200_EINVAL, "device_errors received a null pointer");
+  const cudaError_t err = sbb::read_sticky_errors(static_cast<cudaStream_t>(stream), errors);
+  if (err != cudaSuccess) return cuda_fail(err, "device_errors");
+  return SBB200_OK;
+}
+
 size_t sbb200_route_plan_scratch_bytes(size_t routes, size_t E) {
   return sbb::route_plan_scratch_bytes(routes, E);
 }
@@ -327,7 +336,8 @@ int sbb200_route_plan(void* stream, const int32_t* topk_ids, size_t M, size_t to
                       void* scratch, uint32_t* bad_ids) {
   if (E == 0 || E > (size_t)sbb::kMaxExperts)
     return fail(SBB200_EINVAL, "route_plan: E must be in [1, 512]");
-  if (M * top_k > (size_t)0x7fffffff) return fail(SBB200_EUNSUPPORTED, "route_plan: too many routes");
+  if (top_k != 0 && M > (size_t)0x7fffffff / top_k)
+    return fail(SBB200_EUNSUPPORTED, "route_plan: too many routes");
   if (!counts || !offsets || (M * top_k != 0 && (!topk_ids || !sorted || !slot_of || !scratch)))
     return fail(SBB200_EINVAL, "route_plan received a null pointer");
   cudaStream_t s = static_cast<cudaStream_t>(stream);
@@ -504,6 +514,20 @@ int sbb200_health(sbb200_provider_t* p, sbb200_health_t* health, char* last_erro
   health->loaded = p->layers.empty() ? 0u : 1u;
   health->pending = 0;
   health->stopped = 0;
+  // the device error word of the last forward (bit 0: a kernel wait gave up
+  // and its result is not valid); reading it waits for the device
+  if (p->dispatches > 0 && p->workspace) {
+    int prev = 0;
+    cudaGetDevice(&prev);
+    uint32_t word = 0;
+    cudaError_t e = cudaSetDevice(p->device);
+    if (e == cudaSuccess) e = cudaDeviceSynchronize();
+    if (e == cudaSuccess)
+      e = cudaMemcpy(&word, static_cast<const char*>(p->workspace) + sbb::kStatusOffset + 4,
+                     sizeof word, cudaMemcpyDeviceToHost);
+    cudaSetDevice(prev);
+    health->device_errors = e == cudaSuccess ? word : 0x80000000u;
+  }
   if (last_error && last_error_size) {
     const size_t need = p->last_error.size() + 1;
     const size_t n = need <= last_error_size ? need - 1 : last_error_size - 1;

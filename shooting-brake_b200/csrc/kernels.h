@@ -112,6 +112,11 @@ struct BsLaunch {
 };
 
 bool bs_supported(int K, int I);
+// Sets the limit of the grouped GEMMs' pipeline waits for later launches (0:
+// the 2 s default); returns the previous limit.
+uint64_t set_kernel_wait_ns(uint64_t ns);
+// Reads and clears the current device's sticky GEMM error bits (synchronises).
+cudaError_t read_sticky_errors(cudaStream_t stream, uint32_t* errors);
 int bs_tile_rows(int64_t routes, int E, int mode, int nt);
 cudaError_t launch_moe_bs(const BsLaunch& a, cudaStream_t stream, const char** step);
 

@@ -66,7 +66,16 @@ constexpr int kRowScales = kBK / 16;  // scale bytes per row per stage (16)
 constexpr int kM = 128;
 constexpr int kThreads = 512;
 constexpr int kTmemCols = 512;
-constexpr uint64_t kTimeoutNs = 2000000000ull;
+constexpr uint64_t kTimeoutNs = 2000000000ull;  // default wait limit; drains always get this
+
+// Limit of the pipeline waits of the grouped GEMMs (sbb200_set_kernel_wait_ns).
+std::atomic<uint64_t> g_wait_ns{kTimeoutNs};
+
+// Error bits of every GEMM launch on this device since the host last read
+// them (sbb200_device_errors): unlike the per-call word in the workspace,
+// which each call clears, this one keeps a failure of any earlier call, so a
+// run of graph replays can be checked once at its end. Zero at load.
+__device__ uint32_t g_sticky_errors = 0;
 
 enum : int { kGateUp = 0, kDown = 1 };
 
@@ -88,6 +97,8 @@ struct BsParams {
                         // (decode): weights evict_first, term rows evict_last;
                         // 0: tiles are shared by several token tiles in
                         // flight (prefill): both evict_normal
+  uint64_t wait_ns;     // limit of every pipeline wait, counted from the
+                        // moment the previous kernel's results are visible
 };
 
 template <int MODE, int BNR, int NT>
@@ -197,7 +208,6 @@ __global__ void __launch_bounds__(kThreads, 1)
   const int tid = threadIdx.x;
   const int warp = tid >> 5;
   const int lane = tid & 31;
-  const uint64_t deadline = now_ns() + kTimeoutNs;
   volatile int* abort = &abort_s;
 
   if (tid == 0) {
@@ -231,6 +241,8 @@ __global__ void __launch_bounds__(kThreads, 1)
   // the previous kernel wrote
   pdl_wait();
   pdl_trigger();
+  // the wait limit runs from here, so a long predecessor does not eat into it
+  const uint64_t deadline = now_ns() + p.wait_ns;
   if (warp == 2) {
     int carry = 0;
     for (int e0 = 0; e0 < p.E; e0 += 32) {
@@ -476,7 +488,10 @@ __global__ void __launch_bounds__(kThreads, 1)
   __syncthreads();
   tc_fence_after();
   if (warp == 1) tmem_dealloc(tmem, kTmemCols);
-  if (tid == 0 && abort_s) atomicOr(&p.status[1], 1u);
+  if (tid == 0 && abort_s) {
+    atomicOr(&p.status[1], 1u);
+    atomicOr(&g_sticky_errors, 1u);
+  }
 }
 
 // ---- activation splitter ----------------------------------------------------
@@ -894,6 +909,23 @@ cudaError_t launch_split(const void* src, int src_dt, const SplitRows* rows,
 
 }  // namespace
 
+cudaError_t read_sticky_errors(cudaStream_t stream, uint32_t* errors) {
+  cudaError_t err = cudaMemcpyFromSymbolAsync(errors, g_sticky_errors, sizeof(uint32_t), 0,
+                                              cudaMemcpyDeviceToHost, stream);
+  if (err != cudaSuccess) return err;
+  err = cudaStreamSynchronize(stream);
+  if (err != cudaSuccess) return err;
+  const uint32_t zero = 0;
+  err = cudaMemcpyToSymbolAsync(g_sticky_errors, &zero, sizeof(zero), 0, cudaMemcpyHostToDevice,
+                                stream);
+  if (err != cudaSuccess) return err;
+  return cudaStreamSynchronize(stream);
+}
+
+uint64_t set_kernel_wait_ns(uint64_t ns) {
+  return g_wait_ns.exchange(ns ? ns : kTimeoutNs, std::memory_order_relaxed);
+}
+
 bool bs_supported(int K, int I) {
   return K % kBK == 0 && I % kBK == 0 && K <= 16384 && I <= 16384 && get_encode() != nullptr;
 }
@@ -955,6 +987,7 @@ cudaError_t launch_moe_bs(const BsLaunch& a, cudaStream_t stream, const char** s
   p1.out_ld = a.I;
   // about one token tile per expert: every weight tile is read once
   p1.stream_weights = R <= static_cast<int64_t>(a.E) * (bnr1 / NT);
+  p1.wait_ns = g_wait_ns.load(std::memory_order_relaxed);
   BsParams p2 = p1;
   p2.gscale = w4a4_static ? a.alpha2 : a.g2;
   p2.bg = a.hg;

@@ -315,13 +315,17 @@ cudaError_t launch_router_topk(const void* logits, int dt, int64_t M, int E, int
 // ---------------------------------------------------------------------------
 // Route plan without any allocation.
 //
-// Some callers cannot hand the library a workspace: code running inside a
-// CUDA stream capture (a cudaMalloc there is not part of the graph and can
-// stall the device), engines whose device memory belongs to a pooling
-// allocator that forbids allocations outside the pool, and thin FFI bindings
-// that have no device allocator at all. sbb200_route_plan_static serves them
+// Some callers cannot hand the library a workspace: serving engines whose
+// device memory belongs to a pooling allocator that forbids allocations
+// outside the pool (and whose pool is sized before the model runs), and thin
+// FFI bindings (ctypes, cgo, JNI) that hold only the tensors they were given
+// and have no device allocator at all. sbb200_route_plan_static serves them
 // with scratch that the library owns: the per-chunk expert counts live in the
 // file-scope array below, so a call allocates nothing.
+//
+// The device address of that array is looked up once per device and kept for
+// the life of the process. cudaDeviceReset unloads the library's device image,
+// so this entry point is not usable after a reset of a device it has run on.
 // ---------------------------------------------------------------------------
 #include <mutex>
 #include <string>
@@ -353,6 +357,12 @@ extern "C" int sbb200_route_plan_static(void* stream, const int32_t* topk_ids, s
                                         int32_t* offsets, int32_t* sorted, int32_t* slot_of,
                                         uint32_t* bad_ids) {
   using namespace sbb;
+  // M * top_k is formed only once it cannot wrap around
+  if (top_k != 0 && M > static_cast<size_t>(kStaticMaxRoutes) / top_k) {
+    set_last_error("route_plan_static: M*top_k routes exceed its static scratch limit of "
+                   "262144; use sbb200_route_plan with a caller workspace");
+    return SBB200_EUNSUPPORTED;
+  }
   const size_t R = M * top_k;
   if (E == 0 || E > static_cast<size_t>(kMaxExperts)) {
     set_last_error("route_plan_static: E must be in [1, 512]");

@@ -106,12 +106,28 @@ class RoutedExpertsB200:
                                         device=dev)
 
     @classmethod
-    def from_layer(cls, layer, **kw) -> "RoutedExpertsB200":
-        """Build from a vLLM-style layer object holding ``w13_weight``,
-        ``w13_weight_scale``, ``w13_weight_scale_2`` and the ``w2_*``
-        counterparts (``routed_experts.py:1529-1552, 1744-1753``). The scales
-        must be linear (unswizzled); a ``_w13_is_reordered()`` method, when
-        present, says whether the w13 halves are ``[up; gate]``."""
+    def from_layer(cls, layer, scale_layout: str = "swizzled", **kw) -> "RoutedExpertsB200":
+        """Build from a vLLM NVFP4 MoE layer after weight loading: ``w13_weight``
+        [E, 2I, d/2], ``w13_weight_scale``, ``w2_weight``, ``w2_weight_scale``
+        and the per-expert globals (``routed_experts.py:1529-1552, 1744-1753``).
+
+        Block scales: vLLM keeps them swizzled for its CUTLASS/FlashInfer
+        kernels (128-row x 4-column tiles, padded; ``swizzle_blockscale``), so
+        by default they are converted to linear order once, here, as the
+        reference's hook does before its CPU tier reads them
+        (``routed_experts.py:1926-1938``, vLLM ``convert_swizzled_to_linear``).
+        ``scale_layout="linear"`` takes them as they are (bank layout).
+
+        Globals: the dequant multiplier g (W = e2m1 * e4m3 * g) comes from
+        the quant config when the layer has one: ``alpha_or_gscale`` of w1/w2
+        is g divided by the activation global (vLLM's g1/g2 alphas,
+        ``expert_bank.py:270-295``), so g = alpha * a_gscale. Otherwise from
+        ``w13_weight_scale_2`` / ``w2_weight_scale_2`` ([E], or [E, 2] with
+        separate w1/w3 globals, of which vLLM keeps the first column and
+        warns when they differ; the same is done here).
+
+        A ``_w13_is_reordered()`` method, when present, says whether the w13
+        halves are ``[up; gate]``."""
         reordered = getattr(layer, "_w13_is_reordered", None)
         kw.setdefault("w13_is_up_gate", bool(reordered()) if callable(reordered) else False)
 
@@ -119,8 +135,24 @@ class RoutedExpertsB200:
             v = getattr(layer, name)
             return v.data if hasattr(v, "data") else v
 
-        return cls(t("w13_weight"), t("w13_weight_scale"), t("w13_weight_scale_2"),
-                   t("w2_weight"), t("w2_weight_scale"), t("w2_weight_scale_2"), **kw)
+        w13, w2 = t("w13_weight"), t("w2_weight")
+        E, two_i, half_d = w13.shape
+        d, I = half_d * 2, two_i // 2
+        s13, s2 = t("w13_weight_scale"), t("w2_weight_scale")
+        if scale_layout == "swizzled":
+            s13 = unswizzle_block_scales(s13, two_i, d // 16)
+            s2 = unswizzle_block_scales(s2, d, I // 16)
+        elif scale_layout != "linear":
+            raise ValueError("sbb200: scale_layout must be 'swizzled' or 'linear'")
+        g13, g2 = layer_globals(layer, E)
+        return cls(w13, s13, g13.to(w13.device), w2, s2, g2.to(w13.device), **kw)
+
+    def device_errors(self) -> int:
+        """Device error word of this layer's last forward on the current
+        stream (bit 0: a kernel wait passed its limit and that result is not
+        valid). Synchronises the stream."""
+        from . import nvfp4_moe_device_errors
+        return nvfp4_moe_device_errors(self.w13.device)
 
     @property
     def num_experts(self) -> int:
@@ -156,6 +188,64 @@ class RoutedExpertsB200:
         return y
 
     __call__ = forward_modular
+
+
+def unswizzle_block_scales(sf: torch.Tensor, rows: int, cols: int) -> torch.Tensor:
+    """Linear [E, rows, cols] e4m3 block scales (uint8) from vLLM's swizzled
+    layout (``swizzle_blockscale``: per expert, rows padded to 128 and
+    columns to 4, stored as [rows/128, cols/4, 32, 4, 4] with element
+    (m, k, r, q, c) = linear[128 m + 32 q + r, 4 k + c]); the inverse of
+    vLLM's ``convert_swizzled_to_linear``, expert by expert. Runs once, with
+    torch ops on the tensor's device."""
+    if sf.dim() == 2:
+        sf = sf.unsqueeze(0)
+    E = sf.shape[0]
+    rp, cp = -(-rows // 128) * 128, -(-cols // 4) * 4
+    flat = sf.reshape(E, -1)
+    if flat.shape[1] != rp * cp:
+        raise ValueError(f"sbb200: swizzled block scales of {tuple(sf.shape)} do not cover "
+                         f"[{E}, {rp}, {cp}] (rows {rows}, cols {cols} padded to 128 x 4)")
+    raw = flat.view(torch.uint8) if flat.dtype != torch.uint8 else flat
+    tiles = raw.reshape(E, rp // 128, cp // 4, 32, 4, 4)
+    lin = tiles.permute(0, 1, 4, 3, 2, 5).reshape(E, rp, cp)
+    return lin[:, :rows, :cols].contiguous()
+
+
+def layer_globals(layer, E: int) -> tuple[torch.Tensor, torch.Tensor]:
+    """Per-expert fp32 dequant multipliers (g13, g2) of a vLLM NVFP4 MoE layer:
+    alpha * a_gscale from the quant config when present (vLLM's alphas are the
+    weight global divided by the activation global), else the
+    ``*_weight_scale_2`` tensors ([E] or [E, 2] -> first column)."""
+    import warnings
+
+    qc = getattr(getattr(layer, "quant_method", None), "moe_quant_config", None)
+    desc = [getattr(qc, n, None) for n in ("_w1", "_w2", "_a1", "_a2")] if qc else []
+    vals = [getattr(x, "alpha_or_gscale", None) for x in desc]
+    if len(vals) == 4 and all(v is not None for v in vals):
+        out = []
+        for alpha, a_g in ((vals[0], vals[2]), (vals[1], vals[3])):
+            alpha = alpha.detach().float().reshape(-1)
+            a_g = a_g.detach().float().reshape(-1).to(alpha.device)
+            if alpha.numel() != E or a_g.numel() not in (1, E):
+                raise ValueError("sbb200: quant config alphas must be [E] and activation "
+                                 "globals [1] or [E]")
+            out.append((alpha * a_g).contiguous())
+        return out[0], out[1]
+
+    def g(name):
+        v = getattr(layer, name)
+        v = (v.data if hasattr(v, "data") else v).detach().float()
+        if v.dim() == 2 and v.shape == (E, 2):
+            if not torch.equal(v[:, 0], v[:, 1]):
+                warnings.warn(f"sbb200: {name} holds different w1 and w3 globals; using the "
+                              "first (as vLLM does)", stacklevel=3)
+            v = v[:, 0]
+        v = v.reshape(-1)
+        if v.numel() != E:
+            raise ValueError(f"sbb200: {name} must hold E (or E x 2) values")
+        return v.contiguous()
+
+    return g("w13_weight_scale_2"), g("w2_weight_scale_2")
 
 
 _registered = None

@@ -126,8 +126,21 @@ def test_custom_op_and_validation(sbb, oracle, cuda):
     ids = torch.zeros((3, 2), dtype=torch.int32, device=cuda)
     w = torch.full((3, 2), 0.5, device=cuda)
     tensors = layer_to(L, cuda)
-    out = torch.ops.sbb200.nvfp4_moe(hidden, ids, w, *tensors, True, 0)
+    # the reference op's positional signature (tk_xpu_ext.sycl:296-302):
+    # ..., split_scratch, split, multiply_router_weight -> fp32
+    out = torch.ops.sbb200.nvfp4_moe(hidden, ids, w, *tensors, None, False, True)
     assert out.shape == (3, 256) and out.dtype == torch.float32
+    scratch = torch.empty((6, 128), dtype=torch.float32, device=cuda)
+    out_split = torch.ops.sbb200.nvfp4_moe(hidden, ids, w, *tensors, scratch, True, True)
+    assert torch.equal(out_split, out)
+    # both routes of a token go to expert 0 with weight 0.5: unweighted is 2x
+    unweighted = torch.ops.sbb200.nvfp4_moe(hidden, ids, w, *tensors, None, False, False)
+    assert torch.allclose(unweighted, out * 2.0, rtol=1e-5, atol=1e-6)
+    typed = torch.ops.sbb200.nvfp4_moe_typed(hidden, ids, w, *tensors, True, 2)
+    assert typed.dtype == torch.bfloat16
+    assert torch.allclose(typed.float(), out, rtol=1e-2, atol=1e-2 * float(out.abs().max()))
+    with pytest.raises(ValueError, match="split scratch must be float32"):
+        torch.ops.sbb200.nvfp4_moe(hidden, ids, w, *tensors, scratch[:5], True, True)
     with pytest.raises(ValueError, match="topk ids must be int32"):
         sbb.nvfp4_moe(hidden, ids.long(), w, *tensors)
     with pytest.raises(ValueError, match="w2 must be byte"):

@@ -115,8 +115,9 @@ def test_single_hot_expert(sbb, oracle, cuda):
 
 @pytest.mark.parametrize("scale", [1e-4, 1.0, 3000.0])
 def test_activation_range(sbb, oracle, cuda, scale):
-    """Activations far from unit scale: the per-row power-of-two staging keeps
-    the f16 operand exact whatever the magnitude."""
+    """Activations far from unit scale: the 4-term split takes each row's
+    global from the row's own maximum, so a uniform scale of the whole row
+    changes nothing but that global."""
     K, I, E, T = 512, 256, 8, 33
     tensors = random_layer(E, K, I, seed=7, device=cuda)
     ids, w = oracle.route_logits(T, E, 3, seed=8)
@@ -141,3 +142,61 @@ def test_deterministic_repeat(sbb, oracle, cuda, big_layer):
     b = sbb.nvfp4_moe(hidden, dev(ids, cuda), dev(w, cuda), *big_layer)
     torch.cuda.synchronize()
     assert torch.equal(a, b)
+
+
+def per_token_check(got, want):
+    """The bar applied token by token: for every token t,
+    max|got_t - want_t| / max|want_t| <= 1e-2 and cos(got_t, want_t) >= 0.9999.
+    Returns the worst of each."""
+    worst_rel, worst_cos = 0.0, 1.0
+    for t in range(want.shape[0]):
+        if not np.any(want[t]):
+            assert not np.any(got[t])
+            continue
+        worst_rel = max(worst_rel, rel_err(got[t], want[t]))
+        worst_cos = min(worst_cos, cosine(got[t], want[t]))
+    assert worst_rel <= REL_TOL, worst_rel
+    assert worst_cos >= COS_TOL, worst_cos
+    return worst_rel, worst_cos
+
+
+def _outlier_hidden(oracle, T, K, seed, kind):
+    """bf16 bits of hidden rows with the dynamic range of real hidden states:
+    'one1e3' one channel per row 10^3 x the rest; 'few1e4' four fixed
+    channels 10^4 x; 'tiny_blocks' every 16-element block but the first at
+    2^-14 (and some at 2^-20) of the row maximum."""
+    rng = np.random.default_rng(seed)
+    x = rng.standard_normal((T, K)).astype(np.float32)
+    if kind == "one1e3":
+        ch = rng.integers(0, K, T)
+        x[np.arange(T), ch] *= 1e3
+    elif kind == "few1e4":
+        for ch in (7, 300, 301, K - 5):
+            x[:, ch] = np.sign(x[:, ch] + 1e-3) * (1e4 + 100 * rng.random(T))
+    elif kind == "tiny_blocks":
+        x[:, 16:] *= 2.0 ** -14
+        x[:, 16 * 9:16 * 20] *= 2.0 ** -6  # these blocks end at 2^-20
+    else:
+        raise ValueError(kind)
+    b = x.view(np.uint32)
+    b = ((b + 0x7FFF + ((b >> 16) & 1)) >> 16).astype(np.uint16)  # round to nearest even
+    return b
+
+
+@pytest.mark.parametrize("kind", ["one1e3", "few1e4", "tiny_blocks"])
+def test_outlier_channels_per_token(sbb, oracle, cuda, kind):
+    """W4A16 numerics of the 4-term activation split under outliers and
+    blocks far below their row maximum, judged token by token rather than
+    over the batch, at the decode shape's K and I."""
+    E, K, I, T, top_k = 16, 4096, 1280, 48, 4
+    tensors = random_layer(E, K, I, seed=71, device=cuda)
+    ids, w = oracle.route_logits(T, E, top_k, seed=72)
+    hidden = _outlier_hidden(oracle, T, K, seed=73, kind=kind)
+    h = dev(hidden, cuda, torch.bfloat16)
+    out = sbb.nvfp4_moe(h, dev(ids, cuda), dev(w, cuda), *tensors)
+    torch.cuda.synchronize()
+    assert sbb.nvfp4_moe_device_errors(cuda) == 0
+    L = host_layer(oracle, tensors, E, K, I)
+    want = oracle.moe_forward(hidden, ids, w, L)
+    worst = per_token_check(out.cpu().numpy(), want)
+    print(f"{kind}: worst per-token rel {worst[0]:.3e}, cos {worst[1]:.7f}")

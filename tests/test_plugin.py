@@ -52,8 +52,87 @@ def test_from_layer_reads_vllm_attribute_names(plugin, oracle):
                         "w2_weight_scale", "w2_weight_scale_2"), ts):
         setattr(layer, name, torch.nn.Parameter(t, requires_grad=False))
     layer._w13_is_reordered = lambda: False
-    ex = plugin.RoutedExpertsB200.from_layer(layer)
+    ex = plugin.RoutedExpertsB200.from_layer(layer, scale_layout="linear")
     assert ex.num_experts == L.E and torch.equal(ex.w2, ts[3])
+
+
+def _vllm_swizzle(monkeypatch, sf_u8: torch.Tensor) -> torch.Tensor:
+    """vLLM's own swizzle_blockscale on a CPU tensor (the helper ends in
+    .cuda(); that move is made a no-op here so it runs without a GPU)."""
+    nu = pytest.importorskip("vllm.model_executor.layers.quantization.utils.nvfp4_utils")
+    with monkeypatch.context() as m:
+        m.setattr(torch.Tensor, "cuda", lambda self, *a, **k: self)
+        return nu.swizzle_blockscale(sf_u8.view(torch.float8_e4m3fn)).view(torch.uint8)
+
+
+def _fake_vllm_layer(ts, monkeypatch, E, scale2_shape="E"):
+    class FakeLayer:
+        pass
+
+    layer = FakeLayer()
+    w13, s13, g13, w2, s2, g2 = ts
+    layer.w13_weight = torch.nn.Parameter(w13, requires_grad=False)
+    layer.w2_weight = torch.nn.Parameter(w2, requires_grad=False)
+    layer.w13_weight_scale = torch.nn.Parameter(_vllm_swizzle(monkeypatch, s13),
+                                                requires_grad=False)
+    layer.w2_weight_scale = torch.nn.Parameter(_vllm_swizzle(monkeypatch, s2),
+                                               requires_grad=False)
+    if scale2_shape == "E2":
+        g13 = torch.stack([g13, g13], dim=1)
+        g2 = torch.stack([g2, g2], dim=1)
+    layer.w13_weight_scale_2 = torch.nn.Parameter(g13, requires_grad=False)
+    layer.w2_weight_scale_2 = torch.nn.Parameter(g2, requires_grad=False)
+    return layer
+
+
+@pytest.mark.parametrize("K,I", [(256, 256), (512, 96)])
+def test_from_layer_unswizzles_vllm_block_scales(plugin, oracle, monkeypatch, K, I):
+    """Scales swizzled by vLLM's swizzle_blockscale (rows padded to 128,
+    columns to 4 when I/16 is not a multiple of 4) come back byte-exact in
+    the linear bank layout, and agree with vLLM's convert_swizzled_to_linear."""
+    emu = pytest.importorskip(
+        "vllm.model_executor.layers.quantization.utils.nvfp4_emulation_utils")
+    E = 3
+    L, ts = _layer_tensors(oracle, "cpu", E, K, I, seed=5)
+    layer = _fake_vllm_layer(ts, monkeypatch, E, scale2_shape="E2")
+    assert layer.w2_weight_scale.shape[-1] % 4 == 0
+    ex = plugin.RoutedExpertsB200.from_layer(layer)
+    assert torch.equal(ex.w13_scale, ts[1]) and torch.equal(ex.w2_scale, ts[4])
+    assert torch.equal(ex.w13_global, ts[2]) and torch.equal(ex.w2_global, ts[5])
+    for e in range(E):
+        # that helper slices its result to k columns, not k/16, so padding
+        # columns may remain on its side
+        lin = emu.convert_swizzled_to_linear(layer.w2_weight_scale.data[e], K, I, 16)
+        assert torch.equal(lin[:, :I // 16].contiguous().view(torch.uint8), ts[4][e])
+
+
+def test_from_layer_globals_from_quant_config(plugin, oracle):
+    """vLLM's alphas are the weight global over the activation global
+    (expert_bank.py:270-295 of the reference): g = alpha * a_gscale."""
+    E, K, I = 4, 256, 256
+    L, ts = _layer_tensors(oracle, "cpu", E, K, I, seed=7)
+
+    class Desc:
+        def __init__(self, v):
+            self.alpha_or_gscale = v
+
+    class QC:
+        pass
+
+    a1, a2 = torch.tensor([54.75]), torch.full((E,), 154.0)
+    qc = QC()
+    qc._w1, qc._w2 = Desc(ts[2] / a1), Desc(ts[5] / a2)
+    qc._a1, qc._a2 = Desc(a1), Desc(a2)
+    g13, g2 = plugin.layer_globals(type("L", (), {"quant_method": type(
+        "Q", (), {"moe_quant_config": qc})()})(), E)
+    assert torch.allclose(g13, ts[2], rtol=1e-6) and torch.allclose(g2, ts[5], rtol=1e-6)
+
+
+def test_from_layer_rejects_unpadded_swizzled_scales(plugin, oracle):
+    E, K, I = 2, 256, 96
+    L, ts = _layer_tensors(oracle, "cpu", E, K, I, seed=9)
+    with pytest.raises(ValueError, match="swizzled block scales"):
+        plugin.unswizzle_block_scales(ts[4], K, I // 16)  # [E, 256, 6]: not padded to 8
 
 
 def test_forward_on_cpu_tensors_raises(plugin, oracle):
@@ -172,3 +251,29 @@ def test_fused_shared_expert_matches_oracle(plugin, oracle, cuda):
     shared = oracle.moe_forward(hidden, np.zeros((T, 1), np.int32), np.ones((T, 1), np.float32), S)
     want = routed + gate[:, None] * shared
     _check(y.float().cpu().numpy(), want)
+
+
+@pytest.mark.gpu
+def test_from_layer_swizzled_vllm_layer_matches_oracle(plugin, oracle, cuda):
+    """A vLLM-style layer with scales from vLLM's swizzle_blockscale on the
+    device and [E, 2] weight_scale_2, through from_layer, against the oracle."""
+    nu = pytest.importorskip("vllm.model_executor.layers.quantization.utils.nvfp4_utils")
+    E, K, I, T, top_k = 10, 512, 256, 40, 4
+    L, ts = _layer_tensors(oracle, cuda, E, K, I, seed=51)
+
+    class FakeLayer:
+        pass
+
+    layer = FakeLayer()
+    layer.w13_weight, layer.w2_weight = ts[0], ts[3]
+    layer.w13_weight_scale = nu.swizzle_blockscale(ts[1].view(torch.float8_e4m3fn))
+    layer.w2_weight_scale = nu.swizzle_blockscale(ts[4].view(torch.float8_e4m3fn))
+    layer.w13_weight_scale_2 = torch.stack([ts[2], ts[2]], 1)
+    layer.w2_weight_scale_2 = torch.stack([ts[5], ts[5]], 1)
+    ex = plugin.RoutedExpertsB200.from_layer(layer)
+    hidden = oracle.make_hidden(T, K, seed=52)
+    ids, w = oracle.route_logits(T, E, top_k, seed=53)
+    x = torch.from_numpy(hidden).to(cuda).view(torch.bfloat16)
+    y = ex.forward_modular(x, torch.from_numpy(w).to(cuda), torch.from_numpy(ids).to(cuda))
+    _check(y.float().cpu().numpy(), oracle.moe_forward(hidden, ids, w, L))
+    assert ex.device_errors() == 0

@@ -1,11 +1,12 @@
 """The scratch-free route plan, sbb200_route_plan_static.
 
-It exists for callers that cannot hand the library device memory: code inside
-a CUDA stream capture, engines whose device memory belongs to a pooling
-allocator, FFI bindings without a device allocator. Its scratch is a fixed
-array inside the library, shared by every call, so two calls in a row must
-each agree with the workspace entry point, sbb200_route_plan, whatever the
-previous call left in that array. Integer outputs: compared exactly.
+It exists for callers that cannot hand the library device memory: serving
+engines whose device memory belongs to a pooling allocator sized up front, and
+FFI bindings that hold only the tensors they were given and have no device
+allocator. Its scratch is a fixed array inside the library, shared by every
+call, so calls in a row must each agree with the workspace entry point,
+sbb200_route_plan, whatever the previous call left in that array. Integer
+outputs: compared exactly.
 
 The file name sorts last so that a stop-at-first-failure run has already run
 every other test when it gets here."""
@@ -70,9 +71,35 @@ def test_static_route_plan_matches_workspace_entry_point(sbb, cuda):
             assert int(bad.item()) == int(want["bad_ids"].item()) == 1
 
 
+def test_static_route_plan_single_chunk_and_empty(sbb, cuda):
+    # One 4096-route chunk (no per-chunk counts in the shared array), then a
+    # call with no routes (counts and offsets cleared, nothing else touched),
+    # then the single-chunk call again after a multi-chunk one.
+    rng = np.random.default_rng(21)
+    small = rng.integers(-1, 170, size=(100, 8)).astype(np.int32)
+    big = rng.integers(0, 96, size=(1500, 8)).astype(np.int32)
+    for ids, E in ((small, 170), (np.zeros((0, 8), np.int32), 170), (big, 96), (small, 170)):
+        t = torch.from_numpy(ids).to(cuda)
+        counts, offsets, sorted_routes, slot_of, bad = run_static(sbb, t, E, False)
+        torch.cuda.synchronize()
+        if ids.shape[0] == 0:
+            assert torch.equal(counts, torch.zeros_like(counts))
+            assert torch.equal(offsets, torch.zeros_like(offsets))
+            continue
+        want = sbb.route_plan(t, E)
+        n = int(want["offsets"][-1].item())
+        assert torch.equal(counts, want["counts"])
+        assert torch.equal(offsets, want["offsets"])
+        assert torch.equal(sorted_routes[:n], want["sorted"][:n])
+        assert torch.equal(slot_of, want["slot_of"])
+
+
 def test_static_route_plan_rejects_oversize(sbb):
     lib = sbb.lib()
     dummy = P(1)
     rc = static_entry(lib)(None, dummy, 65537, 4, 170, dummy, dummy, dummy, dummy, None)
     assert rc == -4
     assert "262144" in sbb.last_error()
+    # a route count that would wrap around size_t is rejected, not wrapped
+    rc = static_entry(lib)(None, dummy, (1 << 63) + 1, 2, 170, dummy, dummy, dummy, dummy, None)
+    assert rc == -4
