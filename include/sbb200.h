@@ -363,7 +363,10 @@ int sbb200_ep_connect(sbb200_ep_t* ep, const void* handles, size_t size);
  * [M, K] in act_dt, topk_ids int32 [M, top_k] with global expert ids,
  * topk_weights fp32 [M, top_k]) in, out [M, K] in out_dt; w13..w2_global_scales
  * are this rank's shard (sbb200_ep_shard) in the layout of sbb200_nvfp4_moe,
- * indexed by local expert id. M may be 0 (the rank still serves its experts). */
+ * indexed by local expert id. M may be 0 (the rank still serves its experts).
+ * Each route's expert output is computed on the rank that holds the expert
+ * and summed on the token's own rank in ascending k with the router weights,
+ * the arithmetic of sbb200_nvfp4_moe's combine. */
 int sbb200_ep_forward(sbb200_ep_t* ep, void* stream, const void* hidden, const int32_t* topk_ids,
                       const float* topk_weights, size_t M, const void* w13,
                       const void* w13_scales, const float* w13_global_scales, const void* w2,
@@ -373,9 +376,12 @@ int sbb200_ep_forward(sbb200_ep_t* ep, void* stream, const void* hidden, const i
 /* sbb200_ep_forward that also records SBB200_EP_STAGE_EVENTS cudaEvent_t on
  * `stream`: [0] start, [1] after publish, [2] after the gather (including the
  * wait for every rank's publish), [3] after the route plan and the pulled
- * activation split, [4] after gate/up, [5] after down, [6] after the combine
- * push, [7] after the final sum (including the wait for every rank). No
- * counterpart in the reference; it times the exchange against the GEMMs. */
+ * activation split, [4] after gate/up, [5] after down (which pushes each
+ * route's row to its source), [6] = [5], [7] after the final sum (including
+ * the wait for every rank). In decode-sized steps (world * max_tokens *
+ * top_k <= 1024) the activation split does the publish and the gather
+ * itself, so [0] = [1] = [2]. No counterpart in the reference; it times the
+ * exchange against the GEMMs. */
 #define SBB200_EP_STAGE_EVENTS 8
 int sbb200_ep_forward_staged(sbb200_ep_t* ep, void* stream, const void* hidden,
                              const int32_t* topk_ids, const float* topk_weights, size_t M,
@@ -389,9 +395,11 @@ int sbb200_ep_forward_staged(sbb200_ep_t* ep, void* stream, const void* hidden,
  * another rank passed its 2 s deadline); reads, clears, synchronises. */
 int sbb200_ep_device_errors(sbb200_ep_t* ep, void* stream, uint32_t* errors);
 
-/* Number of kernels one sbb200_ep_forward step launches on its stream
- * (publish, gather, the shard's expert step, final sum), or -1 for a null
- * handle. No counterpart in the reference. */
+/* Number of kernels one sbb200_ep_forward step launches on its stream, or
+ * -1 for a null handle: 5 for decode-sized steps (exchange split, gate/up,
+ * SwiGLU split, down, final sum), more for larger ones (publish, gather and
+ * the route plan run as kernels of their own). No counterpart in the
+ * reference. */
 int sbb200_ep_launches(const sbb200_ep_t* ep);
 
 void sbb200_ep_destroy(sbb200_ep_t* ep);

@@ -38,48 +38,34 @@ __device__ __forceinline__ void store4(void* out, int out_dt, int64_t at, float4
   }
 }
 
-// dst.base != nullptr: expert-parallel partials (fp32, peer memory, rows with
-// no valid route skipped).
 __global__ void __launch_bounds__(kThreads) combine_kernel(
     const float* __restrict__ y, const int32_t* __restrict__ slot_of,
     const float* __restrict__ weights, int multiply_router_weight, void* __restrict__ out,
-    int out_dt, int top_k, int K, SplitRows dst) {
+    int out_dt, int top_k, int K) {
   const int64_t t = blockIdx.x;
   __shared__ int32_t s_slot[kMaxTopK];
   __shared__ float s_w[kMaxTopK];
-  __shared__ int s_any;
   pdl_wait();
   pdl_trigger();
-  if (threadIdx.x == 0) s_any = 0;
-  __syncthreads();
   if (threadIdx.x < top_k) {
     s_slot[threadIdx.x] = slot_of[t * top_k + threadIdx.x];
     s_w[threadIdx.x] = multiply_router_weight ? weights[t * top_k + threadIdx.x] : 1.0f;
-    if (s_slot[threadIdx.x] >= 0) s_any = 1;
   }
   __syncthreads();
-  void* orow = out;
-  int64_t obase = t * K;
-  if (dst.base) {
-    orow = const_cast<void*>(dst.base[t / dst.rows_per_src]);
-    obase = (t % dst.rows_per_src) * K;
-  }
-  if (!dst.base || s_any) {
-    for (int n4 = (blockIdx.y * kThreads + threadIdx.x) * 4; n4 < K;
-         n4 += gridDim.y * kThreads * 4) {
-      float4 acc = make_float4(0.f, 0.f, 0.f, 0.f);
-      for (int k = 0; k < top_k; ++k) {
-        const int32_t s = s_slot[k];
-        if (s < 0) continue;
-        const float w = s_w[k];
-        const float4 v = __ldg(reinterpret_cast<const float4*>(y + (int64_t)s * K + n4));
-        acc.x = fmaf(w, v.x, acc.x);
-        acc.y = fmaf(w, v.y, acc.y);
-        acc.z = fmaf(w, v.z, acc.z);
-        acc.w = fmaf(w, v.w, acc.w);
-      }
-      store4(orow, dst.base ? static_cast<int>(kF32) : out_dt, obase + n4, acc);
+  for (int n4 = (blockIdx.y * kThreads + threadIdx.x) * 4; n4 < K;
+       n4 += gridDim.y * kThreads * 4) {
+    float4 acc = make_float4(0.f, 0.f, 0.f, 0.f);
+    for (int k = 0; k < top_k; ++k) {
+      const int32_t s = s_slot[k];
+      if (s < 0) continue;
+      const float w = s_w[k];
+      const float4 v = __ldg(reinterpret_cast<const float4*>(y + (int64_t)s * K + n4));
+      acc.x = fmaf(w, v.x, acc.x);
+      acc.y = fmaf(w, v.y, acc.y);
+      acc.z = fmaf(w, v.z, acc.z);
+      acc.w = fmaf(w, v.w, acc.w);
     }
+    store4(out, out_dt, t * K + n4, acc);
   }
 }
 
@@ -87,14 +73,13 @@ __global__ void __launch_bounds__(kThreads) combine_kernel(
 
 cudaError_t launch_combine(const float* y, const int32_t* slot_of, const float* weights,
                            int multiply_router_weight, void* out, int out_dt, int64_t M,
-                           int top_k, int K, cudaStream_t stream, const SplitRows* dst) {
+                           int top_k, int K, cudaStream_t stream) {
   if (M == 0) return cudaSuccess;
   // K is a multiple of 32, so whole float4 groups cover each row.
   const int per_cta = kThreads * 4;
   dim3 grid((unsigned)M, (unsigned)((K + per_cta - 1) / per_cta));
-  const SplitRows d = dst ? *dst : SplitRows{nullptr, 1};
   return launch_kernel(true, combine_kernel, grid, dim3(kThreads), 0, stream, y, slot_of, weights,
-                       multiply_router_weight, out, out_dt, top_k, K, d);
+                       multiply_router_weight, out, out_dt, top_k, K);
 }
 
 }  // namespace sbb

@@ -87,4 +87,26 @@ __device__ __forceinline__ unsigned long long ld_acquire_sys(const unsigned long
   return v;
 }
 
+// Spin until *flag (its high word when hi_word) equals epoch, or give up at
+// `deadline` (globaltimer ns) or once *errors has bit 0 set (an earlier wait
+// of this rank gave up), raising bit 0 of *errors. *seen gets the flag.
+__device__ __forceinline__ bool ep_wait_epoch(const unsigned long long* flag,
+                                              unsigned long long epoch, bool hi_word,
+                                              unsigned long long* seen, unsigned int* errors,
+                                              uint64_t deadline) {
+  for (uint32_t i = 0;; ++i) {
+    const unsigned long long v = ld_acquire_sys(flag);
+    if ((hi_word ? (v >> 32) : v) == epoch) {
+      *seen = v;
+      return true;
+    }
+    if ((i & 63u) == 63u) {
+      if (globaltimer_ns() > deadline || (*reinterpret_cast<volatile unsigned int*>(errors) & 1u)) {
+        atomicOr(errors, 1u);
+        return false;
+      }
+    }
+  }
+}
+
 }  // namespace sbb

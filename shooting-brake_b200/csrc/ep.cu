@@ -1,51 +1,51 @@
 // Expert parallelism over NVLink: the routed experts of a layer are sharded
 // contiguously over the GPUs of one node (one process per GPU), the tokens
 // stay with the rank that owns them, and each step exchanges activations and
-// partial outputs through peer memory.
+// per-route outputs through peer memory.
 //
 // The reference splits experts disjointly over its cards with dense per-card
 // slot maps; every card sees all routes with foreign experts as -1 and the
 // host sums the per-card partial outputs (src/phase4/src/shooting_brake_vllm/
 // routed_experts.py:354-382, 2460-2463, 2522-2524). Here the exchange is
-// device-resident and stream-ordered:
+// device-resident and stream-ordered. A step's virtual tokens are
+// v = s * max_tokens + t over every source rank s; a destination d serves the
+// routes of all virtual tokens that go to its experts.
 //
-//   publish  (source s)  bump the device epoch and copy this step's hidden
-//                        rows, ids and weights into s's exchange buffer.
-//   gather   (dest d)    block 0 first sets ready[d] = epoch << 32 | M on
-//                        every rank (the copies of the kernel before are
-//                        complete; system-scope fence, release stores through
-//                        NVLink); then every block waits for the other ranks'
-//                        ready flags (bounded), reads each source's ids over
-//                        NVLink and keeps the routes to d's experts as local
-//                        ids (-1 elsewhere) for the virtual tokens
-//                        v = s * max_tokens + t.
-//   MoE      (dest d)    the single-GPU pipeline on the virtual tokens: the
-//                        activation split reads each routed token's row
-//                        straight from its source GPU (pull), the GEMMs run
-//                        on d's shard, and the combine stores each token's
-//                        fp32 partial sum (router weights applied) into its
-//                        source's partial[d] rows (push).
-//   final    (source s)  block 0 first sets done[s] = epoch on every rank
-//                        (this rank's pushes, the kernel before, are
-//                        complete); every block waits for the other ranks'
-//                        done flags (bounded) and sums the partials of the
-//                        ranks that own the token's experts in ascending rank
-//                        order (a fixed order, so repeat runs are
-//                        bit-identical).
-// Each flag is raised by the kernel after the one whose writes it announces,
-// once griddepcontrol.wait has returned: that grid has completed, so every
-// one of its stores is performed before the release. (A last-CTA counter
-// inside the writing kernel was tried first and, at 8 ranks, let a flag out
-// ahead of some of the kernel's peer stores.)
+// Decode-sized steps (world * max_tokens * top_k <= 1,024 virtual routes),
+// five kernels:
+//   exchange split  the CTAs of d's own tokens copy them into d's exchange
+//                   buffer and the last of them raises ready[d] = epoch << 32
+//                   | M on every rank; every CTA waits for the other ranks'
+//                   ready flags, plans d's local routes from every rank's ids
+//                   and pulls its token's row from its source GPU
+//                   (ep_split_kernel, moe_bs.cu);
+//   gate/up, SwiGLU split, down   the single-GPU kernels on d's shard; the
+//                   down epilogue stores each route's fp32 row straight into
+//                   the source's partial[t][k] (no combine kernel);
+//   final  (s)      block 0 raises done[s] = epoch on every rank (s's pushes,
+//                   the kernel before, are complete); every block waits for
+//                   every rank's done flag and sums its token's routes,
+//                   w[t,k] * partial[t][k], in ascending k: the single-GPU
+//                   combine's arithmetic and order, so the result does not
+//                   depend on how the experts are sharded. The last block
+//                   moves the device epoch to the next step.
+// Larger steps: a publish kernel, a gather kernel (raises ready, waits,
+// keeps the local routes), the route plan, the split pulling rows from the
+// sources, the same GEMMs and final.
 //
-// No NCCL call is on the data path; the process group only exchanges the
-// CUDA IPC handles of the exchange buffers once. The buffers are reused
-// every step without a barrier: a source republishes only after its final
-// combine has seen every destination's done flag, and a destination sends
-// partials for step i+1 only after it saw ready for step i+1, so neither
-// side can overwrite data the other still reads. Every wait gives up after a
-// deadline and raises an error bit instead of spinning forever. No TMA or
-// bulk copy reads peer memory: peer data moves with plain loads and stores.
+// Flags are raised only after the writes they announce have completed: by
+// the kernel after the writing one (griddepcontrol.wait has returned), or,
+// inside the exchange split, by the last publishing CTA after every writer
+// fenced its stores at system scope. No NCCL call is on the data path; the
+// process group only exchanges the CUDA IPC handles of the exchange buffers
+// once. The buffers are reused every step without a barrier: a source
+// republishes only after its final kernel has seen every rank's done flag
+// (raised after that rank's last read of the step), and a destination
+// pushes rows for step i+1 only after it saw that source's ready flag for
+// step i+1, raised after the source finished reading step i. Every wait
+// gives up after 2 s and raises an error bit instead of spinning forever. No
+// TMA or bulk copy touches peer memory: peer data moves with plain loads and
+// stores.
 #include <cuda_runtime.h>
 
 #include <algorithm>
@@ -65,21 +65,20 @@
 namespace sbb {
 namespace {
 
-constexpr int kMaxWorld = 64;
-constexpr uint64_t kWaitNs = 2000000000ull;  // 2 s per wait
 constexpr int kEpThreads = 256;
 
 inline size_t align256(size_t v) { return (v + 255) / 256 * 256; }
 
 // Exchange buffer of one rank (identical layout on every rank; peers write
-// ready/done flags and partial rows into it).
+// ready/done flags and per-route rows into it).
 struct ExLayout {
   size_t ready;    // u64[world]: ready[s] written by source s
   size_t done;     // u64[world]: done[d] written by destination d
   size_t hidden;   // act [max_tokens, K]
   size_t ids;      // i32 [max_tokens, top_k]
   size_t weights;  // f32 [max_tokens, top_k]
-  size_t partial;  // f32 [world, max_tokens, K]: partial[d] written by d
+  size_t partial;  // f32 [max_tokens, top_k, K]: row (t, k) written by the
+                   // owner of route (t, k)'s expert
   size_t total;
 };
 
@@ -96,56 +95,18 @@ ExLayout ex_layout(int world, size_t max_tokens, size_t top_k, size_t K, size_t 
   l.hidden = take(max_tokens * K * act_bytes);
   l.ids = take(max_tokens * top_k * 4);
   l.weights = take(max_tokens * top_k * 4);
-  l.partial = take(static_cast<size_t>(world) * max_tokens * K * 4);
+  l.partial = take(max_tokens * top_k * K * 4);
   l.total = at;
   return l;
 }
 
-// Device-side state of this rank (local memory).
-struct EpDev {
-  unsigned long long epoch;     // step counter, bumped by publish (one writer)
-  unsigned int errors;          // bit 0: a wait timed out (sticky until read)
-  unsigned int pad[5];
-};
-
-struct EpTables {
-  // [world] each
-  unsigned long long* ready_at_peer[kMaxWorld];  // &peer.ready[rank]
-  unsigned long long* done_at_peer[kMaxWorld];   // &peer.done[rank]
-  const void* peer_hidden[kMaxWorld];
-  const int32_t* peer_ids[kMaxWorld];
-  const float* peer_weights[kMaxWorld];
-  void* partial_at_peer[kMaxWorld];              // &peer.partial[rank][0]
-  int shard_begin[kMaxWorld + 1];
-};
-
-__device__ __forceinline__ bool wait_epoch(const unsigned long long* flag, unsigned long long epoch,
-                                           bool hi_word, unsigned long long* seen,
-                                           unsigned int* errors, uint64_t deadline) {
-  for (uint32_t i = 0;; ++i) {
-    const unsigned long long v = ld_acquire_sys(flag);
-    if ((hi_word ? (v >> 32) : v) == epoch) {
-      *seen = v;
-      return true;
-    }
-    if ((i & 63u) == 63u) {
-      if (globaltimer_ns() > deadline || (*reinterpret_cast<volatile unsigned int*>(errors) & 1u)) {
-        atomicOr(errors, 1u);
-        return false;
-      }
-    }
-  }
-}
-
-// Copy this step's tokens into the exchange buffer. Thread 0 of CTA 0 is the
-// only writer of the step epoch; the kernels after this one read it.
+// Copy this step's tokens into the exchange buffer (larger steps).
 __global__ void __launch_bounds__(kEpThreads) ep_publish_kernel(
     const uint4* __restrict__ hidden, int64_t hidden_vec, const int32_t* __restrict__ ids,
     const float* __restrict__ weights, int64_t routes, uint4* __restrict__ ex_hidden,
-    int32_t* __restrict__ ex_ids, float* __restrict__ ex_weights, EpDev* dev) {
+    int32_t* __restrict__ ex_ids, float* __restrict__ ex_weights) {
   pdl_wait();
   pdl_trigger();
-  if (blockIdx.x == 0 && threadIdx.x == 0) dev->epoch = dev->epoch + 1ull;
   const int64_t stride = static_cast<int64_t>(gridDim.x) * blockDim.x;
   for (int64_t i = blockIdx.x * blockDim.x + threadIdx.x; i < hidden_vec; i += stride)
     ex_hidden[i] = hidden[i];
@@ -160,34 +121,35 @@ __global__ void __launch_bounds__(kEpThreads) ep_publish_kernel(
 // (griddepcontrol.wait returned, or plain stream order), so a system-scope
 // fence and release stores make them visible to every rank before the flags.
 __device__ __forceinline__ void raise_flags(unsigned long long* const* at_peer, int world,
-                                            unsigned long long value) {
+                                            int rank, unsigned long long value) {
   if (blockIdx.x != 0 || blockIdx.y != 0) return;
-  if (threadIdx.x < world) {
+  if (threadIdx.x < world && threadIdx.x != rank) {
     __threadfence_system();
     st_release_sys(at_peer[threadIdx.x], value);
   }
 }
 
-// Announce this rank's tokens (ready[rank] = epoch << 32 | M on every rank),
-// then keep the local routes of every virtual token v = s * max_tokens + t.
+// Larger steps: announce this rank's tokens (ready[rank] = epoch << 32 | M on
+// every rank), then keep the local routes of every virtual token
+// v = s * max_tokens + t.
 __global__ void __launch_bounds__(kEpThreads) ep_gather_kernel(
     const unsigned long long* __restrict__ ready, EpDev* dev, const EpTables* __restrict__ tab,
-    int world, int64_t max_tokens, int top_k, int rank, int64_t M, int32_t* __restrict__ local_ids,
-    float* __restrict__ local_w) {
+    int world, int64_t max_tokens, int top_k, int rank, int64_t M,
+    int32_t* __restrict__ local_ids) {
   __shared__ int64_t s_count[kMaxWorld];
   pdl_wait();
   pdl_trigger();
   const unsigned long long epoch = dev->epoch;
-  raise_flags(const_cast<unsigned long long* const*>(tab->ready_at_peer), world,
+  raise_flags(const_cast<unsigned long long* const*>(tab->ready_at_peer), world, rank,
               (epoch << 32) | static_cast<unsigned long long>(M));
-  const uint64_t deadline = globaltimer_ns() + kWaitNs;
+  const uint64_t deadline = globaltimer_ns() + kEpWaitNs;
   for (int s = threadIdx.x; s < world; s += blockDim.x) {
     unsigned long long v = 0;
     if (s == rank) {  // this rank's own tokens: published by the kernel before
       s_count[s] = M;
       continue;
     }
-    s_count[s] = wait_epoch(&ready[s], epoch, true, &v, &dev->errors, deadline)
+    s_count[s] = ep_wait_epoch(&ready[s], epoch, true, &v, &dev->errors, deadline)
                      ? static_cast<int64_t>(v & 0xffffffffull)
                      : 0;
   }
@@ -201,76 +163,80 @@ __global__ void __launch_bounds__(kEpThreads) ep_gather_kernel(
     const int s = static_cast<int>(v / max_tokens);
     const int64_t t = v % max_tokens;
     int32_t lid = -1;
-    float w = 0.0f;
     if (t < s_count[s]) {
-      const int64_t r = t * top_k + (i % top_k);
-      const int32_t e = __ldcg(tab->peer_ids[s] + r);
-      if (e >= e_lo && e < e_hi) {
-        lid = e - e_lo;
-        w = __ldcg(tab->peer_weights[s] + r);
-      }
+      const int32_t e = __ldcg(tab->peer_ids[s] + t * top_k + (i % top_k));
+      if (e >= e_lo && e < e_hi) lid = e - e_lo;
     }
     local_ids[i] = lid;
-    local_w[i] = w;
   }
 }
 
-// out[t] = sum over owning ranks d (ascending) of partial[d][t].
+// out[t] = sum over this token's valid routes k (ascending) of
+// w[t, k] * partial[t][k], after every rank's done flag for this step.
 __global__ void __launch_bounds__(kEpThreads) ep_final_kernel(
     const unsigned long long* __restrict__ done, EpDev* dev, const EpTables* __restrict__ tab,
-    int world, int rank, const int32_t* __restrict__ ids, int top_k, int E, const float* __restrict__ partial,
-    int64_t max_tokens, int K, void* __restrict__ out, int out_dt) {
-  __shared__ unsigned long long s_mask;
+    int world, int rank, const int32_t* __restrict__ ids, const float* __restrict__ weights,
+    int multiply_router_weight, int top_k, int E, const float* __restrict__ partial, int64_t M,
+    int K, void* __restrict__ out, int out_dt) {
+  __shared__ int s_k[kMaxTopK];
+  __shared__ float s_w[kMaxTopK];
   const int64_t t = blockIdx.x;
   pdl_wait();
   pdl_trigger();
   const unsigned long long epoch = dev->epoch;
-  // this rank's partials (the combine before this kernel) are in place
-  raise_flags(const_cast<unsigned long long* const*>(tab->done_at_peer), world, epoch);
-  if (threadIdx.x == 0) {
-    unsigned long long mask = 0;
-    for (int k = 0; k < top_k; ++k) {
-      const int32_t e = ids[t * top_k + k];
-      if (e < 0 || e >= E) continue;
-      int d = 0;
-      while (d + 1 < world && tab->shard_begin[d + 1] <= e) ++d;
-      mask |= 1ull << d;
-    }
-    s_mask = mask;
+  // this rank's pushes (the down projection before this kernel) are in place
+  raise_flags(const_cast<unsigned long long* const*>(tab->done_at_peer), world, rank, epoch);
+  if (t < M && threadIdx.x < top_k) {
+    const int32_t e = ids[t * top_k + threadIdx.x];
+    s_k[threadIdx.x] = (e >= 0 && e < E) ? 1 : 0;
+    s_w[threadIdx.x] = multiply_router_weight ? weights[t * top_k + threadIdx.x] : 1.0f;
   }
-  const uint64_t deadline = globaltimer_ns() + kWaitNs;
+  const uint64_t deadline = globaltimer_ns() + kEpWaitNs;
   for (int d = threadIdx.x; d < world; d += blockDim.x) {
     unsigned long long v = 0;
-    if (d != rank)  // this rank's own partials: written by the kernel before
-      wait_epoch(&done[d], epoch, false, &v, &dev->errors, deadline);
+    if (d != rank)  // this rank's own pushes: the kernel before
+      ep_wait_epoch(&done[d], epoch, false, &v, &dev->errors, deadline);
   }
   __syncthreads();
-  const unsigned long long mask = s_mask;
-  for (int n4 = (blockIdx.y * blockDim.x + threadIdx.x) * 4; n4 < K;
-       n4 += gridDim.y * blockDim.x * 4) {
-    float4 acc = make_float4(0.f, 0.f, 0.f, 0.f);
-    for (int d = 0; d < world; ++d) {
-      if (!((mask >> d) & 1ull)) continue;
-      const float4 p = __ldcg(reinterpret_cast<const float4*>(
-          partial + (static_cast<int64_t>(d) * max_tokens + t) * K + n4));
-      acc.x += p.x;
-      acc.y += p.y;
-      acc.z += p.z;
-      acc.w += p.w;
+  if (t < M) {
+    for (int n4 = (blockIdx.y * blockDim.x + threadIdx.x) * 4; n4 < K;
+         n4 += gridDim.y * blockDim.x * 4) {
+      float4 acc = make_float4(0.f, 0.f, 0.f, 0.f);
+      for (int k = 0; k < top_k; ++k) {
+        if (!s_k[k]) continue;
+        const float w = s_w[k];
+        const float4 p = __ldcg(reinterpret_cast<const float4*>(
+            partial + (t * top_k + k) * static_cast<int64_t>(K) + n4));
+        acc.x = fmaf(w, p.x, acc.x);
+        acc.y = fmaf(w, p.y, acc.y);
+        acc.z = fmaf(w, p.z, acc.z);
+        acc.w = fmaf(w, p.w, acc.w);
+      }
+      const int64_t at = t * K + n4;
+      if (out_dt == kF32) {
+        *reinterpret_cast<float4*>(static_cast<float*>(out) + at) = acc;
+      } else if (out_dt == kBF16) {
+        __nv_bfloat162 a = __floats2bfloat162_rn(acc.x, acc.y);
+        __nv_bfloat162 b = __floats2bfloat162_rn(acc.z, acc.w);
+        *reinterpret_cast<uint2*>(static_cast<__nv_bfloat16*>(out) + at) =
+            make_uint2(*reinterpret_cast<uint32_t*>(&a), *reinterpret_cast<uint32_t*>(&b));
+      } else {
+        __half2 a = __floats2half2_rn(acc.x, acc.y);
+        __half2 b = __floats2half2_rn(acc.z, acc.w);
+        *reinterpret_cast<uint2*>(static_cast<__half*>(out) + at) =
+            make_uint2(*reinterpret_cast<uint32_t*>(&a), *reinterpret_cast<uint32_t*>(&b));
+      }
     }
-    const int64_t at = t * K + n4;
-    if (out_dt == kF32) {
-      *reinterpret_cast<float4*>(static_cast<float*>(out) + at) = acc;
-    } else if (out_dt == kBF16) {
-      __nv_bfloat162 a = __floats2bfloat162_rn(acc.x, acc.y);
-      __nv_bfloat162 b = __floats2bfloat162_rn(acc.z, acc.w);
-      *reinterpret_cast<uint2*>(static_cast<__nv_bfloat16*>(out) + at) =
-          make_uint2(*reinterpret_cast<uint32_t*>(&a), *reinterpret_cast<uint32_t*>(&b));
-    } else {
-      __half2 a = __floats2half2_rn(acc.x, acc.y);
-      __half2 b = __floats2half2_rn(acc.z, acc.w);
-      *reinterpret_cast<uint2*>(static_cast<__half*>(out) + at) =
-          make_uint2(*reinterpret_cast<uint32_t*>(&a), *reinterpret_cast<uint32_t*>(&b));
+  }
+  // every block has read this step's epoch; the last one moves it on
+  __syncthreads();
+  if (threadIdx.x == 0) {
+    __threadfence();
+    const unsigned int total = gridDim.x * gridDim.y;
+    if (atomicAdd(&dev->final_count, 1u) + 1u == total) {
+      dev->final_count = 0u;
+      __threadfence();
+      dev->epoch = epoch + 1ull;
     }
   }
 }
@@ -298,9 +264,9 @@ struct sbb200_ep {
   sbb::EpDev* dev = nullptr;          // local device state
   sbb::EpTables* tab = nullptr;       // device copy of the peer tables
   sbb::EpTables host_tab{};
-  int32_t* local_ids = nullptr;       // [world * max_tokens, top_k]
-  float* local_w = nullptr;
+  int32_t* local_ids = nullptr;       // [world * max_tokens, top_k] (larger steps)
   void* workspace = nullptr;          // MoE workspace for world * max_tokens tokens
+  bool fused = false;                 // steps exchanged by the activation split
   sbb::WorkspacePlan plan{};
   bool connected = false;
   std::mutex mu;
@@ -331,7 +297,6 @@ void ep_free(sbb200_ep* p) {
   cudaFree(p->dev);
   cudaFree(p->tab);
   cudaFree(p->local_ids);
-  cudaFree(p->local_w);
   cudaFree(p->workspace);
 }
 
@@ -381,15 +346,20 @@ sbb200_ep_t* sbb200_ep_create(int device, int rank, int world, size_t max_tokens
     const size_t vt = static_cast<size_t>(world) * max_tokens;
     const size_t e_local_max = (E + world - 1) / world;
     p->plan = sbb::plan_workspace(vt, e_local_max, top_k, K, I);
+    p->fused = sbb::ep_split_fits(static_cast<int64_t>(vt), static_cast<int>(top_k),
+                                  static_cast<int>(K), static_cast<int>(I),
+                                  static_cast<int>(e_local_max));
     DeviceGuard g(device);
     cudaError_t e = g.ok ? cudaSuccess : cudaErrorInvalidDevice;
     if (e == cudaSuccess) e = cudaMalloc(&p->ex, p->lay.total);
     if (e == cudaSuccess) e = cudaMemset(p->ex, 0, p->lay.hidden);  // ready and done flags
     if (e == cudaSuccess) e = cudaMalloc(&p->dev, sizeof(sbb::EpDev));
-    if (e == cudaSuccess) e = cudaMemset(p->dev, 0, sizeof(sbb::EpDev));
+    // epochs start at 1, so the zeroed flags match no step
+    sbb::EpDev init{};
+    init.epoch = 1ull;
+    if (e == cudaSuccess) e = cudaMemcpy(p->dev, &init, sizeof init, cudaMemcpyHostToDevice);
     if (e == cudaSuccess) e = cudaMalloc(&p->tab, sizeof(sbb::EpTables));
-    if (e == cudaSuccess) e = cudaMalloc(&p->local_ids, vt * top_k * 4);
-    if (e == cudaSuccess) e = cudaMalloc(&p->local_w, vt * top_k * 4);
+    if (e == cudaSuccess && !p->fused) e = cudaMalloc(&p->local_ids, vt * top_k * 4);
     if (e == cudaSuccess) e = cudaMalloc(&p->workspace, p->plan.total);
     if (e == cudaSuccess) e = cudaDeviceSynchronize();
     if (e != cudaSuccess) {
@@ -450,8 +420,7 @@ int sbb200_ep_connect(sbb200_ep_t* p, const void* handles, size_t size) {
     t.peer_hidden[r] = b + p->lay.hidden;
     t.peer_ids[r] = reinterpret_cast<const int32_t*>(b + p->lay.ids);
     t.peer_weights[r] = reinterpret_cast<const float*>(b + p->lay.weights);
-    t.partial_at_peer[r] =
-        reinterpret_cast<float*>(b + p->lay.partial) + static_cast<size_t>(p->rank) * p->max_tokens * p->K;
+    t.partial_at_peer[r] = reinterpret_cast<float*>(b + p->lay.partial);
   }
   for (int r = 0; r <= p->world; ++r) {
     size_t b = 0, c = 0;
@@ -499,42 +468,61 @@ int sbb200_ep_forward_staged(sbb200_ep_t* p, void* stream, const void* hidden,
     mark(0);
     const int64_t K = static_cast<int64_t>(p->K);
     const int64_t routes = static_cast<int64_t>(M * p->top_k);
+    const int64_t vt = static_cast<int64_t>(p->world) * p->max_tokens;
     char* ex = p->ex;
-    // 1. publish
-    {
+    char* tab = reinterpret_cast<char*>(p->tab);  // device address, not dereferenced here
+    sbb::EpSplitArgs xa{};
+    if (p->fused) {
+      // the activation split publishes, announces and gathers the step itself
+      xa.tab = p->tab;
+      xa.dev = p->dev;
+      xa.ready = reinterpret_cast<const unsigned long long*>(ex + p->lay.ready);
+      xa.hidden = hidden;
+      xa.ids = topk_ids;
+      xa.weights = topk_weights;
+      xa.ex_hidden = ex + p->lay.hidden;
+      xa.ex_ids = reinterpret_cast<int32_t*>(ex + p->lay.ids);
+      xa.ex_weights = reinterpret_cast<float*>(ex + p->lay.weights);
+      xa.world = p->world;
+      xa.rank = p->rank;
+      xa.act_bytes = static_cast<int>(sbb::act_size(p->act_dt));
+      xa.M = static_cast<int64_t>(M);
+      xa.max_tokens = static_cast<int64_t>(p->max_tokens);
+      mark(1);
+      mark(2);
+    } else {
+      // 1. publish
       const int64_t vec = static_cast<int64_t>(M) * K * sbb::act_size(p->act_dt) / 16;
-      int blocks = static_cast<int>(std::min<int64_t>(148 * 4, (vec + sbb::kEpThreads - 1) / sbb::kEpThreads));
+      int blocks = static_cast<int>(
+          std::min<int64_t>(148 * 4, (vec + sbb::kEpThreads - 1) / sbb::kEpThreads));
       if (blocks < 1) blocks = 1;
-      sbb::ep_publish_kernel<<<blocks, sbb::kEpThreads, 0, s>>>(
+      cudaError_t e = sbb::launch_kernel(
+          true, sbb::ep_publish_kernel, dim3(blocks), dim3(sbb::kEpThreads), 0, s,
           static_cast<const uint4*>(hidden), vec, topk_ids, topk_weights, routes,
           reinterpret_cast<uint4*>(ex + p->lay.hidden), reinterpret_cast<int32_t*>(ex + p->lay.ids),
-          reinterpret_cast<float*>(ex + p->lay.weights), p->dev);
-      const cudaError_t e = cudaGetLastError();
+          reinterpret_cast<float*>(ex + p->lay.weights));
       if (e != cudaSuccess) return ep_fail(SBB200_ECUDA, std::string("ep publish: ") + cudaGetErrorString(e));
-    }
-    mark(1);
-    // 2. gather the local routes of every source
-    const int64_t vt = static_cast<int64_t>(p->world) * p->max_tokens;
-    {
+      mark(1);
+      // 2. gather the local routes of every source
       const int64_t total = vt * p->top_k;
-      const int blocks = static_cast<int>(std::min<int64_t>(148 * 2, (total + sbb::kEpThreads - 1) / sbb::kEpThreads));
-      const cudaError_t e = sbb::launch_kernel(
-          true, sbb::ep_gather_kernel, dim3(blocks), dim3(sbb::kEpThreads), 0, s,
-          reinterpret_cast<const unsigned long long*>(ex + p->lay.ready), p->dev,
-          static_cast<const sbb::EpTables*>(p->tab), p->world,
-          static_cast<int64_t>(p->max_tokens), static_cast<int>(p->top_k), p->rank,
-          static_cast<int64_t>(M), p->local_ids, p->local_w);
+      blocks = static_cast<int>(
+          std::min<int64_t>(148 * 2, (total + sbb::kEpThreads - 1) / sbb::kEpThreads));
+      e = sbb::launch_kernel(true, sbb::ep_gather_kernel, dim3(blocks), dim3(sbb::kEpThreads), 0,
+                             s, reinterpret_cast<const unsigned long long*>(ex + p->lay.ready),
+                             p->dev, static_cast<const sbb::EpTables*>(p->tab), p->world,
+                             static_cast<int64_t>(p->max_tokens), static_cast<int>(p->top_k),
+                             p->rank, static_cast<int64_t>(M), p->local_ids);
       if (e != cudaSuccess) return ep_fail(SBB200_ECUDA, std::string("ep gather: ") + cudaGetErrorString(e));
+      mark(2);
     }
-    mark(2);
     // 3. the shard's MoE on the virtual tokens: rows pulled from their
-    // sources, partials pushed back, done flags raised
+    // sources, each route's row pushed back to its source
     {
       sbb::MoeArgs a{};
       a.hidden = nullptr;
       a.act_dt = p->act_dt;
       a.ids = p->local_ids;
-      a.weights = p->local_w;
+      a.weights = nullptr;  // router weights are applied by the source's final sum
       a.multiply_router_weight = multiply_router_weight;
       a.w13 = static_cast<const uint8_t*>(w13);
       a.s13 = static_cast<const uint8_t*>(w13_scales);
@@ -551,33 +539,34 @@ int sbb200_ep_forward_staged(sbb200_ep_t* p, void* stream, const void* hidden,
       a.K = static_cast<int>(p->K);
       a.I = static_cast<int>(p->I);
       // the expert step's own marks land in events [2..6]: [3] after the
-      // route plan and split, [4] after gate/up, [5] after down, [6] after
-      // the combine push
+      // split (exchange, route plan), [4] after gate/up, [5] after down
+      // (including the pushes), [6] = [5] (no combine)
       a.stage_events = stage_events ? stage_events + 2 : nullptr;
-      // device addresses of the tables inside p->tab (never dereferenced here)
-      char* tab = reinterpret_cast<char*>(p->tab);
-      a.hidden_rows = sbb::SplitRows{
-          reinterpret_cast<const void* const*>(tab + offsetof(sbb::EpTables, peer_hidden)),
-          static_cast<int64_t>(p->max_tokens)};
-      a.out_rows = sbb::SplitRows{
-          reinterpret_cast<const void* const*>(tab + offsetof(sbb::EpTables, partial_at_peer)),
+      if (p->fused) {
+        a.ep_split = &xa;
+      } else {
+        a.hidden_rows = sbb::SplitRows{
+            reinterpret_cast<const void* const*>(tab + offsetof(sbb::EpTables, peer_hidden)),
+            static_cast<int64_t>(p->max_tokens)};
+      }
+      a.push = sbb::PushRows{
+          reinterpret_cast<float* const*>(tab + offsetof(sbb::EpTables, partial_at_peer)),
           static_cast<int64_t>(p->max_tokens)};
       std::string why;
       const cudaError_t e = sbb::run_moe(a, p->plan, p->workspace, s, &why);
       if (e != cudaSuccess) return ep_fail(SBB200_ECUDA, "ep expert step (" + why + "): " + cudaGetErrorString(e));
     }
-    // 4. sum the partials of this rank's tokens
-    // (with no tokens here the kernel still consumes the done flags, so the
-    // exchange stays in step)
+    // 4. sum the routes of this rank's tokens (with no tokens here the kernel
+    // still raises and consumes the done flags, so the exchange stays in step)
     const dim3 grid(M > 0 ? static_cast<unsigned>(M) : 1u,
-                    M > 0 ? static_cast<unsigned>((K + 4 * sbb::kEpThreads - 1) / (4 * sbb::kEpThreads)) : 1u);
+                    static_cast<unsigned>((K + 4 * sbb::kEpThreads - 1) / (4 * sbb::kEpThreads)));
     const cudaError_t e = sbb::launch_kernel(
         true, sbb::ep_final_kernel, grid, dim3(sbb::kEpThreads), 0, s,
         reinterpret_cast<const unsigned long long*>(ex + p->lay.done), p->dev,
-        static_cast<const sbb::EpTables*>(p->tab), p->world, p->rank, M > 0 ? topk_ids : nullptr,
-        M > 0 ? static_cast<int>(p->top_k) : 0, static_cast<int>(p->E),
-        reinterpret_cast<const float*>(ex + p->lay.partial), static_cast<int64_t>(p->max_tokens),
-        M > 0 ? static_cast<int>(K) : 0, out, out_dt);
+        static_cast<const sbb::EpTables*>(p->tab), p->world, p->rank, topk_ids, topk_weights,
+        multiply_router_weight, static_cast<int>(p->top_k), static_cast<int>(p->E),
+        reinterpret_cast<const float*>(ex + p->lay.partial), static_cast<int64_t>(M),
+        static_cast<int>(K), out, out_dt);
     if (e != cudaSuccess) return ep_fail(SBB200_ECUDA, std::string("ep final: ") + cudaGetErrorString(e));
     mark(7);
     return SBB200_OK;
@@ -598,11 +587,13 @@ int sbb200_ep_forward(sbb200_ep_t* p, void* stream, const void* hidden, const in
 
 int sbb200_ep_launches(const sbb200_ep_t* p) {
   if (!p) return -1;
-  // publish + gather, the expert step on world * max_tokens virtual tokens
-  // (rows read from peers, so the route plan is its own kernel), final
+  // exchange split, gate/up, SwiGLU split, down (pushing), final; larger
+  // steps: publish, gather, route plan (1 or 2), split, gate/up, SwiGLU
+  // split, down, final. No combine kernel either way.
+  if (p->fused) return 5;
   const int64_t vt = static_cast<int64_t>(p->world) * p->max_tokens;
   return 2 + sbb::count_launches(vt, static_cast<int>(p->top_k), static_cast<int>(p->K),
-                                 static_cast<int>(p->I), false) + 1;
+                                 static_cast<int>(p->I), false) - 1 + 1;
 }
 
 int sbb200_ep_device_errors(sbb200_ep_t* p, void* stream, uint32_t* errors) {

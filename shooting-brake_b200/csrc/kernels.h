@@ -54,14 +54,63 @@ struct SplitRows {
   int64_t rows_per_src;
 };
 
+// ---- expert parallelism (ep.cu) ------------------------------------------
+constexpr int kMaxWorld = 64;
+
+// Peer addresses of one rank's exchange (device memory, filled at connect).
+struct EpTables {
+  unsigned long long* ready_at_peer[kMaxWorld];  // &peer.ready[rank]
+  unsigned long long* done_at_peer[kMaxWorld];   // &peer.done[rank]
+  const void* peer_hidden[kMaxWorld];
+  const int32_t* peer_ids[kMaxWorld];
+  const float* peer_weights[kMaxWorld];
+  float* partial_at_peer[kMaxWorld];  // peer's partial [max_tokens, top_k, K] fp32
+  int shard_begin[kMaxWorld + 1];
+};
+
+// Device-side state of one rank (local memory).
+struct EpDev {
+  unsigned long long epoch;   // epoch of the current step (bumped by the last
+                              // CTA of the step's final kernel)
+  unsigned int errors;        // bit 0: a wait for another rank timed out
+  unsigned int final_count;   // CTAs of the final kernel done reading epoch
+  unsigned int publish_count; // CTAs of the exchange split done publishing
+  unsigned int pad[3];
+};
+
+constexpr uint64_t kEpWaitNs = 2000000000ull;  // 2 s per cross-GPU wait
+
+// One expert-parallel step whose virtual routes (world * max_tokens *
+// top_k) fit the in-kernel route plan: the activation split publishes this
+// rank's tokens, raises its ready flag, waits for every rank's, plans the
+// local routes and pulls the routed rows itself (no publish, gather or plan
+// kernel).
+struct EpSplitArgs {
+  const EpTables* tab;               // device
+  EpDev* dev;                        // device
+  const unsigned long long* ready;   // this rank's ready flags [world]
+  const void* hidden;                // this rank's tokens [M, K] (caller memory)
+  const int32_t* ids;                // [M, top_k] global expert ids
+  const float* weights;              // [M, top_k]
+  void* ex_hidden;                   // this rank's exchange buffer regions
+  int32_t* ex_ids;
+  float* ex_weights;
+  int world, rank, act_bytes;
+  int64_t M, max_tokens;
+};
+
+// Down projection results pushed to their source ranks: route r = v * top_k
+// + k of virtual token v = s * rows_per_src + t goes to row (t * top_k + k)
+// of base[s] (fp32 [rows_per_src, top_k, K]).
+struct PushRows {
+  float* const* base;  // device array [world]
+  int64_t rows_per_src;
+};
+
 // out[t, :] = sum over valid k of w[t, k] * y[slot_of[t*top_k + k], :], k ascending.
-// With `dst` set (expert-parallel partials), fp32 row t goes to dst.base[t /
-// rows_per_src] + (t % rows_per_src) * K and rows without a valid route are
-// not written.
 cudaError_t launch_combine(const float* y, const int32_t* slot_of, const float* weights,
                            int multiply_router_weight, void* out, int out_dt, int64_t M,
-                           int top_k, int K, cudaStream_t stream,
-                           const SplitRows* dst = nullptr);
+                           int top_k, int K, cudaStream_t stream);
 
 // Bit-exact NVFP4 dequant: out[r, c] = e2m1 * fp32(e4m3 * g[r / rows_per_scale]).
 cudaError_t launch_dequant(const uint8_t* q, const uint8_t* sf, const float* g,
@@ -109,6 +158,11 @@ struct BsLaunch {
   int E, top_k, K, I;
   void (*stage_mark)(void* ctx, int stage);
   void* stage_ctx;
+  // expert parallel: the split exchanges the step itself (ep != nullptr;
+  // M is then world * max_tokens virtual tokens) and/or the down projection
+  // pushes its rows to the sources (push.base != nullptr, no y)
+  const EpSplitArgs* ep = nullptr;
+  PushRows push{nullptr, 1};
 };
 
 bool bs_supported(int K, int I);

@@ -99,6 +99,12 @@ struct BsParams {
                         // flight (prefill): both evict_normal
   uint64_t wait_ns;     // limit of every pipeline wait, counted from the
                         // moment the previous kernel's results are visible
+  // down, expert parallel: rows go to their source ranks (PushRows), found
+  // through the route id of each slot
+  const int32_t* sorted;
+  float* const* push_base;
+  int64_t push_rows;
+  int top_k;
 };
 
 template <int MODE, int BNR, int NT>
@@ -165,7 +171,7 @@ __device__ __forceinline__ bool warp_wait(uint64_t* bar, uint32_t parity, volati
   for (uint32_t i = 0;; ++i) {
     const bool done = mbar_try_wait(bar, parity);
     if (__all_sync(0xffffffffu, done)) return true;
-    if ((i & 15) == 15) {
+    if ((i & 15) == 0) {
       int stop = 0;
       if (lane == 0) {
         stop = *abort || now_ns() > deadline;
@@ -468,6 +474,15 @@ __global__ void __launch_bounds__(kThreads, 1)
               v1 = fmaf(__uint_as_float(t1[jj * NT + tt]), g, v1);
             }
             float* orow = p.out + static_cast<int64_t>(slot) * p.out_ld;
+            if (MODE == kDown && p.push_base) {
+              // route r = v * top_k + k of virtual token v = src * rows + t:
+              // row (t * top_k + k) of the source's partial buffer
+              const int32_t rv = p.sorted[slot];
+              const int64_t v = rv / p.top_k;
+              const int64_t src = v / p.push_rows;
+              orow = p.push_base[src] +
+                     ((v - src * p.push_rows) * p.top_k + (rv - v * p.top_k)) * p.out_ld;
+            }
             if (MODE == kGateUp) {
               const float gv = v0 * gs, uv = v1 * gs;
               orow[mt * kM + r] = silu(gv) * uv;
@@ -593,6 +608,54 @@ __device__ __forceinline__ void quant_block(float* v, float G, float g, uint32_t
   *scale_byte = static_cast<uint8_t>(s8);
 }
 
+// The dynamic-global split of one row held in registers, one 16-element
+// block per thread (v; active: the block lies inside the row): the row
+// maximum by a CTA reduction, then NT residual terms under G0 * 4^t written
+// to every destination row dst[d] (d < ndst, -1 skipped), or to `row` alone
+// when dst is null. Every thread of the CTA calls it; s_max holds 32 floats.
+__device__ __forceinline__ void split_row_terms(float* v, bool active, int NT, int K,
+                                                const int32_t* dst, int ndst, int64_t row,
+                                                uint8_t* q, uint8_t* sf, float* gout,
+                                                float* s_max) {
+  const int tid = threadIdx.x;
+  const int nwarps = blockDim.x >> 5;
+  const int blk = tid;
+  float amax = 0.0f;
+  if (active) {
+#pragma unroll
+    for (int i = 0; i < 16; ++i) amax = fmaxf(amax, fabsf(v[i]));
+  }
+#pragma unroll
+  for (int d = 16; d > 0; d >>= 1) amax = fmaxf(amax, __shfl_xor_sync(0xffffffffu, amax, d));
+  if ((tid & 31) == 0) s_max[tid >> 5] = amax;
+  __syncthreads();
+  amax = s_max[0];
+  for (int w = 1; w < nwarps; ++w) amax = fmaxf(amax, s_max[w]);
+  const float G0 = amax > 0.0f ? __fdiv_rn(2688.0f, amax) : 1.0f;
+  const float g0 = __fdiv_rn(1.0f, G0);
+  if (tid < ndst) {
+    const int64_t d = dst ? static_cast<int64_t>(dst[tid]) : row;
+    if (d >= 0)
+      for (int t = 0; t < NT; ++t) gout[d * NT + t] = ldexpf(g0, -2 * t);
+  }
+  if (!active) return;
+  float G = G0, g = g0;
+  for (int t = 0; t < NT; ++t) {
+    uint32_t w[2];
+    uint8_t s8;
+    quant_block<true>(v, G, g, w, &s8);
+    for (int i = 0; i < ndst; ++i) {
+      const int64_t d = dst ? static_cast<int64_t>(dst[i]) : row;
+      if (d < 0) continue;
+      const int64_t orow = d * NT + t;
+      *reinterpret_cast<uint2*>(q + orow * (K / 2) + blk * 8) = make_uint2(w[0], w[1]);
+      sf[orow * (K / 16) + blk] = s8;
+    }
+    G = __fmul_rn(G, 4.0f);
+    g = __fmul_rn(g, 0.25f);
+  }
+}
+
 // Route plan of a small call (R = gridDim.x * top_k <= kInlinePlanRoutes
 // routes, blockDim >= kSplitThreads) computed inside the token-mode split, so
 // no separate plan kernel runs ahead of it. Every CTA histograms all route
@@ -614,19 +677,24 @@ struct InlinePlan {
 constexpr int kInlinePer = kInlinePlanRoutes / kSplitThreads;  // route ids per thread
 
 // s_off: kMaxExperts + 1 entries; s_rank, s_exp, s_dst: top_k entries.
+// id_of(r) is the expert id of route r (r < R = gridDim.x * top_k); ids
+// outside [0, E) are dropped, and counted in *status unless they are -1.
 // Ends with every s_dst entry written and visible to the CTA.
-__device__ __forceinline__ void inline_route_slots(const InlinePlan& plan, int64_t row, int top_k,
-                                                   int32_t* s_off, int32_t* s_rank, int32_t* s_exp,
-                                                   int32_t* s_dst) {
+template <class IdOf>
+__device__ __forceinline__ void plan_route_slots(IdOf id_of, int E, int64_t row, int top_k,
+                                                 int32_t* counts, int32_t* offsets,
+                                                 int32_t* sorted, int32_t* slot_of,
+                                                 uint32_t* status, int32_t* s_off,
+                                                 int32_t* s_rank, int32_t* s_exp,
+                                                 int32_t* s_dst) {
   const int tid = threadIdx.x;
   const int lane = tid & 31;
-  const int E = plan.E;
   const int R = static_cast<int>(gridDim.x) * top_k;
   const int r0 = static_cast<int>(row) * top_k;
   for (int e = tid; e <= E; e += blockDim.x) s_off[e] = 0;
   for (int i = tid; i < top_k; i += blockDim.x) {
     s_rank[i] = 0;
-    s_exp[i] = plan.ids[r0 + i];
+    s_exp[i] = id_of(r0 + i);
   }
   __syncthreads();
   int32_t mine[kInlinePer];
@@ -634,12 +702,12 @@ __device__ __forceinline__ void inline_route_slots(const InlinePlan& plan, int64
 #pragma unroll
   for (int j = 0; j < kInlinePer; ++j) {
     const int r = tid + j * static_cast<int>(blockDim.x);
-    const int32_t e = r < R ? plan.ids[r] : -1;
+    const int32_t e = r < R ? id_of(r) : -1;
     mine[j] = e;
     if (e >= 0 && e < E) atomicAdd(&s_off[e], 1);
     else if (e != -1) ++bad;
   }
-  if (bad && blockIdx.x == 0) atomicAdd(plan.status, bad);
+  if (bad && blockIdx.x == 0 && status) atomicAdd(status, bad);
   // rank of each of the token's routes among the earlier routes of its expert
   for (int i = 0; i < top_k; ++i) {
     const int32_t e = s_exp[i];  // the same for every thread of the CTA
@@ -675,17 +743,26 @@ __device__ __forceinline__ void inline_route_slots(const InlinePlan& plan, int64
     const int32_t e = s_exp[i];
     const int32_t slot = (e >= 0 && e < E) ? s_off[e] + s_rank[i] : -1;
     s_dst[i] = slot;
-    plan.slot_of[r0 + i] = slot;
-    if (slot >= 0) plan.sorted[slot] = r0 + i;
+    slot_of[r0 + i] = slot;
+    if (slot >= 0) sorted[slot] = r0 + i;
   }
   if (blockIdx.x == 0) {
     for (int e = tid; e < E; e += blockDim.x) {
-      plan.counts[e] = s_off[e + 1] - s_off[e];
-      plan.offsets[e] = s_off[e];
+      counts[e] = s_off[e + 1] - s_off[e];
+      offsets[e] = s_off[e];
     }
-    if (tid == 0) plan.offsets[E] = s_off[E];
+    if (tid == 0) offsets[E] = s_off[E];
   }
   __syncthreads();
+}
+
+__device__ __forceinline__ void inline_route_slots(const InlinePlan& plan, int64_t row, int top_k,
+                                                   int32_t* s_off, int32_t* s_rank, int32_t* s_exp,
+                                                   int32_t* s_dst) {
+  const int32_t* ids = plan.ids;
+  plan_route_slots([ids](int r) { return ids[r]; }, plan.E, row, top_k, plan.counts,
+                   plan.offsets, plan.sorted, plan.slot_of, plan.status, s_off, s_rank, s_exp,
+                   s_dst);
 }
 
 // gstatic != nullptr (W4A4 with static activation globals, NT = 1): the
@@ -710,7 +787,6 @@ __global__ void __launch_bounds__(1024) split_nvfp4_kernel(
   pdl_trigger();
   if (n_rows_dev && row >= static_cast<int64_t>(*n_rows_dev)) return;
   const int tid = threadIdx.x;
-  const int nwarps = blockDim.x >> 5;
   int ndst = 1;
   const bool token = slot_of != nullptr || plan.ids != nullptr;  // token mode
   if (token) {
@@ -767,40 +843,122 @@ __global__ void __launch_bounds__(1024) split_nvfp4_kernel(
     }
     return;
   }
-  float amax = 0.0f;
-  if (active) {
-#pragma unroll
-    for (int i = 0; i < 16; ++i) amax = fmaxf(amax, fabsf(v[i]));
-  }
-#pragma unroll
-  for (int d = 16; d > 0; d >>= 1) amax = fmaxf(amax, __shfl_xor_sync(0xffffffffu, amax, d));
-  if ((tid & 31) == 0) s_max[tid >> 5] = amax;
-  __syncthreads();
-  amax = s_max[0];
-  for (int w = 1; w < nwarps; ++w) amax = fmaxf(amax, s_max[w]);
-  const float G0 = amax > 0.0f ? __fdiv_rn(2688.0f, amax) : 1.0f;
-  const float g0 = __fdiv_rn(1.0f, G0);
-  if (tid < ndst) {
-    const int64_t dst = token ? static_cast<int64_t>(s_dst[tid]) : row;
-    if (dst >= 0)
-      for (int t = 0; t < NT; ++t) gout[dst * NT + t] = ldexpf(g0, -2 * t);
-  }
-  if (!active) return;
-  float G = G0, g = g0;
-  for (int t = 0; t < NT; ++t) {
-    uint32_t w[2];
-    uint8_t s8;
-    quant_block<true>(v, G, g, w, &s8);
-    for (int d = 0; d < ndst; ++d) {
-      const int64_t dst = token ? static_cast<int64_t>(s_dst[d]) : row;
-      if (dst < 0) continue;
-      const int64_t orow = dst * NT + t;
-      *reinterpret_cast<uint2*>(q + orow * (K / 2) + blk * 8) = make_uint2(w[0], w[1]);
-      sf[orow * (K / 16) + blk] = s8;
+  split_row_terms(v, active, NT, K, token ? s_dst : nullptr, ndst, row, q, sf, gout, s_max);
+}
+
+// Expert-parallel exchange split (EpSplitArgs): one CTA per virtual token
+// v = src * max_tokens + t of the whole world's step, blockDim as the split.
+//  1. The CTAs of this rank's own tokens copy their row, ids and weights into
+//     the exchange buffer; each writer fences at system scope, and the last
+//     of them (a completion count) raises ready = epoch << 32 | M on every
+//     other rank.
+//  2. Every CTA waits (bounded) for the other ranks' ready flags, reads every
+//     rank's ids (its own from the caller, the others' over NVLink), keeps
+//     the routes to this rank's experts and plans their slots in the stable
+//     (expert, virtual route) order, like the single-GPU in-split plan.
+//  3. A CTA whose token has a local route reads the row (from the caller, or
+//     from the source GPU through L2 only) and splits it into its slots.
+// The publishing CTAs raise the flag before they wait, and the waiting CTAs
+// need nothing from this rank's publishers, so the grid completes even when
+// it is not all resident at once.
+__global__ void __launch_bounds__(1024) ep_split_kernel(
+    const EpSplitArgs a, int src_dt, int top_k, int K, int NT, int32_t* __restrict__ counts,
+    int32_t* __restrict__ offsets, int32_t* __restrict__ sorted, int32_t* __restrict__ slot_of,
+    uint32_t* __restrict__ status, uint8_t* __restrict__ q, uint8_t* __restrict__ sf,
+    float* __restrict__ gout) {
+  __shared__ float s_max[32];
+  __shared__ int32_t s_dst[kMaxTopK];
+  __shared__ int32_t s_off[kMaxExperts + 1];
+  __shared__ int32_t s_rank[kMaxTopK];
+  __shared__ int32_t s_exp[kMaxTopK];
+  __shared__ int64_t s_cnt[kMaxWorld];
+  __shared__ int s_any;
+  pdl_wait();
+  pdl_trigger();
+  const int tid = threadIdx.x;
+  const int64_t v = blockIdx.x;
+  const int src = static_cast<int>(v / a.max_tokens);
+  const int64_t t = v - static_cast<int64_t>(src) * a.max_tokens;
+  const EpTables* tab = a.tab;
+  const unsigned long long epoch = a.dev->epoch;
+  if (v == 0 && tid < 2) status[tid] = 0u;  // bad-id count, error word of this call
+  // 1. publish this rank's tokens
+  const int64_t publishers = a.M > 0 ? a.M : 1;
+  if (src == a.rank && t < publishers) {
+    if (t < a.M) {
+      const int64_t vec = static_cast<int64_t>(K) * a.act_bytes / 16;
+      const uint4* from = static_cast<const uint4*>(a.hidden) + t * vec;
+      uint4* to = static_cast<uint4*>(a.ex_hidden) + t * vec;
+      for (int64_t i = tid; i < vec; i += blockDim.x) to[i] = from[i];
+      for (int i = tid; i < top_k; i += blockDim.x) {
+        a.ex_ids[t * top_k + i] = a.ids[t * top_k + i];
+        a.ex_weights[t * top_k + i] = a.weights[t * top_k + i];
+      }
+      __threadfence_system();
     }
-    G = __fmul_rn(G, 4.0f);
-    g = __fmul_rn(g, 0.25f);
+    __syncthreads();
+    if (tid == 0) {
+      __threadfence_system();
+      const unsigned int done = atomicAdd(&a.dev->publish_count, 1u) + 1u;
+      if (done == static_cast<unsigned int>(publishers)) {
+        a.dev->publish_count = 0u;
+        __threadfence_system();
+        const unsigned long long val = (epoch << 32) | static_cast<unsigned long long>(a.M);
+        for (int d = 0; d < a.world; ++d)
+          if (d != a.rank) st_release_sys(tab->ready_at_peer[d], val);
+      }
+    }
   }
+  // 2. every rank's token count, then the plan of the local routes
+  const uint64_t deadline = globaltimer_ns() + kEpWaitNs;
+  for (int s2 = tid; s2 < a.world; s2 += blockDim.x) {
+    unsigned long long seen = 0;
+    if (s2 == a.rank) {
+      s_cnt[s2] = a.M;
+    } else {
+      s_cnt[s2] = ep_wait_epoch(&a.ready[s2], epoch, true, &seen, &a.dev->errors, deadline)
+                      ? static_cast<int64_t>(seen & 0xffffffffull)
+                      : 0;
+    }
+  }
+  __syncthreads();
+  const int e_lo = tab->shard_begin[a.rank];
+  const int e_hi = tab->shard_begin[a.rank + 1];
+  const int64_t mt = a.max_tokens;
+  const int rank = a.rank;
+  const int32_t* own_ids = a.ids;
+  auto id_of = [&](int r) -> int32_t {
+    const int64_t vv = r / top_k;
+    const int ss = static_cast<int>(vv / mt);
+    const int64_t tt = vv - static_cast<int64_t>(ss) * mt;
+    if (tt >= s_cnt[ss]) return -1;
+    const int64_t at = tt * top_k + (r - vv * top_k);
+    const int32_t e = ss == rank ? own_ids[at] : __ldcg(tab->peer_ids[ss] + at);
+    return (e >= e_lo && e < e_hi) ? e - e_lo : -1;
+  };
+  plan_route_slots(id_of, e_hi - e_lo, v, top_k, counts, offsets, sorted, slot_of, nullptr,
+                   s_off, s_rank, s_exp, s_dst);
+  // 3. the token's row into its slots
+  if (t >= s_cnt[src]) return;  // the whole CTA leaves together
+  if (tid == 0) s_any = 0;
+  __syncthreads();
+  for (int i = tid; i < top_k; i += blockDim.x)
+    if (s_dst[i] >= 0) s_any = 1;
+  __syncthreads();
+  if (!s_any) return;
+  const bool active = tid * 16 < K;
+  float x[16];
+  if (active) {
+    const int64_t at = t * K + tid * 16;
+    if (src == a.rank) {
+      load8(a.hidden, src_dt, at, x);
+      load8(a.hidden, src_dt, at + 8, x + 8);
+    } else {
+      load8<true>(tab->peer_hidden[src], src_dt, at, x);
+      load8<true>(tab->peer_hidden[src], src_dt, at + 8, x + 8);
+    }
+  }
+  split_row_terms(x, active, NT, K, s_dst, top_k, 0, q, sf, gout, s_max);
 }
 
 // ---- host ---------------------------------------------------------------------
@@ -999,14 +1157,33 @@ cudaError_t launch_moe_bs(const BsLaunch& a, cudaStream_t stream, const char** s
   p2.out_ld = a.K;
   p2.stream_weights = R <= static_cast<int64_t>(a.E) * (bnr2 / NT);
 
+  if (a.push.base) {
+    // expert parallel: rows go back to their source ranks, unweighted
+    p2.push_base = a.push.base;
+    p2.push_rows = a.push.rows_per_src;
+    p2.sorted = a.sorted;
+    p2.top_k = a.top_k;
+  }
+
   // 1. split each token once; its terms go to all of its route slots (for a
-  //    small call the split also computes the route plan)
+  //    small call the split also computes the route plan, and in an
+  //    expert-parallel step it also exchanges the step with the other ranks)
   *step = "activation split";
-  const InlinePlan plan{a.inline_plan ? a.ids : nullptr, a.E, a.counts, a.offsets, a.sorted,
-                        a.slot_of, a.status};
-  cudaError_t err = launch_split(a.hidden, a.act_dt, &a.hidden_rows, a.slot_of, a.top_k, nullptr,
-                                 a.M, a.K, NT, a.xq, a.xsf, a.xg, a.a13_gscale, a.ids, a.sorted,
-                                 stream, &plan);
+  cudaError_t err = cudaSuccess;
+  if (a.ep) {
+    if (a.K % 16 != 0 || a.K / 16 > 1024 || a.M * a.top_k > kInlinePlanRoutes ||
+        a.a13_gscale || a.E > kMaxExperts)
+      return cudaErrorInvalidValue;
+    const int threads = std::max(kSplitThreads, (a.K / 16 + 31) / 32 * 32);
+    err = launch_kernel(true, ep_split_kernel, dim3(static_cast<unsigned>(a.M)), dim3(threads), 0,
+                        stream, *a.ep, a.act_dt, a.top_k, a.K, NT, a.counts, a.offsets, a.sorted,
+                        a.slot_of, a.status, a.xq, a.xsf, a.xg);
+  } else {
+    const InlinePlan plan{a.inline_plan ? a.ids : nullptr, a.E, a.counts, a.offsets, a.sorted,
+                          a.slot_of, a.status};
+    err = launch_split(a.hidden, a.act_dt, &a.hidden_rows, a.slot_of, a.top_k, nullptr, a.M, a.K,
+                       NT, a.xq, a.xsf, a.xg, a.a13_gscale, a.ids, a.sorted, stream, &plan);
+  }
   if (err != cudaSuccess) return err;
   if (a.stage_mark) a.stage_mark(a.stage_ctx, 1);
   // 2. gate/up + SwiGLU

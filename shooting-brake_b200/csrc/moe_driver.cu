@@ -41,6 +41,11 @@ WorkspacePlan plan_workspace(size_t M, size_t E, size_t top_k, size_t K, size_t 
   return p;
 }
 
+bool ep_split_fits(int64_t virtual_tokens, int top_k, int K, int I, int E_local) {
+  return virtual_tokens > 0 && virtual_tokens * top_k <= kInlinePlanRoutes &&
+         E_local <= kMaxExperts && bs_supported(K, I);
+}
+
 bool plan_in_split(int64_t R, int K, int I, bool rows_local, bool from_logits) {
   return rows_local && !from_logits && R > 0 && R <= kInlinePlanRoutes && bs_supported(K, I);
 }
@@ -75,13 +80,19 @@ cudaError_t run_moe(const MoeArgs& a, const WorkspacePlan& plan, void* workspace
 
   cudaError_t err = mark(0);
   if (err != cudaSuccess) { *why = "stage event"; return err; }
-  err = cudaMemsetAsync(status, 0, 256, stream);
-  if (err != cudaSuccess) { *why = "status clear"; return err; }
+  if (a.ep_split && !bs_supported(a.K, a.I)) {
+    *why = "expert-parallel exchange needs K and I multiples of 256";
+    return cudaErrorInvalidValue;
+  }
+  if (!a.ep_split) {  // the exchange split clears the status words itself
+    err = cudaMemsetAsync(status, 0, 256, stream);
+    if (err != cudaSuccess) { *why = "status clear"; return err; }
+  }
   const int32_t* ids = a.router_logits ? a.routed_ids : a.ids;
   const float* weights = a.router_logits ? a.routed_weights : a.weights;
   const bool inline_plan = plan_in_split(R, a.K, a.I, a.hidden_rows.base == nullptr,
                                          a.router_logits != nullptr);
-  if (!inline_plan) {
+  if (!inline_plan && !a.ep_split) {
     err = launch_route_plan(ids, R, a.E, chunk_counts, counts, offsets, sorted, slot_of, status,
                             stream, a.router_logits, a.logits_dt, a.top_k, a.routed_weights);
     if (err != cudaSuccess) { *why = "route plan"; return err; }
@@ -117,6 +128,8 @@ cudaError_t run_moe(const MoeArgs& a, const WorkspacePlan& plan, void* workspace
     t.hg = reinterpret_cast<float*>(ws + plan.hg);
     t.y = y;
     t.status = status;
+    t.ep = a.ep_split;
+    t.push = a.push;
     t.M = a.M;
     t.R = R;
     t.E = a.E;
@@ -138,9 +151,9 @@ cudaError_t run_moe(const MoeArgs& a, const WorkspacePlan& plan, void* workspace
     err = launch_moe_bs(t, stream, &step);
     if (err != cudaSuccess) { *why = step; return err; }
   } else {
-    if (a.hidden_rows.base || a.act_terms != kSplitTerms) {
-      *why = a.hidden_rows.base ? "expert-parallel rows need K and I multiples of 256"
-                                : "W4A4 needs K and I multiples of 256";
+    if (a.hidden_rows.base || a.push.base || a.act_terms != kSplitTerms) {
+      *why = a.act_terms != kSplitTerms ? "W4A4 needs K and I multiples of 256"
+                                        : "expert-parallel rows need K and I multiples of 256";
       return cudaErrorInvalidValue;
     }
     if ((err = mark(1)) != cudaSuccess) { *why = "stage event"; return err; }
@@ -152,9 +165,11 @@ cudaError_t run_moe(const MoeArgs& a, const WorkspacePlan& plan, void* workspace
     if (err != cudaSuccess) { *why = "down"; return err; }
     if ((err = mark(3)) != cudaSuccess) { *why = "stage event"; return err; }
   }
-  err = launch_combine(y, slot_of, weights, a.multiply_router_weight, a.out, a.out_dt, a.M,
-                       a.top_k, a.K, stream, a.out_rows.base ? &a.out_rows : nullptr);
-  if (err != cudaSuccess) { *why = "combine"; return err; }
+  if (!a.push.base) {  // expert parallel: the sources sum the pushed rows
+    err = launch_combine(y, slot_of, weights, a.multiply_router_weight, a.out, a.out_dt, a.M,
+                         a.top_k, a.K, stream);
+    if (err != cudaSuccess) { *why = "combine"; return err; }
+  }
   if ((err = mark(4)) != cudaSuccess) { *why = "stage event"; return err; }
   return cudaSuccess;
 }

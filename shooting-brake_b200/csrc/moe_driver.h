@@ -47,9 +47,12 @@ struct MoeArgs {
   int E, top_k, K, I;
   void* const* stage_events;  // optional cudaEvent_t[SBB200_STAGE_EVENTS]
   // expert parallel (block-scaled path only): token rows read from the
-  // source GPUs, fp32 partial rows stored back to them
+  // source GPUs (hidden_rows) or the whole exchange done by the activation
+  // split (ep_split; M is then the number of virtual tokens), and the down
+  // projection's fp32 rows pushed back to their sources (push; no combine)
   SplitRows hidden_rows{nullptr, 1};
-  SplitRows out_rows{nullptr, 1};
+  const EpSplitArgs* ep_split = nullptr;
+  PushRows push{nullptr, 1};
   // routing from router logits [M, E] (logits_dt): the plan writes top-k ids
   // into `routed_ids` and softmax weights into `routed_weights`, which the
   // rest of the forward then uses in place of ids / weights
@@ -77,6 +80,10 @@ bool plan_in_split(int64_t R, int K, int I, bool rows_local, bool from_logits);
 // Kernels (excluding the status memset) one run_moe call enqueues when ids
 // are given; rows_local is false for expert-parallel rows read from peers.
 int count_launches(int64_t M, int top_k, int K, int I, bool rows_local = true);
+
+// True when an expert-parallel step of world * max_tokens virtual tokens is
+// exchanged by the activation split itself (ep_split_kernel).
+bool ep_split_fits(int64_t virtual_tokens, int top_k, int K, int I, int E_local);
 
 // Enqueue the whole forward on `stream`. On failure returns the CUDA error and
 // names the failing step in *why.

@@ -53,11 +53,13 @@ __device__ __forceinline__ bool mbar_try_wait(uint64_t* bar, uint32_t parity) {
 
 // Wait for the phase of `bar` with the given parity to complete. Returns false
 // (and raises *abort) when the deadline passes or another role has aborted.
+// The deadline is first checked after the first unsuccessful try (then every
+// 16th), so a wait that completes at once never reads the clock.
 __device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity, volatile int* abort,
                                           uint64_t deadline) {
   for (uint32_t i = 0;; ++i) {
     if (mbar_try_wait(bar, parity)) return true;
-    if ((i & 15) == 15) {
+    if ((i & 15) == 0) {
       if (*abort) return false;
       if (now_ns() > deadline) {
         *abort = 1;

@@ -6,8 +6,9 @@ contiguously over the ranks (the first E % world ranks hold one extra expert,
 :meth:`ExpertParallel.forward` once per step. Inside, the exchange is
 device-resident (``include/sbb200.h``, ``csrc/ep.cu``): each destination reads
 the rows routed to its experts straight from the source GPUs, runs its shard,
-and stores each token's partial output back into the source's buffer, which
-sums the partials in rank order. This replaces the reference's multi-card
+and stores each route's output row back into the source's buffer, which sums
+its tokens' routes in ascending k with the router weights (the single-GPU
+combine's order, so the result does not depend on the sharding). This replaces the reference's multi-card
 split, where each card receives every route with foreign experts as -1 and
 the host adds the per-card outputs (``src/phase4/src/shooting_brake_vllm/
 routed_experts.py:354-382, 2460-2463, 2522-2524``).
@@ -26,8 +27,8 @@ from . import DTYPE_CODE, Sbb200Error, _check, _check_cuda, _p, _stream, last_er
 
 HANDLE_BYTES = 64
 STAGE_EVENTS = 8
-STAGE_NAMES = ("publish", "gather+wait", "route_plan+split(pull)", "gate_up", "h_split+down",
-               "combine(push)", "final+wait")
+STAGE_NAMES = ("publish", "gather+wait", "exchange+route_plan+split(pull)", "gate_up",
+               "h_split+down(push)", "combine(none)", "final+wait")
 
 
 def expert_shard(E: int, world: int, rank: int) -> tuple[int, int]:

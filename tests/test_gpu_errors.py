@@ -22,7 +22,9 @@ pytestmark = pytest.mark.gpu
 
 
 def _inputs(oracle, cuda):
-    E, K, I, T, top_k = 16, 1024, 512, 64, 2  # the block-scaled (tcgen05) path
+    # the block-scaled (tcgen05) path, with units long enough that the
+    # epilogue's first wait for an accumulator cannot succeed at once
+    E, K, I, T, top_k = 16, 4096, 1280, 64, 2
     L = oracle.make_layer(E, K, I, seed=81)
     hidden = oracle.make_hidden(T, K, seed=82)
     ids, w = oracle.route_logits(T, E, top_k, seed=83)
