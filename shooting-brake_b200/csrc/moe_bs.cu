@@ -849,9 +849,9 @@ __global__ void __launch_bounds__(1024) split_nvfp4_kernel(
 // Expert-parallel exchange split (EpSplitArgs): one CTA per virtual token
 // v = src * max_tokens + t of the whole world's step, blockDim as the split.
 //  1. The CTAs of this rank's own tokens copy their row, ids and weights into
-//     the exchange buffer; each writer fences at system scope, and the last
-//     of them (a completion count) raises ready = epoch << 32 | M on every
-//     other rank.
+//     the exchange buffer; after a CTA barrier one thread per CTA fences at
+//     system scope and counts the CTA done, and the last of them raises
+//     ready = epoch << 32 | M on every other rank.
 //  2. Every CTA waits (bounded) for the other ranks' ready flags, reads every
 //     rank's ids (its own from the caller, the others' over NVLink), keeps
 //     the routes to this rank's experts and plans their slots in the stable
@@ -894,8 +894,9 @@ __global__ void __launch_bounds__(1024) ep_split_kernel(
         a.ex_ids[t * top_k + i] = a.ids[t * top_k + i];
         a.ex_weights[t * top_k + i] = a.weights[t * top_k + i];
       }
-      __threadfence_system();
     }
+    // the barrier orders every thread's copies before thread 0's
+    // system-scope fence (cumulative), which orders them before the count
     __syncthreads();
     if (tid == 0) {
       __threadfence_system();

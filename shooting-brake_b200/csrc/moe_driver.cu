@@ -75,7 +75,9 @@ cudaError_t run_moe(const MoeArgs& a, const WorkspacePlan& plan, void* workspace
   const int64_t R = a.M * a.top_k;
   auto mark = [&](int i) -> cudaError_t {
     if (!a.stage_events || !a.stage_events[i]) return cudaSuccess;
-    return cudaEventRecord(static_cast<cudaEvent_t>(a.stage_events[i]), stream);
+    // external: inside a stream capture the event stays timeable after replay
+    return cudaEventRecordWithFlags(static_cast<cudaEvent_t>(a.stage_events[i]), stream,
+                                    cudaEventRecordExternal);
   };
 
   cudaError_t err = mark(0);
@@ -143,7 +145,9 @@ cudaError_t run_moe(const MoeArgs& a, const WorkspacePlan& plan, void* workspace
     if (a.stage_events) {
       t.stage_mark = [](void* c, int i) {
         auto* x = static_cast<Ctx*>(c);
-        if (x->ev[i]) cudaEventRecord(static_cast<cudaEvent_t>(x->ev[i]), x->s);
+        if (x->ev[i])
+          cudaEventRecordWithFlags(static_cast<cudaEvent_t>(x->ev[i]), x->s,
+                                   cudaEventRecordExternal);
       };
       t.stage_ctx = &ctx;
     }
