@@ -924,7 +924,7 @@ class LayerBench:
         gu_bytes = avg_distinct * W13_EXPERT_BYTES + T * D * 2
         dn_bytes = avg_distinct * W2_EXPERT_BYTES
         gu_gbs = gu_bytes / (stage_ms["gate_up"] * 1e-3) / 1e9
-        dn_gbs = dn_bytes / (stage_ms["down"] * 1e-3) / 1e9
+        dn_gbs = dn_bytes / (stage_ms["h_split+down"] * 1e-3) / 1e9
         info = {"distinct_experts_avg": avg_distinct, "algorithmic_bytes_per_step": avg_bytes}
         if T < 1024:
             traffic = profiled_traffic(T) if not self.w4a4 else None
@@ -950,7 +950,7 @@ class LayerBench:
         tf_src = ("measured bf16_tflops_sustained" if "bf16_tflops_sustained" in peaks
                   else "fallback 1.4 PF sustained") + (" x4 (FP4 rate)" if self.w4a4 else "")
         gu_tf = fl_gu / (stage_ms["gate_up"] * 1e-3) / 1e12
-        dn_tf = fl_gu / 2 / (stage_ms["down"] * 1e-3) / 1e12
+        dn_tf = fl_gu / 2 / (stage_ms["h_split+down"] * 1e-3) / 1e12
         step_tf = fl_all / (ms * 1e-3) / 1e12
         roof = {"bound": "tensor", "achieved": gu_tf, "peak": tf_peak, "unit": "TFLOP/s",
                 "frac": gu_tf / tf_peak, "traffic": None,

@@ -92,13 +92,9 @@ int sbb200_nvfp4_moe(void* stream, const void* hidden, const int32_t* topk_ids,
  * src/QuixiCore-XPU/kernels/moe/nvfp4_moe/nvfp4_moe_kernel.hpp:53-83): the same
  * launches in the same order, with cudaEvent_t stage_events[i] recorded on
  * `stream` at the stage boundaries: [0] start, [1] after the route plan
- * and the activation split, [2] after the gate/up + SwiGLU GEMM (which also
- * splits the SwiGLU rows for the down projection), [3] after the down
- * projection (which also combines the routes on the tensor-core path), [4]
- * after the combine kernel of the CUDA-core path ([4] = [3] otherwise).
- * n_stage_events must be SBB200_STAGE_EVENTS; NULL entries are skipped. The
- * events are recorded as external events, so inside a stream capture they
- * stay timeable after each replay. */
+ * (and the activation split), [2] after the gate/up + SwiGLU GEMM, [3] after
+ * the down projection (and the split of its input), [4] after the combine. n_stage_events must be SBB200_STAGE_EVENTS; NULL entries are
+ * skipped. */
 #define SBB200_STAGE_EVENTS 5
 int sbb200_nvfp4_moe_staged(void* stream, const void* hidden, const int32_t* topk_ids,
                             const float* topk_weights, const void* w13, const void* w13_scales,

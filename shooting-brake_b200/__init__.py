@@ -271,19 +271,14 @@ def _nvfp4_moe_impl(hidden: torch.Tensor, topk_ids: torch.Tensor, topk_weights: 
 def kernels_per_call(M: int, E: int, top_k: int, K: int, I: int,
                      act_dtype: torch.dtype = torch.bfloat16) -> int:
     """Kernels of this library one nvfp4_moe call of this shape launches (the
-    driver's own count: route plan, activation split, gate/up with the SwiGLU
-    split in its epilogue, down with the combine in its epilogue on the
-    block-scaled path; up to 1,024 routes the split computes the route plan
-    itself)."""
+    driver's own count: route plan, activation split, gate/up, SwiGLU split,
+    down, combine on the block-scaled path; up to 1,024 routes the split
+    computes the route plan itself)."""
     return int(lib().sbb200_nvfp4_moe_launches(M, E, top_k, K, I, DTYPE_CODE[act_dtype]))
 
 
 STAGE_EVENTS = 5
-# stage boundaries of sbb200_nvfp4_moe_staged: on the block-scaled path the
-# gate/up GEMM also splits the SwiGLU rows and the down GEMM also combines,
-# so the last stage is empty there (it is the combine kernel of the CUDA-core
-# path)
-STAGE_NAMES = ("route_plan+x_split", "gate_up", "down", "combine")
+STAGE_NAMES = ("route_plan+x_split", "gate_up", "h_split+down", "combine")
 
 
 def stage_events(stream: torch.cuda.Stream | None = None) -> list:

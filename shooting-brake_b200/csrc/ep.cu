@@ -588,13 +588,13 @@ int sbb200_ep_forward(sbb200_ep_t* p, void* stream, const void* hidden, const in
 
 int sbb200_ep_launches(const sbb200_ep_t* p) {
   if (!p) return -1;
-  // exchange split, gate/up (splitting SwiGLU rows), down (pushing), final;
-  // larger steps: publish, gather, route plan (1 or 2 kernels), split,
-  // gate/up, down, final.
-  if (p->fused) return 4;
+  // exchange split, gate/up, SwiGLU split, down (pushing), final; larger
+  // steps: publish, gather, route plan (1 or 2), split, gate/up, SwiGLU
+  // split, down, final. No combine kernel either way.
+  if (p->fused) return 5;
   const int64_t vt = static_cast<int64_t>(p->world) * p->max_tokens;
   return 2 + sbb::count_launches(vt, static_cast<int>(p->top_k), static_cast<int>(p->K),
-                                 static_cast<int>(p->I), false) + 1;
+                                 static_cast<int>(p->I), false) - 1 + 1;
 }
 
 int sbb200_ep_device_errors(sbb200_ep_t* p, void* stream, uint32_t* errors) {

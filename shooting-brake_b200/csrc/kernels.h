@@ -153,12 +153,6 @@ struct BsLaunch {
   uint8_t* hsf;  // [R*NT, I/16]
   float* hg;     // [R*NT]
   float* y;      // fp32 [R, K]
-  int32_t* hcnt;  // [R] per-slot arrival counters of the gate/up row tiles
-  int32_t* ccnt;  // [M, K/256] per-token arrival counters of the down row tiles
-  const float* weights;  // [M, top_k] router weights (combine)
-  int multiply_router_weight;
-  void* out;      // [M, K] in out_dt
-  int out_dt;
   uint32_t* status;
   int64_t M, R;
   int E, top_k, K, I;

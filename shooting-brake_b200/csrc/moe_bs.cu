@@ -105,23 +105,6 @@ struct BsParams {
   float* const* push_base;
   int64_t push_rows;
   int top_k;
-  // fuse: the CTA that completes a row last (arrival counters cnt, counted
-  // down from the values the activation split set) does that row's follow-up
-  // in its epilogue warps: gate/up splits the slot's SwiGLU row into the down
-  // projection's NVFP4 terms (hq, hsf, hg; static W4A4 globals hstatic);
-  // down combines the token's routes into fout (the combine kernel's
-  // arithmetic and order). No separate split or combine kernel runs.
-  int fuse;
-  int32_t* cnt;
-  uint8_t* hq;
-  uint8_t* hsf;
-  float* hg;
-  const float* hstatic;
-  const int32_t* slot_of;
-  const float* weights;
-  int mult;
-  void* fout;
-  int fout_dt;
 };
 
 template <int MODE, int BNR, int NT>
@@ -167,174 +150,6 @@ struct BsCfg {
   static_assert(kSfBufs >= 2 && kSfCol0 + kSfBufs * kSfCols <= kTmemCols, "tensor memory");
   static_assert(BNR % 16 == 0 && BNR >= 16 && BNR <= 256 && BNR % NT == 0, "tile");
 };
-
-// ---- NVFP4 quantisation helpers --------------------------------------------
-
-// Two fp32 -> one byte of e2m1 (lo -> low nibble), round to nearest even,
-// saturating: cvt.rn.satfinite.e2m1x2.f32 places its first source operand in
-// the upper nibble.
-__device__ __forceinline__ uint32_t e2m1x2_from_f32(float lo, float hi) {
-  uint32_t r;
-  asm("{\n .reg .b8 b;\n cvt.rn.satfinite.e2m1x2.f32 b, %1, %2;\n cvt.u32.u8 %0, b;\n}"
-      : "=r"(r)
-      : "f"(hi), "f"(lo));
-  return r;
-}
-
-__device__ __forceinline__ float e4m3_to_f32_hw(uint32_t byte) {
-  uint32_t h;
-  asm("cvt.rn.f16x2.e4m3x2 %0, %1;" : "=r"(h) : "h"(static_cast<uint16_t>(byte & 0xFFu)));
-  return __low2float(*reinterpret_cast<const __half2*>(&h));
-}
-
-__device__ __forceinline__ float2 e2m1x2_to_float2(uint32_t byte) {
-  uint32_t h;
-  asm("{\n .reg .b8 b;\n cvt.u8.u32 b, %1;\n cvt.rn.f16x2.e2m1x2 %0, b;\n}" : "=r"(h) : "r"(byte));
-  return __half22float2(*reinterpret_cast<const __half2*>(&h));
-}
-
-
-// One 16-element block to one NVFP4 term under quantisation global G (g =
-// 1/G): scale = min(G * bmax / 6, 448) to e4m3, elements to the nearest e2m1
-// of x / (e4m3 * g) (vLLM ref_nvfp4_quant). With RESID the block is left
-// holding what the term does not represent.
-template <bool RESID>
-__device__ __forceinline__ void quant_block(float* v, float G, float g, uint32_t* w,
-                                            uint8_t* scale_byte) {
-  float bmax = 0.0f;
-#pragma unroll
-  for (int i = 0; i < 16; ++i) bmax = fmaxf(bmax, fabsf(v[i]));
-  const float scale = fminf(__fmul_rn(G, __fmul_rn(bmax, 1.0f / 6.0f)), 448.0f);
-  const __nv_fp8_storage_t s8 = __nv_cvt_float_to_fp8(scale, __NV_SATFINITE, __NV_E4M3);
-  const float sg = __fmul_rn(e4m3_to_f32_hw(s8), g);  // one e2m1 step of this block
-  const float inv = sg == 0.0f ? 0.0f : __frcp_rn(sg);
-  w[0] = w[1] = 0u;
-#pragma unroll
-  for (int j = 0; j < 8; ++j) {
-    // nearest e2m1 (ties to even, saturating at 6) of both elements
-    const uint32_t pair = e2m1x2_from_f32(__fmul_rn(v[2 * j], inv), __fmul_rn(v[2 * j + 1], inv));
-    if (RESID) {
-      // the MMA sees e2m1 * e4m3 * g; the next term quantises what is left
-      const float2 dq = e2m1x2_to_float2(pair);
-      v[2 * j] -= __fmul_rn(dq.x, sg);
-      v[2 * j + 1] -= __fmul_rn(dq.y, sg);
-    }
-    w[j >> 2] |= pair << (8 * (j & 3));
-  }
-  *scale_byte = static_cast<uint8_t>(s8);
-}
-
-// Named barrier of the eight epilogue warps (barrier 1; barrier 0 is
-// __syncthreads), and the same barrier returning whether any of the 256
-// threads passed a true predicate.
-__device__ __forceinline__ void epi_sync() { asm volatile("bar.sync 1, 256;" ::: "memory"); }
-
-__device__ __forceinline__ bool epi_any(bool pred) {
-  uint32_t r;
-  asm volatile(
-      "{\n .reg .pred p, q;\n setp.ne.u32 p, %1, 0;\n bar.red.or.pred q, 1, 256, p;\n"
-      " selp.u32 %0, 1, 0, q;\n}"
-      : "=r"(r)
-      : "r"(static_cast<uint32_t>(pred))
-      : "memory");
-  return r != 0;
-}
-
-__device__ __forceinline__ void load16_cg(const float* src, float* x) {
-#pragma unroll
-  for (int i = 0; i < 4; ++i) {
-    const float4 v = __ldcg(reinterpret_cast<const float4*>(src) + i);
-    x[4 * i] = v.x;
-    x[4 * i + 1] = v.y;
-    x[4 * i + 2] = v.z;
-    x[4 * i + 3] = v.w;
-  }
-}
-
-// The complete SwiGLU row of `slot` (fp32 h[slot, 0:I], read through L2)
-// split by the 256 epilogue threads (etid) into the down projection's NT
-// NVFP4 terms, as the activation split does for hidden rows: a dynamic
-// global from the row maximum and NT residual terms at G0 * 4^t, or one term
-// under the static W4A4 global G_static (g = 1) when it is positive.
-template <int NT>
-__device__ void epi_split_h(const BsParams& p, int slot, float G_static, int etid,
-                            float* s_red) {
-  const int nb = p.I / 16;
-  const float* row = p.out + static_cast<int64_t>(slot) * p.I;
-  uint8_t* q = p.hq;
-  uint8_t* sf = p.hsf;
-  if (G_static > 0.0f) {
-    if (etid == 0) p.hg[slot] = 1.0f;
-    const float g = __fdiv_rn(1.0f, G_static);
-    for (int b = etid; b < nb; b += 256) {
-      float x[16];
-      load16_cg(row + b * 16, x);
-      uint32_t w[2];
-      uint8_t s8;
-      quant_block<false>(x, G_static, g, w, &s8);
-      *reinterpret_cast<uint2*>(q + static_cast<int64_t>(slot) * (p.I / 2) + b * 8) =
-          make_uint2(w[0], w[1]);
-      sf[static_cast<int64_t>(slot) * (p.I / 16) + b] = s8;
-    }
-    return;
-  }
-  float amax = 0.0f;
-  for (int b = etid; b < nb; b += 256) {
-    float x[16];
-    load16_cg(row + b * 16, x);
-#pragma unroll
-    for (int i = 0; i < 16; ++i) amax = fmaxf(amax, fabsf(x[i]));
-  }
-#pragma unroll
-  for (int d = 16; d > 0; d >>= 1) amax = fmaxf(amax, __shfl_xor_sync(0xffffffffu, amax, d));
-  if ((etid & 31) == 0) s_red[etid >> 5] = amax;
-  epi_sync();
-  amax = s_red[0];
-#pragma unroll
-  for (int w = 1; w < 8; ++w) amax = fmaxf(amax, s_red[w]);
-  const float G0 = amax > 0.0f ? __fdiv_rn(2688.0f, amax) : 1.0f;
-  const float g0 = __fdiv_rn(1.0f, G0);
-  if (etid < NT) p.hg[static_cast<int64_t>(slot) * NT + etid] = ldexpf(g0, -2 * etid);
-  for (int b = etid; b < nb; b += 256) {
-    float x[16];
-    load16_cg(row + b * 16, x);
-    float G = G0, g = g0;
-#pragma unroll 1
-    for (int t = 0; t < NT; ++t) {
-      uint32_t w[2];
-      uint8_t s8;
-      quant_block<true>(x, G, g, w, &s8);
-      const int64_t orow = static_cast<int64_t>(slot) * NT + t;
-      *reinterpret_cast<uint2*>(q + orow * (p.I / 2) + b * 8) = make_uint2(w[0], w[1]);
-      sf[orow * (p.I / 16) + b] = s8;
-      G = __fmul_rn(G, 4.0f);
-      g = __fmul_rn(g, 0.25f);
-    }
-  }
-  epi_sync();  // s_red is free again
-}
-
-// out[t, mt*256 + etid]: the top-k combine of token t over the 256 output
-// columns of this down unit, in ascending k with fmaf, the arithmetic of
-// combine_kernel; the routes' rows are read through L2.
-__device__ void epi_combine(const BsParams& p, int64_t t, int mt, int etid) {
-  const int col = mt * 2 * kM + etid;
-  float acc = 0.0f;
-  for (int k = 0; k < p.top_k; ++k) {
-    const int32_t s = p.slot_of[t * p.top_k + k];
-    if (s < 0) continue;
-    const float w = p.mult ? p.weights[t * p.top_k + k] : 1.0f;
-    acc = fmaf(w, __ldcg(p.out + static_cast<int64_t>(s) * p.out_ld + col), acc);
-  }
-  const int64_t at = t * p.out_ld + col;
-  if (p.fout_dt == kF32) {
-    static_cast<float*>(p.fout)[at] = acc;
-  } else if (p.fout_dt == kBF16) {
-    static_cast<__nv_bfloat16*>(p.fout)[at] = __float2bfloat16_rn(acc);
-  } else {
-    static_cast<__half*>(p.fout)[at] = __float2half_rn(acc);
-  }
-}
 
 __device__ __forceinline__ void decode_unit(int u, int m_tiles, const int* prefix, int E, int& e,
                                             int& nt, int& mt) {
@@ -395,8 +210,6 @@ __global__ void __launch_bounds__(kThreads, 1)
   __shared__ uint32_t tmem_base_s;
   __shared__ int abort_s;
   __shared__ int prefix[kMaxExperts + 1];
-  __shared__ int32_t s_last[C::kTok];  // epilogue: rows this CTA completed last
-  __shared__ float s_red[8];
 
   const int tid = threadIdx.x;
   const int warp = tid >> 5;
@@ -630,16 +443,12 @@ __global__ void __launch_bounds__(kThreads, 1)
     const int team = (warp >> 2) & 1;
     const int r = q * 32 + lane;
     const uint32_t lane_base = static_cast<uint32_t>(q * 32) << 16;
-    const int etid = tid - 256;  // 0..255 over the epilogue warps
     uint32_t ui = 0;
     for (int u = blockIdx.x; u < total_units; u += gridDim.x, ++ui) {
       int e, nt, mt;
       decode_unit(u, p.m_tiles, prefix, p.E, e, nt, mt);
       const int d = ui % NB;
-      const bool ok = warp_wait(&dfull[d], (ui / NB) & 1u, abort, deadline);
-      // with fused follow-ups the epilogue warps meet at named barriers, so
-      // they leave together or not at all
-      if (p.fuse ? epi_any(!ok) : !ok) break;
+      if (!warp_wait(&dfull[d], (ui / NB) & 1u, abort, deadline)) break;
       tc_fence_after();
       const int valid = min(C::kTok, p.counts[e] - nt * C::kTok);
       const int slot0 = p.offsets[e] + nt * C::kTok;
@@ -687,38 +496,6 @@ __global__ void __launch_bounds__(kThreads, 1)
       tc_fence_before();
       __syncwarp();
       if (lane == 0) mbar_arrive(&dempty[d]);
-      if (p.fuse) {
-        // every epilogue thread's stores of this unit are issued; one thread
-        // per completed row counts it down, fenced (cumulative over the
-        // barrier), and the CTA that takes a counter to zero does the row's
-        // follow-up after a fence of its own
-        epi_sync();
-        if (etid < valid) {
-          const int slot = slot0 + etid;
-          int32_t* c;
-          int32_t who;
-          if (MODE == kGateUp) {
-            c = p.cnt + slot;
-            who = slot;
-          } else {
-            who = p.sorted[slot] / p.top_k;
-            c = p.cnt + static_cast<int64_t>(who) * p.m_tiles + mt;
-          }
-          __threadfence();
-          s_last[etid] = atomicSub(c, 1) == 1 ? who : -1;
-        }
-        epi_sync();
-        for (int j = 0; j < valid; ++j) {
-          const int32_t who = s_last[j];
-          if (who < 0) continue;
-          __threadfence();
-          if (MODE == kGateUp)
-            epi_split_h<NT>(p, who, p.hstatic ? p.hstatic[e] : 0.0f, etid, s_red);
-          else
-            epi_combine(p, who, mt, etid);
-        }
-        epi_sync();  // s_last is rewritten by the next unit
-      }
     }
   }
 
@@ -732,16 +509,44 @@ __global__ void __launch_bounds__(kThreads, 1)
   }
 }
 
-// Splits token rows into NT NVFP4 terms. One CTA per token, one 16-element
+// ---- activation splitter ----------------------------------------------------
+
+// Two fp32 -> one byte of e2m1 (lo -> low nibble), round to nearest even,
+// saturating: cvt.rn.satfinite.e2m1x2.f32 places its first source operand in
+// the upper nibble.
+__device__ __forceinline__ uint32_t e2m1x2_from_f32(float lo, float hi) {
+  uint32_t r;
+  asm("{\n .reg .b8 b;\n cvt.rn.satfinite.e2m1x2.f32 b, %1, %2;\n cvt.u32.u8 %0, b;\n}"
+      : "=r"(r)
+      : "f"(hi), "f"(lo));
+  return r;
+}
+
+__device__ __forceinline__ float e4m3_to_f32_hw(uint32_t byte) {
+  uint32_t h;
+  asm("cvt.rn.f16x2.e4m3x2 %0, %1;" : "=r"(h) : "h"(static_cast<uint16_t>(byte & 0xFFu)));
+  return __low2float(*reinterpret_cast<const __half2*>(&h));
+}
+
+__device__ __forceinline__ float2 e2m1x2_to_float2(uint32_t byte) {
+  uint32_t h;
+  asm("{\n .reg .b8 b;\n cvt.u8.u32 b, %1;\n cvt.rn.f16x2.e2m1x2 %0, b;\n}" : "=r"(h) : "r"(byte));
+  return __half22float2(*reinterpret_cast<const __half2*>(&h));
+}
+
+
+// Splits rows into NT NVFP4 terms. One CTA per source row, one 16-element
 // block per thread (blockDim: K / 16 rounded up to whole warps, at least
 // kSplitThreads), so block maxima need no shuffles, the row maximum is one
 // CTA reduction of values already in registers, every element is read once
-// and a thread's packed block is one 8-byte store. A token's terms go to
-// every route slot it feeds (slot_of[t*top_k + k], -1 skipped), so a token is
-// split once however many experts it visits, and a token with no slot is not
-// read at all. With an InlinePlan the slots are computed here instead of
-// read. Outputs: packed e2m1 [slot*NT + t, K/2], e4m3 scales
-// [slot*NT + t, K/16] and the dequant global g [slot*NT + t].
+// and a thread's packed block is one 8-byte store. Without slot_of, row i is
+// written to output rows i*NT + t; with slot_of (token mode) source row i is
+// token i and its terms go to every route slot the token feeds
+// (slot_of[i*top_k + k], -1 skipped), so a token is split once however many
+// experts it visits, and a token with no slot is not read at all. In token
+// mode with an InlinePlan the slots are computed here instead of read.
+// Outputs: packed e2m1 [row*NT + t, K/2], e4m3 scales [row*NT + t, K/16] and
+// the dequant global g [row*NT + t].
 constexpr int kSplitThreads = 64;
 
 // CG: read through L2 only. Rows on another GPU are rewritten every step by
@@ -771,6 +576,36 @@ __device__ __forceinline__ void load8(const void* src, int src_dt, int64_t at, f
       }
     }
   }
+}
+
+// One 16-element block to one NVFP4 term under quantisation global G (g =
+// 1/G): scale = min(G * bmax / 6, 448) to e4m3, elements to the nearest e2m1
+// of x / (e4m3 * g) (vLLM ref_nvfp4_quant). With RESID the block is left
+// holding what the term does not represent.
+template <bool RESID>
+__device__ __forceinline__ void quant_block(float* v, float G, float g, uint32_t* w,
+                                            uint8_t* scale_byte) {
+  float bmax = 0.0f;
+#pragma unroll
+  for (int i = 0; i < 16; ++i) bmax = fmaxf(bmax, fabsf(v[i]));
+  const float scale = fminf(__fmul_rn(G, __fmul_rn(bmax, 1.0f / 6.0f)), 448.0f);
+  const __nv_fp8_storage_t s8 = __nv_cvt_float_to_fp8(scale, __NV_SATFINITE, __NV_E4M3);
+  const float sg = __fmul_rn(e4m3_to_f32_hw(s8), g);  // one e2m1 step of this block
+  const float inv = sg == 0.0f ? 0.0f : __frcp_rn(sg);
+  w[0] = w[1] = 0u;
+#pragma unroll
+  for (int j = 0; j < 8; ++j) {
+    // nearest e2m1 (ties to even, saturating at 6) of both elements
+    const uint32_t pair = e2m1x2_from_f32(__fmul_rn(v[2 * j], inv), __fmul_rn(v[2 * j + 1], inv));
+    if (RESID) {
+      // the MMA sees e2m1 * e4m3 * g; the next term quantises what is left
+      const float2 dq = e2m1x2_to_float2(pair);
+      v[2 * j] -= __fmul_rn(dq.x, sg);
+      v[2 * j + 1] -= __fmul_rn(dq.y, sg);
+    }
+    w[j >> 2] |= pair << (8 * (j & 3));
+  }
+  *scale_byte = static_cast<uint8_t>(s8);
 }
 
 // The dynamic-global split of one row held in registers, one 16-element
@@ -930,66 +765,47 @@ __device__ __forceinline__ void inline_route_slots(const InlinePlan& plan, int64
                    s_dst);
 }
 
-// Arrival counters the GEMM epilogues count down (see BsParams::fuse), set by
-// the split of the token that owns them: hcnt[slot] = number of gate/up row
-// tiles of each of the token's slots, ccnt[t * per + i] = the token's valid
-// routes for each of the `per` down row tiles. A token with no valid route
-// gets its output row zeroed here (no epilogue writes it).
-struct SplitInit {
-  int32_t* hcnt;
-  int32_t hinit;
-  int32_t* ccnt;
-  int per;
-  void* out;  // [M, K] in out_dt, or nullptr
-  int out_dt;
-};
-
-__device__ __forceinline__ void init_counters(const SplitInit& in, int64_t tok, int top_k,
-                                              const int32_t* s_dst, int K) {
-  const int tid = threadIdx.x;
-  int n = 0;
-  for (int i = 0; i < top_k; ++i) n += s_dst[i] >= 0 ? 1 : 0;
-  if (in.hcnt)
-    for (int i = tid; i < top_k; i += blockDim.x)
-      if (s_dst[i] >= 0) in.hcnt[s_dst[i]] = in.hinit;
-  if (in.ccnt)
-    for (int i = tid; i < in.per; i += blockDim.x) in.ccnt[tok * in.per + i] = n;
-  if (n == 0 && in.out) {
-    const int esz = in.out_dt == kF32 ? 4 : 2;
-    uint4* o = reinterpret_cast<uint4*>(static_cast<char*>(in.out) + tok * K * esz);
-    for (int i = tid; i < K * esz / 16; i += blockDim.x) o[i] = make_uint4(0, 0, 0, 0);
-  }
-}
-
 // gstatic != nullptr (W4A4 with static activation globals, NT = 1): the
 // block of each destination slot is quantised under gstatic[e] of that
-// slot's expert e = eids[t * top_k + k] and its g is 1, because the GEMM
-// epilogue then scales by the caller's per-expert alpha. Otherwise the row's
-// global is dynamic, G0 = 448 * 6 / max|row|, with NT terms at G0 * 4^t.
+// slot's expert e (token mode: eids[row * top_k + k]; row mode:
+// eids[sorted[row]]) and its g is 1, because the GEMM epilogue then scales by
+// the caller's per-expert alpha. Otherwise the row's global is dynamic,
+// G0 = 448 * 6 / max|row|, with NT terms at G0 * 4^t.
 __global__ void __launch_bounds__(1024) split_nvfp4_kernel(
     const void* __restrict__ src, int src_dt, SplitRows rows, const int32_t* __restrict__ slot_of,
-    int top_k, int K, int NT, uint8_t* __restrict__ q, uint8_t* __restrict__ sf,
-    float* __restrict__ gout, const float* __restrict__ gstatic, const int32_t* __restrict__ eids,
-    const InlinePlan plan, const SplitInit init) {
+    int top_k, const int32_t* __restrict__ n_rows_dev, int K, int NT, uint8_t* __restrict__ q,
+    uint8_t* __restrict__ sf, float* __restrict__ gout, const float* __restrict__ gstatic,
+    const int32_t* __restrict__ eids, const int32_t* __restrict__ sorted, const InlinePlan plan) {
   __shared__ float s_max[32];
   __shared__ int32_t s_dst[kMaxTopK];
   __shared__ int32_t s_off[kMaxExperts + 1];
   __shared__ int32_t s_rank[kMaxTopK];
   __shared__ int32_t s_exp[kMaxTopK];
-  const int64_t row = blockIdx.x;  // token
+  __shared__ int s_any;
+  const int64_t row = blockIdx.x;
   pdl_wait();
   pdl_trigger();
+  if (n_rows_dev && row >= static_cast<int64_t>(*n_rows_dev)) return;
   const int tid = threadIdx.x;
-  if (plan.ids) {
-    inline_route_slots(plan, row, top_k, s_off, s_rank, s_exp, s_dst);
-  } else {
-    for (int i = tid; i < top_k; i += blockDim.x) s_dst[i] = slot_of[row * top_k + i];
+  int ndst = 1;
+  const bool token = slot_of != nullptr || plan.ids != nullptr;  // token mode
+  if (token) {
+    if (tid == 0) s_any = 0;
+    if (plan.ids) {
+      inline_route_slots(plan, row, top_k, s_off, s_rank, s_exp, s_dst);
+      for (int i = tid; i < top_k; i += blockDim.x)
+        if (s_dst[i] >= 0) s_any = 1;
+    } else {
+      __syncthreads();
+      for (int i = tid; i < top_k; i += blockDim.x) {
+        s_dst[i] = slot_of[row * top_k + i];
+        if (s_dst[i] >= 0) s_any = 1;
+      }
+    }
     __syncthreads();
+    if (!s_any) return;  // the whole CTA leaves together
+    ndst = top_k;
   }
-  init_counters(init, row, top_k, s_dst, K);
-  bool any = false;
-  for (int i = 0; i < top_k; ++i) any |= s_dst[i] >= 0;
-  if (!any) return;  // the whole CTA leaves together
   const void* rsrc = src;
   int64_t rbase = row * K;
   if (rows.base) {
@@ -1009,10 +825,11 @@ __global__ void __launch_bounds__(1024) split_nvfp4_kernel(
     }
   }
   if (gstatic) {
-    for (int d = 0; d < top_k; ++d) {
-      const int64_t dst = s_dst[d];
+    for (int d = 0; d < ndst; ++d) {
+      const int64_t dst = token ? static_cast<int64_t>(s_dst[d]) : row;
       if (dst < 0) continue;
-      const float G = gstatic[eids[row * top_k + d]];
+      const int32_t e = token ? eids[row * top_k + d] : eids[sorted[row]];
+      const float G = gstatic[e];
       if (tid == 0) gout[dst] = 1.0f;
       if (!active) continue;
       float x[16];
@@ -1026,7 +843,7 @@ __global__ void __launch_bounds__(1024) split_nvfp4_kernel(
     }
     return;
   }
-  split_row_terms(v, active, NT, K, s_dst, top_k, row, q, sf, gout, s_max);
+  split_row_terms(v, active, NT, K, token ? s_dst : nullptr, ndst, row, q, sf, gout, s_max);
 }
 
 // Expert-parallel exchange split (EpSplitArgs): one CTA per virtual token
@@ -1048,13 +865,14 @@ __global__ void __launch_bounds__(1024) ep_split_kernel(
     const EpSplitArgs a, int src_dt, int top_k, int K, int NT, int32_t* __restrict__ counts,
     int32_t* __restrict__ offsets, int32_t* __restrict__ sorted, int32_t* __restrict__ slot_of,
     uint32_t* __restrict__ status, uint8_t* __restrict__ q, uint8_t* __restrict__ sf,
-    float* __restrict__ gout, const SplitInit init) {
+    float* __restrict__ gout) {
   __shared__ float s_max[32];
   __shared__ int32_t s_dst[kMaxTopK];
   __shared__ int32_t s_off[kMaxExperts + 1];
   __shared__ int32_t s_rank[kMaxTopK];
   __shared__ int32_t s_exp[kMaxTopK];
   __shared__ int64_t s_cnt[kMaxWorld];
+  __shared__ int s_any;
   pdl_wait();
   pdl_trigger();
   const int tid = threadIdx.x;
@@ -1123,10 +941,12 @@ __global__ void __launch_bounds__(1024) ep_split_kernel(
                    s_off, s_rank, s_exp, s_dst);
   // 3. the token's row into its slots
   if (t >= s_cnt[src]) return;  // the whole CTA leaves together
-  init_counters(init, v, top_k, s_dst, K);
-  bool any = false;
-  for (int i = 0; i < top_k; ++i) any |= s_dst[i] >= 0;
-  if (!any) return;
+  if (tid == 0) s_any = 0;
+  __syncthreads();
+  for (int i = tid; i < top_k; i += blockDim.x)
+    if (s_dst[i] >= 0) s_any = 1;
+  __syncthreads();
+  if (!s_any) return;
   const bool active = tid * 16 < K;
   float x[16];
   if (active) {
@@ -1222,24 +1042,28 @@ int sm_count() {
   return n;
 }
 
-// The activation split of M tokens: each token's terms go to its route
-// slots (slot_of), or, with plan->ids (token rows on this GPU,
-// M * top_k <= kInlinePlanRoutes), the split computes the slots itself and is
-// the first kernel of the call, launched without PDL.
+// slot_of != nullptr or plan->ids != nullptr: token mode (n_rows source
+// tokens, terms scattered to their route slots); otherwise n_rows rows
+// (device count n_rows_dev when given, n_rows an upper bound). The plan
+// (token rows on this GPU, n_rows * top_k <= kInlinePlanRoutes) makes the
+// split the first kernel of the call, so it is launched without PDL.
 cudaError_t launch_split(const void* src, int src_dt, const SplitRows* rows,
-                         const int32_t* slot_of, int top_k, int64_t M, int K, int nt, uint8_t* q,
-                         uint8_t* sf, float* g, const float* gstatic, const int32_t* eids,
-                         const SplitInit& init, cudaStream_t stream, const InlinePlan& plan) {
-  if (M <= 0) return cudaSuccess;
+                         const int32_t* slot_of, int top_k, const int32_t* n_rows_dev,
+                         int64_t n_rows, int K, int nt, uint8_t* q, uint8_t* sf, float* g,
+                         const float* gstatic, const int32_t* eids, const int32_t* sorted,
+                         cudaStream_t stream, const InlinePlan* plan = nullptr) {
+  if (n_rows <= 0) return cudaSuccess;
   const SplitRows r = rows ? *rows : SplitRows{nullptr, 1};
-  if (plan.ids && (r.base || M * top_k > kInlinePlanRoutes || plan.E > kMaxExperts))
+  const InlinePlan ip = plan ? *plan : InlinePlan{};
+  if (ip.ids && (r.base || n_rows * top_k > kInlinePlanRoutes || ip.E > kMaxExperts))
     return cudaErrorInvalidValue;
   if (K % 16 != 0 || K / 16 > 1024) return cudaErrorInvalidValue;
-  // one CTA per token (rows on another GPU then cross NVLink once)
+  // one CTA per row (rows on another GPU then cross NVLink once)
   const int threads = std::max(kSplitThreads, (K / 16 + 31) / 32 * 32);
-  return launch_kernel(plan.ids == nullptr, split_nvfp4_kernel, dim3(static_cast<unsigned>(M)),
-                       dim3(threads), 0, stream, src, src_dt, r, plan.ids ? nullptr : slot_of,
-                       top_k, K, nt, q, sf, g, gstatic, eids, plan, init);
+  const dim3 grid(static_cast<unsigned>(n_rows));
+  return launch_kernel(ip.ids == nullptr, split_nvfp4_kernel, grid, dim3(threads), 0, stream, src,
+                       src_dt, r, ip.ids ? nullptr : slot_of, top_k, n_rows_dev, K, nt, q, sf, g,
+                       gstatic, eids, sorted, ip);
 }
 
 }  // namespace
@@ -1334,31 +1158,13 @@ cudaError_t launch_moe_bs(const BsLaunch& a, cudaStream_t stream, const char** s
   p2.out_ld = a.K;
   p2.stream_weights = R <= static_cast<int64_t>(a.E) * (bnr2 / NT);
 
-  // gate/up: the last CTA to finish a slot's SwiGLU row splits it
-  p1.fuse = 1;
-  p1.cnt = a.hcnt;
-  p1.hq = a.hq;
-  p1.hsf = a.hsf;
-  p1.hg = a.hg;
-  p1.hstatic = a.a2_gscale;
-  p2.sorted = a.sorted;
-  p2.top_k = a.top_k;
   if (a.push.base) {
     // expert parallel: rows go back to their source ranks, unweighted
     p2.push_base = a.push.base;
     p2.push_rows = a.push.rows_per_src;
-  } else {
-    // the last CTA to finish a token's row tile combines the token's routes
-    p2.fuse = 1;
-    p2.cnt = a.ccnt;
-    p2.slot_of = a.slot_of;
-    p2.weights = a.weights;
-    p2.mult = a.multiply_router_weight;
-    p2.fout = a.out;
-    p2.fout_dt = a.out_dt;
+    p2.sorted = a.sorted;
+    p2.top_k = a.top_k;
   }
-  const SplitInit init{a.hcnt, a.I / kM, a.push.base ? nullptr : a.ccnt, a.K / (2 * kM),
-                       a.push.base ? nullptr : a.out, a.out_dt};
 
   // 1. split each token once; its terms go to all of its route slots (for a
   //    small call the split also computes the route plan, and in an
@@ -1372,23 +1178,25 @@ cudaError_t launch_moe_bs(const BsLaunch& a, cudaStream_t stream, const char** s
     const int threads = std::max(kSplitThreads, (a.K / 16 + 31) / 32 * 32);
     err = launch_kernel(true, ep_split_kernel, dim3(static_cast<unsigned>(a.M)), dim3(threads), 0,
                         stream, *a.ep, a.act_dt, a.top_k, a.K, NT, a.counts, a.offsets, a.sorted,
-                        a.slot_of, a.status, a.xq, a.xsf, a.xg, init);
+                        a.slot_of, a.status, a.xq, a.xsf, a.xg);
   } else {
     const InlinePlan plan{a.inline_plan ? a.ids : nullptr, a.E, a.counts, a.offsets, a.sorted,
                           a.slot_of, a.status};
-    err = launch_split(a.hidden, a.act_dt, &a.hidden_rows, a.slot_of, a.top_k, a.M, a.K, NT,
-                       a.xq, a.xsf, a.xg, a.a13_gscale, a.ids, init, stream, plan);
+    err = launch_split(a.hidden, a.act_dt, &a.hidden_rows, a.slot_of, a.top_k, nullptr, a.M, a.K,
+                       NT, a.xq, a.xsf, a.xg, a.a13_gscale, a.ids, a.sorted, stream, &plan);
   }
   if (err != cudaSuccess) return err;
   if (a.stage_mark) a.stage_mark(a.stage_ctx, 1);
-  // 2. gate/up + SwiGLU, each completed SwiGLU row split into the down
-  //    projection's terms by the CTA that finished it
+  // 2. gate/up + SwiGLU
   *step = "gate/up";
   err = launch_bnr<kGateUp>(bnr1, NT, m1a, m1sa, m1b, m1sb, p1, grid, stream);
   if (err != cudaSuccess) return err;
   if (a.stage_mark) a.stage_mark(a.stage_ctx, 2);
-  // 3. down projection, each completed token row tile combined over the
-  //    token's routes by the CTA that finished it (or pushed to its source)
+  // 3. split the SwiGLU rows, down projection
+  *step = "h split";
+  err = launch_split(a.h, kF32, nullptr, nullptr, 1, a.offsets + a.E, R, a.I, NT, a.hq, a.hsf,
+                     a.hg, a.a2_gscale, a.ids, a.sorted, stream);
+  if (err != cudaSuccess) return err;
   *step = "down";
   err = launch_bnr<kDown>(bnr2, NT, m2a, m2sa, m2b, m2sb, p2, grid, stream);
   if (err != cudaSuccess) return err;

@@ -37,8 +37,6 @@ WorkspacePlan plan_workspace(size_t M, size_t E, size_t top_k, size_t K, size_t 
   p.hsf = take(RT * I / 16);
   p.hg = take(RT * sizeof(float));
   p.y = take(R * K * sizeof(float));
-  p.hcnt = take(R * sizeof(int32_t));
-  p.ccnt = take(M * ((K + 255) / 256) * sizeof(int32_t));
   p.total = at;
   return p;
 }
@@ -57,10 +55,10 @@ int count_launches(int64_t M, int top_k, int K, int I, bool rows_local) {
   const int plan = plan_in_split(R, K, I, rows_local, false) ? 0
                    : route_plan_chunks(R) > 1                 ? 2
                                                               : 1;
-  // block-scaled path: activation split, gate/up (SwiGLU split in its
-  // epilogue), down (combine in its epilogue); CUDA-core path: gate/up, down,
-  // combine.
-  return plan + 3;
+  // block-scaled path: activation split, gate/up, SwiGLU split, down;
+  // CUDA-core path: gate/up, down. Both end with the combine.
+  const int body = bs_supported(K, I) ? 4 : 2;
+  return plan + body + 1;
 }
 
 cudaError_t run_moe(const MoeArgs& a, const WorkspacePlan& plan, void* workspace,
@@ -131,12 +129,6 @@ cudaError_t run_moe(const MoeArgs& a, const WorkspacePlan& plan, void* workspace
     t.hsf = reinterpret_cast<uint8_t*>(ws + plan.hsf);
     t.hg = reinterpret_cast<float*>(ws + plan.hg);
     t.y = y;
-    t.hcnt = reinterpret_cast<int32_t*>(ws + plan.hcnt);
-    t.ccnt = reinterpret_cast<int32_t*>(ws + plan.ccnt);
-    t.weights = weights;
-    t.multiply_router_weight = a.multiply_router_weight;
-    t.out = a.out;
-    t.out_dt = a.out_dt;
     t.status = status;
     t.ep = a.ep_split;
     t.push = a.push;
@@ -177,7 +169,7 @@ cudaError_t run_moe(const MoeArgs& a, const WorkspacePlan& plan, void* workspace
     if (err != cudaSuccess) { *why = "down"; return err; }
     if ((err = mark(3)) != cudaSuccess) { *why = "stage event"; return err; }
   }
-  if (!bs_supported(a.K, a.I)) {  // the block-scaled down projection combines itself
+  if (!a.push.base) {  // expert parallel: the sources sum the pushed rows
     err = launch_combine(y, slot_of, weights, a.multiply_router_weight, a.out, a.out_dt, a.M,
                          a.top_k, a.K, stream);
     if (err != cudaSuccess) { *why = "combine"; return err; }

@@ -27,8 +27,6 @@ struct WorkspacePlan {
   size_t xq, xsf, xg;   // activation split terms: [R*NT, K/2], [R*NT, K/16], fp32 [R*NT]
   size_t hq, hsf, hg;   // SwiGLU split terms:     [R*NT, I/2], [R*NT, I/16], fp32 [R*NT]
   size_t y;             // fp32[R, K] down-projection output per slot
-  size_t hcnt;          // int32[R]        arrival counters, gate/up row tiles
-  size_t ccnt;          // int32[M, K/256] arrival counters, down row tiles
   size_t total;
 };
 

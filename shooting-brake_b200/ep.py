@@ -28,7 +28,7 @@ from . import DTYPE_CODE, Sbb200Error, _check, _check_cuda, _p, _stream, last_er
 HANDLE_BYTES = 64
 STAGE_EVENTS = 8
 STAGE_NAMES = ("publish", "gather+wait", "exchange+route_plan+split(pull)", "gate_up",
-               "down(push)", "none", "final+wait")
+               "h_split+down(push)", "combine(none)", "final+wait")
 
 
 def expert_shard(E: int, world: int, rank: int) -> tuple[int, int]:

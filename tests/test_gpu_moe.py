@@ -112,12 +112,12 @@ def test_out_of_range_ids_are_dropped_and_counted(sbb, oracle, cuda, K, I, T):
 
 
 def test_launch_count(sbb, cuda):
-    # block-scaled path: split (+ route plan above 1,024 routes), gate/up
-    # (SwiGLU split in its epilogue), down (combine in its epilogue)
-    assert sbb.kernels_per_call(64, 170, 8, 4096, 1280) == 3
-    assert sbb.kernels_per_call(128, 170, 8, 4096, 1280) == 3
-    assert sbb.kernels_per_call(129, 170, 8, 4096, 1280) == 4
-    assert sbb.kernels_per_call(8192, 170, 8, 4096, 1280) == 5  # 16 route-plan chunks
+    # block-scaled path: split (+ route plan above 1,024 routes), gate/up,
+    # SwiGLU split, down, combine
+    assert sbb.kernels_per_call(64, 170, 8, 4096, 1280) == 5
+    assert sbb.kernels_per_call(128, 170, 8, 4096, 1280) == 5
+    assert sbb.kernels_per_call(129, 170, 8, 4096, 1280) == 6
+    assert sbb.kernels_per_call(8192, 170, 8, 4096, 1280) == 7  # 16 route-plan chunks
 
 
 def test_custom_op_and_validation(sbb, oracle, cuda):
