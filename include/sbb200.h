@@ -93,8 +93,10 @@ int sbb200_nvfp4_moe(void* stream, const void* hidden, const int32_t* topk_ids,
  * launches in the same order, with cudaEvent_t stage_events[i] recorded on
  * `stream` at the stage boundaries: [0] start, [1] after the route plan
  * (and the activation split), [2] after the gate/up + SwiGLU GEMM, [3] after
- * the down projection (and the split of its input), [4] after the combine. n_stage_events must be SBB200_STAGE_EVENTS; NULL entries are
- * skipped. */
+ * the down projection (and the split of its input), [4] after the combine.
+ * n_stage_events must be SBB200_STAGE_EVENTS; NULL entries are skipped.
+ * Inside a stream capture the events are recorded as external events, so
+ * they stay timeable after each replay of the graph. */
 #define SBB200_STAGE_EVENTS 5
 int sbb200_nvfp4_moe_staged(void* stream, const void* hidden, const int32_t* topk_ids,
                             const float* topk_weights, const void* w13, const void* w13_scales,

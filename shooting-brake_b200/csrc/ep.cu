@@ -463,8 +463,7 @@ int sbb200_ep_forward_staged(sbb200_ep_t* p, void* stream, const void* hidden,
     auto s = static_cast<cudaStream_t>(stream);
     auto mark = [&](int i) {
       if (stage_events && stage_events[i])
-        cudaEventRecordWithFlags(static_cast<cudaEvent_t>(stage_events[i]), s,
-                                 cudaEventRecordExternal);
+        sbb::record_stage_event(static_cast<cudaEvent_t>(stage_events[i]), s);
     };
     mark(0);
     const int64_t K = static_cast<int64_t>(p->K);

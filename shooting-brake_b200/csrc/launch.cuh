@@ -38,4 +38,16 @@ cudaError_t launch_kernel(bool pdl, void (*kernel)(KArgs...), dim3 grid, dim3 bl
   return cudaLaunchKernelEx(&cfg, kernel, static_cast<KArgs>(args)...);
 }
 
+// Records a stage event on `stream`; inside a stream capture as an external
+// event node, so the event stays timeable after each replay of the graph
+// (outside a capture a plain record, the only form allowed there).
+inline cudaError_t record_stage_event(cudaEvent_t ev, cudaStream_t stream) {
+  cudaStreamCaptureStatus st = cudaStreamCaptureStatusNone;
+  const cudaError_t err = cudaStreamIsCapturing(stream, &st);
+  if (err != cudaSuccess) return err;
+  return st == cudaStreamCaptureStatusActive
+             ? cudaEventRecordWithFlags(ev, stream, cudaEventRecordExternal)
+             : cudaEventRecord(ev, stream);
+}
+
 }  // namespace sbb

@@ -2,6 +2,7 @@
 #include "moe_driver.h"
 
 #include "kernels.h"
+#include "launch.cuh"
 
 namespace sbb {
 
@@ -75,9 +76,7 @@ cudaError_t run_moe(const MoeArgs& a, const WorkspacePlan& plan, void* workspace
   const int64_t R = a.M * a.top_k;
   auto mark = [&](int i) -> cudaError_t {
     if (!a.stage_events || !a.stage_events[i]) return cudaSuccess;
-    // external: inside a stream capture the event stays timeable after replay
-    return cudaEventRecordWithFlags(static_cast<cudaEvent_t>(a.stage_events[i]), stream,
-                                    cudaEventRecordExternal);
+    return record_stage_event(static_cast<cudaEvent_t>(a.stage_events[i]), stream);
   };
 
   cudaError_t err = mark(0);
@@ -145,9 +144,7 @@ cudaError_t run_moe(const MoeArgs& a, const WorkspacePlan& plan, void* workspace
     if (a.stage_events) {
       t.stage_mark = [](void* c, int i) {
         auto* x = static_cast<Ctx*>(c);
-        if (x->ev[i])
-          cudaEventRecordWithFlags(static_cast<cudaEvent_t>(x->ev[i]), x->s,
-                                   cudaEventRecordExternal);
+        if (x->ev[i]) record_stage_event(static_cast<cudaEvent_t>(x->ev[i]), x->s);
       };
       t.stage_ctx = &ctx;
     }

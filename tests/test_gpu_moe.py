@@ -191,3 +191,35 @@ def test_cuda_graph_replay(sbb, oracle, cuda):
     g.replay()
     torch.cuda.synchronize()
     check(out.cpu().numpy(), oracle.moe_forward(hidden, ids2, w2, L))
+
+
+def test_staged_call_matches_plain_call(sbb, oracle, cuda):
+    """The staged entry point (events between the stages) gives the same bytes
+    as the plain one, eagerly and inside a CUDA graph, and its events time."""
+    L = oracle.make_layer(16, 1024, 512, seed=91)
+    hidden = dev(oracle.make_hidden(40, 1024, seed=92), cuda, torch.bfloat16)
+    ids, w = oracle.route_logits(40, 16, 4, seed=93)
+    ids, w = dev(ids, cuda), dev(w, cuda)
+    tensors = layer_to(L, cuda)
+    want = sbb._nvfp4_moe_impl(hidden, ids, w, *tensors, True, torch.float32)
+    evs = sbb.stage_events()
+    got = sbb._nvfp4_moe_impl(hidden, ids, w, *tensors, True, torch.float32, stage_events=evs)
+    torch.cuda.synchronize()
+    assert torch.equal(got, want)
+    assert all(evs[j].elapsed_time(evs[j + 1]) >= 0 for j in range(len(evs) - 1))
+    out = torch.empty_like(want)
+    cap = torch.cuda.Stream(cuda)
+    cap.wait_stream(torch.cuda.current_stream(cuda))
+    with torch.cuda.stream(cap):
+        sbb._nvfp4_moe_impl(hidden, ids, w, *tensors, True, torch.float32, out=out)
+    torch.cuda.synchronize()
+    g = torch.cuda.CUDAGraph()
+    evs = sbb.stage_events()
+    with torch.cuda.graph(g, stream=cap):
+        sbb._nvfp4_moe_impl(hidden, ids, w, *tensors, True, torch.float32, out=out,
+                            stage_events=evs)
+    out.zero_()
+    g.replay()
+    torch.cuda.synchronize()
+    assert torch.equal(out, want)
+    assert evs[0].elapsed_time(evs[-1]) > 0
