@@ -55,15 +55,25 @@ __global__ void __launch_bounds__(kThreads) combine_kernel(
   for (int n4 = (blockIdx.y * kThreads + threadIdx.x) * 4; n4 < K;
        n4 += gridDim.y * kThreads * 4) {
     float4 acc = make_float4(0.f, 0.f, 0.f, 0.f);
-    for (int k = 0; k < top_k; ++k) {
-      const int32_t s = s_slot[k];
-      if (s < 0) continue;
-      const float w = s_w[k];
-      const float4 v = __ldg(reinterpret_cast<const float4*>(y + (int64_t)s * K + n4));
-      acc.x = fmaf(w, v.x, acc.x);
-      acc.y = fmaf(w, v.y, acc.y);
-      acc.z = fmaf(w, v.z, acc.z);
-      acc.w = fmaf(w, v.w, acc.w);
+    // routes in groups of 8: the group's loads are all issued before the
+    // sums, which still run in ascending k
+    for (int k0 = 0; k0 < top_k; k0 += 8) {
+      float4 v[8];
+#pragma unroll
+      for (int j = 0; j < 8; ++j) {
+        const int32_t s = k0 + j < top_k ? s_slot[k0 + j] : -1;
+        v[j] = s >= 0 ? __ldg(reinterpret_cast<const float4*>(y + (int64_t)s * K + n4))
+                      : make_float4(0.f, 0.f, 0.f, 0.f);
+      }
+#pragma unroll
+      for (int j = 0; j < 8; ++j) {
+        if (k0 + j >= top_k || s_slot[k0 + j] < 0) continue;
+        const float w = s_w[k0 + j];
+        acc.x = fmaf(w, v[j].x, acc.x);
+        acc.y = fmaf(w, v[j].y, acc.y);
+        acc.z = fmaf(w, v[j].z, acc.z);
+        acc.w = fmaf(w, v[j].w, acc.w);
+      }
     }
     store4(out, out_dt, t * K + n4, acc);
   }

@@ -202,15 +202,25 @@ __global__ void __launch_bounds__(kEpThreads) ep_final_kernel(
     for (int n4 = (blockIdx.y * blockDim.x + threadIdx.x) * 4; n4 < K;
          n4 += gridDim.y * blockDim.x * 4) {
       float4 acc = make_float4(0.f, 0.f, 0.f, 0.f);
-      for (int k = 0; k < top_k; ++k) {
-        if (!s_k[k]) continue;
-        const float w = s_w[k];
-        const float4 p = __ldcg(reinterpret_cast<const float4*>(
-            partial + (t * top_k + k) * static_cast<int64_t>(K) + n4));
-        acc.x = fmaf(w, p.x, acc.x);
-        acc.y = fmaf(w, p.y, acc.y);
-        acc.z = fmaf(w, p.z, acc.z);
-        acc.w = fmaf(w, p.w, acc.w);
+      // routes in groups of 8: the group's loads first, the sums in
+      // ascending k
+      for (int k0 = 0; k0 < top_k; k0 += 8) {
+        float4 v[8];
+#pragma unroll
+        for (int j = 0; j < 8; ++j)
+          v[j] = (k0 + j < top_k && s_k[k0 + j])
+                     ? __ldcg(reinterpret_cast<const float4*>(
+                           partial + (t * top_k + k0 + j) * static_cast<int64_t>(K) + n4))
+                     : make_float4(0.f, 0.f, 0.f, 0.f);
+#pragma unroll
+        for (int j = 0; j < 8; ++j) {
+          if (k0 + j >= top_k || !s_k[k0 + j]) continue;
+          const float w = s_w[k0 + j];
+          acc.x = fmaf(w, v[j].x, acc.x);
+          acc.y = fmaf(w, v[j].y, acc.y);
+          acc.z = fmaf(w, v[j].z, acc.z);
+          acc.w = fmaf(w, v[j].w, acc.w);
+        }
       }
       const int64_t at = t * K + n4;
       if (out_dt == kF32) {

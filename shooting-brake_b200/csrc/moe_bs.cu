@@ -210,6 +210,11 @@ __global__ void __launch_bounds__(kThreads, 1)
   __shared__ uint32_t tmem_base_s;
   __shared__ int abort_s;
   __shared__ int prefix[kMaxExperts + 1];
+  // per-expert routed count, first slot and weight global, staged once so
+  // the producer and the epilogue read shared memory at every unit start
+  __shared__ int s_cnt[kMaxExperts];
+  __shared__ int s_off[kMaxExperts];
+  __shared__ float s_gs[kMaxExperts];
 
   const int tid = threadIdx.x;
   const int warp = tid >> 5;
@@ -249,20 +254,31 @@ __global__ void __launch_bounds__(kThreads, 1)
   pdl_trigger();
   // the wait limit runs from here, so a long predecessor does not eat into it
   const uint64_t deadline = now_ns() + p.wait_ns;
-  if (warp == 2) {
-    int carry = 0;
-    for (int e0 = 0; e0 < p.E; e0 += 32) {
-      const int e = e0 + lane;
-      int v = e < p.E ? (p.counts[e] + C::kTok - 1) / C::kTok : 0;
-#pragma unroll
-      for (int d = 1; d < 32; d <<= 1) {
-        const int n = __shfl_up_sync(0xffffffffu, v, d);
-        if (lane >= d) v += n;
-      }
-      if (e < p.E) prefix[e + 1] = carry + v;
-      carry += __shfl_sync(0xffffffffu, v, 31);
+  if (warp == 2 || warp == 3) {
+    // every expert's count, first slot and global in one batch of loads
+    // (kMaxExperts / 64 per thread), then warp 2 scans the tile counts
+    const int t64 = tid - 64;
+    for (int e = t64; e < p.E; e += 64) {
+      s_cnt[e] = p.counts[e];
+      s_off[e] = p.offsets[e];
+      s_gs[e] = p.gscale[e];
     }
-    if (lane == 0) prefix[0] = 0;
+    asm volatile("bar.sync 2, 64;" ::: "memory");
+    if (warp == 2) {
+      int carry = 0;
+      for (int e0 = 0; e0 < p.E; e0 += 32) {
+        const int e = e0 + lane;
+        int v = e < p.E ? (s_cnt[e] + C::kTok - 1) / C::kTok : 0;
+#pragma unroll
+        for (int d = 1; d < 32; d <<= 1) {
+          const int n = __shfl_up_sync(0xffffffffu, v, d);
+          if (lane >= d) v += n;
+        }
+        if (e < p.E) prefix[e + 1] = carry + v;
+        carry += __shfl_sync(0xffffffffu, v, 31);
+      }
+      if (lane == 0) prefix[0] = 0;
+    }
   }
   tc_fence_before();
   __syncthreads();
@@ -285,7 +301,7 @@ __global__ void __launch_bounds__(kThreads, 1)
       for (int u = blockIdx.x; u < total_units && ok; u += gridDim.x) {
         int e, nt, mt;
         decode_unit(u, p.m_tiles, prefix, p.E, e, nt, mt);
-        const int row_b = (p.offsets[e] + nt * C::kTok) * NT;
+        const int row_b = (s_off[e] + nt * C::kTok) * NT;
         const int r0 = e * p.rows_per_expert + mt * (MODE == kGateUp ? kM : 2 * kM);
         for (int kk = 0; kk < p.k_stages; ++kk) {
           if (!mbar_wait(&empty[s], ph ^ 1u, abort, deadline)) {
@@ -450,9 +466,9 @@ __global__ void __launch_bounds__(kThreads, 1)
       const int d = ui % NB;
       if (!warp_wait(&dfull[d], (ui / NB) & 1u, abort, deadline)) break;
       tc_fence_after();
-      const int valid = min(C::kTok, p.counts[e] - nt * C::kTok);
-      const int slot0 = p.offsets[e] + nt * C::kTok;
-      const float gs = p.gscale[e];
+      const int valid = min(C::kTok, s_cnt[e] - nt * C::kTok);
+      const int slot0 = s_off[e] + nt * C::kTok;
+      const float gs = s_gs[e];
       const uint32_t taddr = tmem + lane_base + d * C::kDCols;
 #pragma unroll 1
       for (int c0 = team * 16; c0 < BNR; c0 += 32) {
@@ -691,6 +707,9 @@ __device__ __forceinline__ void plan_route_slots(IdOf id_of, int E, int64_t row,
   const int lane = tid & 31;
   const int R = static_cast<int>(gridDim.x) * top_k;
   const int r0 = static_cast<int>(row) * top_k;
+  // this kernel starts the call: CTA 0 clears the status words (the
+  // bad-id count it adds to below, the GEMMs' error word)
+  if (status && blockIdx.x == 0 && tid < 2) status[tid] = 0u;
   for (int e = tid; e <= E; e += blockDim.x) s_off[e] = 0;
   for (int i = tid; i < top_k; i += blockDim.x) {
     s_rank[i] = 0;

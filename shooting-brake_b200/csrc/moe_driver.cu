@@ -85,14 +85,16 @@ cudaError_t run_moe(const MoeArgs& a, const WorkspacePlan& plan, void* workspace
     *why = "expert-parallel exchange needs K and I multiples of 256";
     return cudaErrorInvalidValue;
   }
-  if (!a.ep_split) {  // the exchange split clears the status words itself
-    err = cudaMemsetAsync(status, 0, 256, stream);
-    if (err != cudaSuccess) { *why = "status clear"; return err; }
-  }
   const int32_t* ids = a.router_logits ? a.routed_ids : a.ids;
   const float* weights = a.router_logits ? a.routed_weights : a.weights;
   const bool inline_plan = plan_in_split(R, a.K, a.I, a.hidden_rows.base == nullptr,
                                          a.router_logits != nullptr);
+  // a split that plans the routes itself, or exchanges the step, is the
+  // call's first kernel and clears the status words; otherwise a memset does
+  if (!a.ep_split && !inline_plan) {
+    err = cudaMemsetAsync(status, 0, 256, stream);
+    if (err != cudaSuccess) { *why = "status clear"; return err; }
+  }
   if (!inline_plan && !a.ep_split) {
     err = launch_route_plan(ids, R, a.E, chunk_counts, counts, offsets, sorted, slot_of, status,
                             stream, a.router_logits, a.logits_dt, a.top_k, a.routed_weights);
