@@ -171,7 +171,14 @@ bool bs_supported(int K, int I);
 uint64_t set_kernel_wait_ns(uint64_t ns);
 // Reads and clears the current device's sticky GEMM error bits (synchronises).
 cudaError_t read_sticky_errors(cudaStream_t stream, uint32_t* errors);
-int bs_tile_rows(int64_t routes, int E, int mode, int nt);
+// Token tile of one grouped GEMM: N = bnr (term rows, or tokens when kt),
+// kt: the activation terms are planes along K (prefill-sized calls).
+struct BsTile {
+  int bnr;
+  bool kt;
+};
+// mode: 0 gate/up, 1 down.
+BsTile bs_tile(int64_t routes, int E, int mode, int nt);
 cudaError_t launch_moe_bs(const BsLaunch& a, cudaStream_t stream, const char** step);
 
 }  // namespace sbb

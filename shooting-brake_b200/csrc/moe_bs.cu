@@ -18,10 +18,18 @@
 // e4m3 range without a new row reduction per term, and each block runs its
 // NT terms on its own. With NT = 4 the represented activations are within
 // ~1e-4 (normwise) of the inputs, finer than the bf16 rounding of the inputs
-// themselves. The terms of a row sit in
-// consecutive rows of the N operand, so one MMA covers all terms of BN/NT
-// routed tokens and the epilogue folds them: D[:, slot] = sum_t D[:, slot*NT
-// + t] * g_t.
+// themselves. Two layouts of the terms:
+//   rows  (decode-sized tiles): the terms of a row sit in consecutive rows of
+//         the N operand, so one MMA covers all terms of BN/NT routed tokens
+//         and the epilogue folds them: D[:, slot] = sum_t D[:, slot*NT + t] *
+//         g_t. Few tokens per expert: N stays small and the MMA count low.
+//   K     (prefill-sized tiles): term t of every slot sits in plane t
+//         ([NT][R][K/2]); every term shares the row's global g_0 (the 4^-t
+//         factor lives in the e4m3 block scales instead, same precision), so
+//         x.W = sum_t x_t.W accumulates in one TMEM column per token: the MMA
+//         runs over the NT planes as if they were a longer K. A weight tile
+//         then serves NT times as many tokens per byte staged, which is what
+//         bounds the prefill GEMMs (shared-memory fill rate from L2).
 //
 // A work unit is (expert, weight-row tile, token tile): 128 gate rows plus
 // the matching 128 up rows (gate/up), or 256 consecutive w2 rows (down),
@@ -61,6 +69,8 @@ namespace {
 using namespace ptx;
 
 constexpr int kBK = 256;              // K elements per pipeline stage
+// Mean routes per expert from which the activation terms go along K.
+constexpr double kKtMinTokens = 96.0;
 constexpr int kRowBytes = kBK / 2;    // packed bytes per row per stage (128)
 constexpr int kRowScales = kBK / 16;  // scale bytes per row per stage (16)
 constexpr int kM = 128;
@@ -107,16 +117,20 @@ struct BsParams {
   int top_k;
 };
 
-template <int MODE, int BNR, int NT>
+// BNR: the MMA's N. KT = false: N = BNR term rows (BNR / NT tokens, terms
+// interleaved); KT = true: N = BNR tokens, their NT term planes staged one
+// after the other and run as NT K-slices into the same accumulator.
+template <int MODE, int BNR, int NT, bool KT = false>
 struct BsCfg {
   // two 128-row weight blocks per unit: gate and up rows (gate/up) or 256
   // consecutive rows of w2 (down), each into its own accumulator
   static constexpr int kNA = 2;
-  static constexpr int kTok = BNR / NT;                    // routed tokens per tile
+  static constexpr int kTok = KT ? BNR : BNR / NT;         // routed tokens per tile
+  static constexpr int kBSets = KT ? NT : 1;               // B operands per K group
   static constexpr int kA = kNA * kM * kRowBytes;          // packed weights
-  static constexpr int kB = BNR * kRowBytes;               // packed term rows
+  static constexpr int kB = kBSets * BNR * kRowBytes;      // packed term rows
   static constexpr int kSA = kNA * kM * kRowScales;        // linear weight scales
-  static constexpr int kSB = BNR * kRowScales;             // linear term scales
+  static constexpr int kSB = kBSets * BNR * kRowScales;    // linear term scales
   static constexpr int kRaw = kA + kB + kSA + kSB;
   static constexpr int kStageBytes = (kRaw + 1023) / 1024 * 1024;
   static constexpr int kStagesRaw = (224 * 1024 - 1024) / kStageBytes;
@@ -130,13 +144,15 @@ struct BsCfg {
   // columns, lane n % 32 of every 32-lane quarter: a 128-row A block takes 4
   // columns per K group, B takes 4 (up to 128 rows) or 8 (up to 256), so
   // every scale address handed to the MMA is 4-column aligned; B fills the
-  // first ceil(rows / 32) of its columns and zeroes the rest.
+  // first ceil(rows / 32) of its columns and zeroes the rest. With KT each
+  // term plane t has its own B scale columns: group kg of plane t at
+  // (t * 4 + kg) * kBC.
   static constexpr int kDCols = kNA * BNR;
   static constexpr int kBQ = (BNR + 31) / 32;        // B row quarters in use
   static constexpr int kBC = BNR > 128 ? 8 : 4;      // B scale columns per K group
   // per buffer, a multiple of 16 so every tcgen05.st (x4/x8/x16) starts on a
   // column aligned to its width
-  static constexpr int kSfCols = kNA * 16 + 4 * kBC;
+  static constexpr int kSfCols = kNA * 16 + kBSets * 4 * kBC;
   static constexpr int kDBufs = 2 * kDCols + 2 * kSfCols <= kTmemCols ? 2 : 1;
   static constexpr int kSfCol0 = kDBufs * kDCols;
   // scale-factor ring: as many buffers as tensor memory leaves room for, up
@@ -148,7 +164,8 @@ struct BsCfg {
   static_assert(kSmem <= 227 * 1024, "shared memory");
   static_assert(kSfCol0 % 16 == 0 && kSfCols % 16 == 0, "tensor-memory store alignment");
   static_assert(kSfBufs >= 2 && kSfCol0 + kSfBufs * kSfCols <= kTmemCols, "tensor memory");
-  static_assert(BNR % 16 == 0 && BNR >= 16 && BNR <= 256 && BNR % NT == 0, "tile");
+  static_assert(BNR % 16 == 0 && BNR >= 16 && BNR <= 256 && (KT || BNR % NT == 0), "tile");
+  static_assert(!KT || (BNR * kRowBytes) % 1024 == 0, "term planes keep the 1024-byte swizzle atom");
 };
 
 __device__ __forceinline__ void decode_unit(int u, int m_tiles, const int* prefix, int E, int& e,
@@ -193,12 +210,12 @@ __device__ __forceinline__ void mma_bs(uint32_t d_tmem, uint64_t a_desc, uint64_
       : "memory");
 }
 
-template <int MODE, int BNR, int NT>
+template <int MODE, int BNR, int NT, bool KT>
 __global__ void __launch_bounds__(kThreads, 1)
     moe_gemm_bs_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmSA,
                        const __grid_constant__ CUtensorMap tmB, const __grid_constant__ CUtensorMap tmSB,
                        const BsParams p) {
-  using C = BsCfg<MODE, BNR, NT>;
+  using C = BsCfg<MODE, BNR, NT, KT>;
   constexpr int S = C::kStages;
   constexpr int NB = C::kDBufs;
   extern __shared__ uint8_t smem_raw[];
@@ -301,7 +318,8 @@ __global__ void __launch_bounds__(kThreads, 1)
       for (int u = blockIdx.x; u < total_units && ok; u += gridDim.x) {
         int e, nt, mt;
         decode_unit(u, p.m_tiles, prefix, p.E, e, nt, mt);
-        const int row_b = (s_off[e] + nt * C::kTok) * NT;
+        // first term row (rows layout) or first slot (KT: the planes' y)
+        const int row_b = (s_off[e] + nt * C::kTok) * (KT ? 1 : NT);
         const int r0 = e * p.rows_per_expert + mt * (MODE == kGateUp ? kM : 2 * kM);
         for (int kk = 0; kk < p.k_stages; ++kk) {
           if (!mbar_wait(&empty[s], ph ^ 1u, abort, deadline)) {
@@ -319,8 +337,14 @@ __global__ void __launch_bounds__(kThreads, 1)
             tma_load_2d_hint(st + C::kOffSA + a * kM * kRowScales, &tmSA, &full[s], xs,
                              r0 + a * p.a_stride, pol_w);
           }
-          tma_load_2d_hint(st + C::kOffB, &tmB, &full[s], xa, row_b, pol_x);
-          tma_load_2d_hint(st + C::kOffSB, &tmSB, &full[s], xs, row_b, pol_x);
+          if (KT) {
+            // all NT planes of the tile's slots in one box: [plane][slot][bytes]
+            tma_load_3d_hint(st + C::kOffB, &tmB, &full[s], xa, row_b, 0, pol_x);
+            tma_load_3d_hint(st + C::kOffSB, &tmSB, &full[s], xs, row_b, 0, pol_x);
+          } else {
+            tma_load_2d_hint(st + C::kOffB, &tmB, &full[s], xa, row_b, pol_x);
+            tma_load_2d_hint(st + C::kOffSB, &tmSB, &full[s], xs, row_b, pol_x);
+          }
           issued[s] = true;
           issued_phase[s] = ph;
           if (++s == S) {
@@ -346,6 +370,14 @@ __global__ void __launch_bounds__(kThreads, 1)
       bool ok = true;
       for (int u = blockIdx.x; u < total_units && ok; u += gridDim.x, ++ui) {
         const int d = ui % NB;
+        // the MMA's N covers the tile's routed tokens (rounded up to 16 rows),
+        // so an expert's last, partly filled tile costs only what it holds
+        int e, nt, mt;
+        decode_unit(u, p.m_tiles, prefix, p.E, e, nt, mt);
+        const int valid = min(C::kTok, s_cnt[e] - nt * C::kTok);
+        const int n_rows = KT ? valid : valid * NT;
+        const int n_mma = min(BNR, max(16, (n_rows + 15) & ~15));
+        const uint32_t idesc = (C::kIdesc & ~(0x3Fu << 17)) | (static_cast<uint32_t>(n_mma >> 3) << 17);
         if (!mbar_wait(&dempty[d], ((ui / NB) & 1u) ^ 1u, abort, deadline)) break;
         tc_fence_after();
         const uint32_t d_tm = tmem + d * C::kDCols;
@@ -363,13 +395,16 @@ __global__ void __launch_bounds__(kThreads, 1)
           const uint32_t sf0 = tmem + C::kSfCol0 + sb * C::kSfCols;
 #pragma unroll
           for (int kg = 0; kg < 4; ++kg) {
-            const uint64_t bd = desc_sw128(b_sa + kg * 32);
-            const uint32_t acc = (kk | kg) != 0;
 #pragma unroll
-            for (int a = 0; a < C::kNA; ++a) {
-              const uint64_t ad = desc_sw128(a_sa + a * kM * kRowBytes + kg * 32);
-              mma_bs(d_tm + a * BNR, ad, bd, C::kIdesc, sf0 + a * 16 + kg * 4,
-                     sf0 + C::kNA * 16 + kg * C::kBC, acc);
+            for (int t = 0; t < C::kBSets; ++t) {
+              const uint64_t bd = desc_sw128(b_sa + t * BNR * kRowBytes + kg * 32);
+              const uint32_t acc = (kk | kg | t) != 0;
+#pragma unroll
+              for (int a = 0; a < C::kNA; ++a) {
+                const uint64_t ad = desc_sw128(a_sa + a * kM * kRowBytes + kg * 32);
+                mma_bs(d_tm + a * BNR, ad, bd, idesc, sf0 + a * 16 + kg * 4,
+                       sf0 + C::kNA * 16 + (t * 4 + kg) * C::kBC, acc);
+              }
             }
           }
           mma_commit(&empty[s]);
@@ -423,20 +458,24 @@ __global__ void __launch_bounds__(kThreads, 1)
           tmem_st16(sf0 + a * 16, ra);
         }
         constexpr int BC = C::kBC;
-        uint32_t rb[4 * BC];
+#pragma unroll 1
+        for (int t = 0; t < C::kBSets; ++t) {
+          uint32_t rb[4 * BC];
 #pragma unroll
-        for (int r1 = 0; r1 < BC; ++r1) {
-          const int n = r1 * 32 + lane;
-          uint4 v = make_uint4(0, 0, 0, 0);
-          if (r1 < C::kBQ && n < BNR)
-            v = *reinterpret_cast<const uint4*>(st + C::kOffSB + n * kRowScales);
-          rb[0 * BC + r1] = v.x;
-          rb[1 * BC + r1] = v.y;
-          rb[2 * BC + r1] = v.z;
-          rb[3 * BC + r1] = v.w;
+          for (int r1 = 0; r1 < BC; ++r1) {
+            const int n = r1 * 32 + lane;
+            uint4 v = make_uint4(0, 0, 0, 0);
+            if (r1 < C::kBQ && n < BNR)
+              v = *reinterpret_cast<const uint4*>(st + C::kOffSB + (t * BNR + n) * kRowScales);
+            rb[0 * BC + r1] = v.x;
+            rb[1 * BC + r1] = v.y;
+            rb[2 * BC + r1] = v.z;
+            rb[3 * BC + r1] = v.w;
+          }
+#pragma unroll
+          for (int c = 0; c < 4 * BC; c += 16)
+            tmem_st16(sf0 + C::kNA * 16 + t * 4 * BC + c, rb + c);
         }
-#pragma unroll
-        for (int c = 0; c < 4 * BC; c += 16) tmem_st16(sf0 + C::kNA * 16 + c, rb + c);
         tmem_wait_st();
         tc_fence_before();
         __syncwarp();
@@ -470,24 +509,33 @@ __global__ void __launch_bounds__(kThreads, 1)
       const int slot0 = s_off[e] + nt * C::kTok;
       const float gs = s_gs[e];
       const uint32_t taddr = tmem + lane_base + d * C::kDCols;
+      // columns past the tile's last token were not written by the MMA
+      const int n_cols = KT ? valid : valid * NT;
 #pragma unroll 1
-      for (int c0 = team * 16; c0 < BNR; c0 += 32) {
+      for (int c0 = team * 16; c0 < n_cols; c0 += 32) {
         uint32_t t0[16], t1[16];
         tmem_ld16(taddr + c0, t0);
         tmem_ld16(taddr + BNR + c0, t1);
         tmem_wait_ld();
-        constexpr int kTokPerChunk = 16 / NT;
+        constexpr int kTokPerChunk = KT ? 16 : 16 / NT;
 #pragma unroll
         for (int jj = 0; jj < kTokPerChunk; ++jj) {
-          const int j = c0 / NT + jj;  // token within the tile
+          const int j = KT ? c0 + jj : c0 / NT + jj;  // token within the tile
           if (j < valid) {
             const int slot = slot0 + j;
             float v0 = 0.0f, v1 = 0.0f;
+            if (KT) {
+              // the MMA summed the terms; they share the slot's global
+              const float g = p.bg[slot];
+              v0 = __uint_as_float(t0[jj]) * g;
+              v1 = __uint_as_float(t1[jj]) * g;
+            } else {
 #pragma unroll
-            for (int tt = 0; tt < NT; ++tt) {
-              const float g = p.bg[static_cast<int64_t>(slot) * NT + tt];
-              v0 = fmaf(__uint_as_float(t0[jj * NT + tt]), g, v0);
-              v1 = fmaf(__uint_as_float(t1[jj * NT + tt]), g, v1);
+              for (int tt = 0; tt < NT; ++tt) {
+                const float g = p.bg[static_cast<int64_t>(slot) * NT + tt];
+                v0 = fmaf(__uint_as_float(t0[jj * NT + tt]), g, v0);
+                v1 = fmaf(__uint_as_float(t1[jj * NT + tt]), g, v1);
+              }
             }
             float* orow = p.out + static_cast<int64_t>(slot) * p.out_ld;
             if (MODE == kDown && p.push_base) {
@@ -626,13 +674,17 @@ __device__ __forceinline__ void quant_block(float* v, float G, float g, uint32_t
 
 // The dynamic-global split of one row held in registers, one 16-element
 // block per thread (v; active: the block lies inside the row): the row
-// maximum by a CTA reduction, then NT residual terms under G0 * 4^t written
-// to every destination row dst[d] (d < ndst, -1 skipped), or to `row` alone
-// when dst is null. Every thread of the CTA calls it; s_max holds 32 floats.
+// maximum by a CTA reduction, then NT residual terms written to every
+// destination slot dst[d] (d < ndst, -1 skipped), or to `row` alone when dst
+// is null. Rows layout (plane = 0): term t of slot d is row d * NT + t,
+// quantised under G0 * 4^t, with global gout[d * NT + t]. K layout (plane =
+// R, the plane height): term t of slot d is row t * plane + d, every term
+// under G0 (the e4m3 block scales carry the shrinking residual), one global
+// gout[d]. Every thread of the CTA calls it; s_max holds 32 floats.
 __device__ __forceinline__ void split_row_terms(float* v, bool active, int NT, int K,
                                                 const int32_t* dst, int ndst, int64_t row,
                                                 uint8_t* q, uint8_t* sf, float* gout,
-                                                float* s_max) {
+                                                float* s_max, int64_t plane = 0) {
   const int tid = threadIdx.x;
   const int nwarps = blockDim.x >> 5;
   const int blk = tid;
@@ -651,8 +703,11 @@ __device__ __forceinline__ void split_row_terms(float* v, bool active, int NT, i
   const float g0 = __fdiv_rn(1.0f, G0);
   if (tid < ndst) {
     const int64_t d = dst ? static_cast<int64_t>(dst[tid]) : row;
-    if (d >= 0)
-      for (int t = 0; t < NT; ++t) gout[d * NT + t] = ldexpf(g0, -2 * t);
+    if (d >= 0) {
+      if (plane) gout[d] = g0;
+      else
+        for (int t = 0; t < NT; ++t) gout[d * NT + t] = ldexpf(g0, -2 * t);
+    }
   }
   if (!active) return;
   float G = G0, g = g0;
@@ -663,12 +718,14 @@ __device__ __forceinline__ void split_row_terms(float* v, bool active, int NT, i
     for (int i = 0; i < ndst; ++i) {
       const int64_t d = dst ? static_cast<int64_t>(dst[i]) : row;
       if (d < 0) continue;
-      const int64_t orow = d * NT + t;
+      const int64_t orow = plane ? t * plane + d : d * NT + t;
       *reinterpret_cast<uint2*>(q + orow * (K / 2) + blk * 8) = make_uint2(w[0], w[1]);
       sf[orow * (K / 16) + blk] = s8;
     }
-    G = __fmul_rn(G, 4.0f);
-    g = __fmul_rn(g, 0.25f);
+    if (!plane) {
+      G = __fmul_rn(G, 4.0f);
+      g = __fmul_rn(g, 0.25f);
+    }
   }
 }
 
@@ -794,7 +851,8 @@ __global__ void __launch_bounds__(1024) split_nvfp4_kernel(
     const void* __restrict__ src, int src_dt, SplitRows rows, const int32_t* __restrict__ slot_of,
     int top_k, const int32_t* __restrict__ n_rows_dev, int K, int NT, uint8_t* __restrict__ q,
     uint8_t* __restrict__ sf, float* __restrict__ gout, const float* __restrict__ gstatic,
-    const int32_t* __restrict__ eids, const int32_t* __restrict__ sorted, const InlinePlan plan) {
+    const int32_t* __restrict__ eids, const int32_t* __restrict__ sorted, const InlinePlan plan,
+    int64_t plane) {
   __shared__ float s_max[32];
   __shared__ int32_t s_dst[kMaxTopK];
   __shared__ int32_t s_off[kMaxExperts + 1];
@@ -862,7 +920,8 @@ __global__ void __launch_bounds__(1024) split_nvfp4_kernel(
     }
     return;
   }
-  split_row_terms(v, active, NT, K, token ? s_dst : nullptr, ndst, row, q, sf, gout, s_max);
+  split_row_terms(v, active, NT, K, token ? s_dst : nullptr, ndst, row, q, sf, gout, s_max,
+                  plane);
 }
 
 // Expert-parallel exchange split (EpSplitArgs): one CTA per virtual token
@@ -1010,11 +1069,27 @@ bool encode_u8(CUtensorMap* map, const void* base, uint64_t inner, uint64_t rows
             CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
 }
 
-template <int MODE, int BNR, int NT>
+// Three-dimensional u8 map of NT term planes [planes][rows][inner] (plane
+// stride rows * inner bytes), box {box_inner, box_rows, planes}.
+bool encode_u8_planes(CUtensorMap* map, const void* base, uint64_t inner, uint64_t rows,
+                      uint64_t planes, uint32_t box_inner, uint32_t box_rows,
+                      CUtensorMapSwizzle swz) {
+  auto fn = get_encode();
+  if (!fn) return false;
+  const cuuint64_t dims[3] = {inner, rows, planes};
+  const cuuint64_t strides[2] = {inner, inner * rows};
+  const cuuint32_t box[3] = {box_inner, box_rows, static_cast<cuuint32_t>(planes)};
+  const cuuint32_t estr[3] = {1, 1, 1};
+  return fn(map, CU_TENSOR_MAP_DATA_TYPE_UINT8, 3, const_cast<void*>(base), dims, strides, box,
+            estr, CU_TENSOR_MAP_INTERLEAVE_NONE, swz, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+            CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
+}
+
+template <int MODE, int BNR, int NT, bool KT>
 cudaError_t launch_gemm(const CUtensorMap& a, const CUtensorMap& sa, const CUtensorMap& b,
                         const CUtensorMap& sb, const BsParams& p, int grid, cudaStream_t stream) {
-  using C = BsCfg<MODE, BNR, NT>;
-  auto kern = moe_gemm_bs_kernel<MODE, BNR, NT>;
+  using C = BsCfg<MODE, BNR, NT, KT>;
+  auto kern = moe_gemm_bs_kernel<MODE, BNR, NT, KT>;
   int dev = 0;
   cudaError_t err = cudaGetDevice(&dev);
   if (err != cudaSuccess) return err;
@@ -1033,24 +1108,34 @@ cudaError_t launch_bnr_nt(int bnr, const CUtensorMap& a, const CUtensorMap& sa,
                           const CUtensorMap& b, const CUtensorMap& sb, const BsParams& p, int grid,
                           cudaStream_t stream) {
   switch (bnr) {
-    case 16: return launch_gemm<MODE, 16, NT>(a, sa, b, sb, p, grid, stream);
-    case 32: return launch_gemm<MODE, 32, NT>(a, sa, b, sb, p, grid, stream);
-    case 64: return launch_gemm<MODE, 64, NT>(a, sa, b, sb, p, grid, stream);
-    case 96: return launch_gemm<MODE, 96, NT>(a, sa, b, sb, p, grid, stream);
-    case 128: return launch_gemm<MODE, 128, NT>(a, sa, b, sb, p, grid, stream);
-    case 192: return launch_gemm<MODE, 192, NT>(a, sa, b, sb, p, grid, stream);
+    case 16: return launch_gemm<MODE, 16, NT, false>(a, sa, b, sb, p, grid, stream);
+    case 32: return launch_gemm<MODE, 32, NT, false>(a, sa, b, sb, p, grid, stream);
+    case 64: return launch_gemm<MODE, 64, NT, false>(a, sa, b, sb, p, grid, stream);
+    case 96: return launch_gemm<MODE, 96, NT, false>(a, sa, b, sb, p, grid, stream);
+    case 128: return launch_gemm<MODE, 128, NT, false>(a, sa, b, sb, p, grid, stream);
+    case 192: return launch_gemm<MODE, 192, NT, false>(a, sa, b, sb, p, grid, stream);
     default: return cudaErrorInvalidValue;
   }
 }
 
 // nt = 4: bf16/f16/f32 activations as four NVFP4 terms (W4A16 results);
-// nt = 1: activations quantised once (W4A4).
+// nt = 1: activations quantised once (W4A4). kt: term planes run along K
+// (N = bnr tokens), for the four-term split only.
 template <int MODE>
-cudaError_t launch_bnr(int bnr, int nt, const CUtensorMap& a, const CUtensorMap& sa,
+cudaError_t launch_bnr(const BsTile& tile, int nt, const CUtensorMap& a, const CUtensorMap& sa,
                        const CUtensorMap& b, const CUtensorMap& sb, const BsParams& p, int grid,
                        cudaStream_t stream) {
-  if (nt == kSplitTerms) return launch_bnr_nt<MODE, kSplitTerms>(bnr, a, sa, b, sb, p, grid, stream);
-  if (nt == 1) return launch_bnr_nt<MODE, 1>(bnr, a, sa, b, sb, p, grid, stream);
+  if (tile.kt) {
+    if (nt != kSplitTerms) return cudaErrorInvalidValue;
+    switch (tile.bnr) {
+      case 64: return launch_gemm<MODE, 64, kSplitTerms, true>(a, sa, b, sb, p, grid, stream);
+      case 128: return launch_gemm<MODE, 128, kSplitTerms, true>(a, sa, b, sb, p, grid, stream);
+      default: return cudaErrorInvalidValue;
+    }
+  }
+  if (nt == kSplitTerms)
+    return launch_bnr_nt<MODE, kSplitTerms>(tile.bnr, a, sa, b, sb, p, grid, stream);
+  if (nt == 1) return launch_bnr_nt<MODE, 1>(tile.bnr, a, sa, b, sb, p, grid, stream);
   return cudaErrorInvalidValue;
 }
 
@@ -1070,7 +1155,8 @@ cudaError_t launch_split(const void* src, int src_dt, const SplitRows* rows,
                          const int32_t* slot_of, int top_k, const int32_t* n_rows_dev,
                          int64_t n_rows, int K, int nt, uint8_t* q, uint8_t* sf, float* g,
                          const float* gstatic, const int32_t* eids, const int32_t* sorted,
-                         cudaStream_t stream, const InlinePlan* plan = nullptr) {
+                         cudaStream_t stream, const InlinePlan* plan = nullptr,
+                         int64_t plane = 0) {
   if (n_rows <= 0) return cudaSuccess;
   const SplitRows r = rows ? *rows : SplitRows{nullptr, 1};
   const InlinePlan ip = plan ? *plan : InlinePlan{};
@@ -1082,7 +1168,7 @@ cudaError_t launch_split(const void* src, int src_dt, const SplitRows* rows,
   const dim3 grid(static_cast<unsigned>(n_rows));
   return launch_kernel(ip.ids == nullptr, split_nvfp4_kernel, grid, dim3(threads), 0, stream, src,
                        src_dt, r, ip.ids ? nullptr : slot_of, top_k, n_rows_dev, K, nt, q, sf, g,
-                       gstatic, eids, sorted, ip);
+                       gstatic, eids, sorted, ip, plane);
 }
 
 }  // namespace
@@ -1110,17 +1196,22 @@ bool bs_supported(int K, int I) {
 
 // Term rows per MMA tile: enough for ~1.5x the mean routes per expert, up to
 // 32 tokens (from N = 128 the block-scaled MMA runs at full rate; below N =
-// 64 it costs a fixed ~46 cycles per instruction). When experts see more than
-// a full tile (prefill), gate/up takes 48 tokens (N = 192: the weight tile is
-// reused by 50 % more tokens per byte staged; one accumulator buffer) and
-// down 24 (N = 96: two accumulator buffers fit, so a unit's epilogue overlaps
-// the next unit's MMAs, which matters with only I / 256 K stages per unit).
-int bs_tile_rows(int64_t routes, int E, int mode, int nt) {
-  const double want = static_cast<double>(routes) / E * 1.5 * nt;  // term rows
+// 64 it costs a fixed ~46 cycles per instruction). When experts see more
+// tokens than that (prefill), the terms go along K instead (kt): N = 128
+// tokens per gate/up tile (one accumulator buffer) and 64 per down tile (two
+// buffers, so a unit's epilogue overlaps the next unit's MMAs, which matters
+// with only I / 256 K stages per unit). Per byte of weights staged a tile
+// then serves 128 (64) tokens instead of 48 (24); each token brings its four
+// term planes, so the bytes staged per MMA cycle drop by about a third.
+BsTile bs_tile(int64_t routes, int E, int mode, int nt) {
+  const double per_expert = static_cast<double>(routes) / E;
+  if (nt == kSplitTerms && routes > kInlinePlanRoutes && per_expert >= kKtMinTokens)
+    return {mode == kGateUp ? 128 : 64, true};
+  const double want = per_expert * 1.5 * nt;  // term rows
   int rows = 16;
   while (rows < want && rows < 128) rows *= 2;
-  if (rows == 128 && want > 192.0) return mode == kGateUp ? 192 : 96;
-  return rows;
+  if (rows == 128 && want > 192.0) return {mode == kGateUp ? 192 : 96, false};
+  return {rows, false};
 }
 
 cudaError_t launch_moe_bs(const BsLaunch& a, cudaStream_t stream, const char** step) {
@@ -1132,21 +1223,35 @@ cudaError_t launch_moe_bs(const BsLaunch& a, cudaStream_t stream, const char** s
   // All tensor maps are encoded before the first launch, so the host never
   // holds the stream up between kernels.
   *step = "tensor maps";
-  const int bnr1 = bs_tile_rows(R, a.E, kGateUp, NT);
-  const int bnr2 = bs_tile_rows(R, a.E, kDown, NT);
+  const BsTile tile1 = bs_tile(R, a.E, kGateUp, NT);
+  const BsTile tile2 = bs_tile(R, a.E, kDown, NT);
+  // the exchange split (at most kInlinePlanRoutes routes) writes the rows layout
+  if (a.ep && tile1.kt) return cudaErrorInvalidValue;
+  // K layout: NT planes of R rows each (the same workspace as R * NT rows)
+  const uint64_t plane_rows = static_cast<uint64_t>(R > 0 ? R : 1);
+  const int64_t plane1 = tile1.kt ? static_cast<int64_t>(plane_rows) : 0;
+  const int64_t plane2 = tile2.kt ? static_cast<int64_t>(plane_rows) : 0;
+  auto encode_b = [&](CUtensorMap* m, CUtensorMap* ms, const void* q, const void* sf, int k,
+                      const BsTile& t) {
+    if (t.kt)
+      return encode_u8_planes(m, q, k / 2, plane_rows, NT, kRowBytes, t.bnr,
+                              CU_TENSOR_MAP_SWIZZLE_128B) &&
+             encode_u8_planes(ms, sf, k / 16, plane_rows, NT, kRowScales, t.bnr,
+                              CU_TENSOR_MAP_SWIZZLE_NONE);
+    return encode_u8(m, q, k / 2, brows, kRowBytes, t.bnr, CU_TENSOR_MAP_SWIZZLE_128B) &&
+           encode_u8(ms, sf, k / 16, brows, kRowScales, t.bnr, CU_TENSOR_MAP_SWIZZLE_NONE);
+  };
   CUtensorMap m1a, m1sa, m1b, m1sb, m2a, m2sa, m2b, m2sb;
   if (!encode_u8(&m1a, a.w13, a.K / 2, (uint64_t)a.E * 2 * a.I, kRowBytes, kM,
                  CU_TENSOR_MAP_SWIZZLE_128B) ||
       !encode_u8(&m1sa, a.s13, a.K / 16, (uint64_t)a.E * 2 * a.I, kRowScales, kM,
                  CU_TENSOR_MAP_SWIZZLE_NONE) ||
-      !encode_u8(&m1b, a.xq, a.K / 2, brows, kRowBytes, bnr1, CU_TENSOR_MAP_SWIZZLE_128B) ||
-      !encode_u8(&m1sb, a.xsf, a.K / 16, brows, kRowScales, bnr1, CU_TENSOR_MAP_SWIZZLE_NONE) ||
+      !encode_b(&m1b, &m1sb, a.xq, a.xsf, a.K, tile1) ||
       !encode_u8(&m2a, a.w2, a.I / 2, (uint64_t)a.E * a.K, kRowBytes, kM,
                  CU_TENSOR_MAP_SWIZZLE_128B) ||
       !encode_u8(&m2sa, a.s2, a.I / 16, (uint64_t)a.E * a.K, kRowScales, kM,
                  CU_TENSOR_MAP_SWIZZLE_NONE) ||
-      !encode_u8(&m2b, a.hq, a.I / 2, brows, kRowBytes, bnr2, CU_TENSOR_MAP_SWIZZLE_128B) ||
-      !encode_u8(&m2sb, a.hsf, a.I / 16, brows, kRowScales, bnr2, CU_TENSOR_MAP_SWIZZLE_NONE))
+      !encode_b(&m2b, &m2sb, a.hq, a.hsf, a.I, tile2))
     return cudaErrorInvalidValue;
   BsParams p1{};
   p1.counts = a.counts;
@@ -1164,7 +1269,7 @@ cudaError_t launch_moe_bs(const BsLaunch& a, cudaStream_t stream, const char** s
   p1.rows_per_expert = 2 * a.I;
   p1.out_ld = a.I;
   // about one token tile per expert: every weight tile is read once
-  p1.stream_weights = R <= static_cast<int64_t>(a.E) * (bnr1 / NT);
+  p1.stream_weights = R <= static_cast<int64_t>(a.E) * (tile1.kt ? tile1.bnr : tile1.bnr / NT);
   p1.wait_ns = g_wait_ns.load(std::memory_order_relaxed);
   BsParams p2 = p1;
   p2.gscale = w4a4_static ? a.alpha2 : a.g2;
@@ -1175,7 +1280,7 @@ cudaError_t launch_moe_bs(const BsLaunch& a, cudaStream_t stream, const char** s
   p2.k_stages = a.I / kBK;
   p2.rows_per_expert = a.K;
   p2.out_ld = a.K;
-  p2.stream_weights = R <= static_cast<int64_t>(a.E) * (bnr2 / NT);
+  p2.stream_weights = R <= static_cast<int64_t>(a.E) * (tile2.kt ? tile2.bnr : tile2.bnr / NT);
 
   if (a.push.base) {
     // expert parallel: rows go back to their source ranks, unweighted
@@ -1202,22 +1307,23 @@ cudaError_t launch_moe_bs(const BsLaunch& a, cudaStream_t stream, const char** s
     const InlinePlan plan{a.inline_plan ? a.ids : nullptr, a.E, a.counts, a.offsets, a.sorted,
                           a.slot_of, a.status};
     err = launch_split(a.hidden, a.act_dt, &a.hidden_rows, a.slot_of, a.top_k, nullptr, a.M, a.K,
-                       NT, a.xq, a.xsf, a.xg, a.a13_gscale, a.ids, a.sorted, stream, &plan);
+                       NT, a.xq, a.xsf, a.xg, a.a13_gscale, a.ids, a.sorted, stream, &plan,
+                       plane1);
   }
   if (err != cudaSuccess) return err;
   if (a.stage_mark) a.stage_mark(a.stage_ctx, 1);
   // 2. gate/up + SwiGLU
   *step = "gate/up";
-  err = launch_bnr<kGateUp>(bnr1, NT, m1a, m1sa, m1b, m1sb, p1, grid, stream);
+  err = launch_bnr<kGateUp>(tile1, NT, m1a, m1sa, m1b, m1sb, p1, grid, stream);
   if (err != cudaSuccess) return err;
   if (a.stage_mark) a.stage_mark(a.stage_ctx, 2);
   // 3. split the SwiGLU rows, down projection
   *step = "h split";
   err = launch_split(a.h, kF32, nullptr, nullptr, 1, a.offsets + a.E, R, a.I, NT, a.hq, a.hsf,
-                     a.hg, a.a2_gscale, a.ids, a.sorted, stream);
+                     a.hg, a.a2_gscale, a.ids, a.sorted, stream, nullptr, plane2);
   if (err != cudaSuccess) return err;
   *step = "down";
-  err = launch_bnr<kDown>(bnr2, NT, m2a, m2sa, m2b, m2sb, p2, grid, stream);
+  err = launch_bnr<kDown>(tile2, NT, m2a, m2sa, m2b, m2sb, p2, grid, stream);
   if (err != cudaSuccess) return err;
   if (a.stage_mark) a.stage_mark(a.stage_ctx, 3);
   return cudaSuccess;

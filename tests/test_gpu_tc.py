@@ -183,12 +183,16 @@ def _outlier_hidden(oracle, T, K, seed, kind):
     return b
 
 
+@pytest.mark.parametrize("T", [48, 512])
 @pytest.mark.parametrize("kind", ["one1e3", "few1e4", "tiny_blocks"])
-def test_outlier_channels_per_token(sbb, oracle, cuda, kind):
+def test_outlier_channels_per_token(sbb, oracle, cuda, kind, T):
     """W4A16 numerics of the 4-term activation split under outliers and
     blocks far below their row maximum, judged token by token rather than
-    over the batch, at the decode shape's K and I."""
-    E, K, I, T, top_k = 16, 4096, 1280, 48, 4
+    over the batch, at the decode shape's K and I. T = 48 runs the terms as
+    interleaved N rows (decode tiles), T = 512 (128 routes per expert) as
+    planes along K with one global per row (prefill tiles); 48 sampled
+    tokens are checked."""
+    E, K, I, top_k = 16, 4096, 1280, 4
     tensors = random_layer(E, K, I, seed=71, device=cuda)
     ids, w = oracle.route_logits(T, E, top_k, seed=72)
     hidden = _outlier_hidden(oracle, T, K, seed=73, kind=kind)
@@ -197,6 +201,7 @@ def test_outlier_channels_per_token(sbb, oracle, cuda, kind):
     torch.cuda.synchronize()
     assert sbb.nvfp4_moe_device_errors(cuda) == 0
     L = host_layer(oracle, tensors, E, K, I)
-    want = oracle.moe_forward(hidden, ids, w, L)
-    worst = per_token_check(out.cpu().numpy(), want)
-    print(f"{kind}: worst per-token rel {worst[0]:.3e}, cos {worst[1]:.7f}")
+    toks = np.sort(np.random.default_rng(T).choice(T, size=min(48, T), replace=False))
+    want = oracle.moe_forward(hidden, ids, w, L, tokens=toks.astype(np.int32))
+    worst = per_token_check(out.cpu().numpy()[toks], want)
+    print(f"{kind} T={T}: worst per-token rel {worst[0]:.3e}, cos {worst[1]:.7f}")
