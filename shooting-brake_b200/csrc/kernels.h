@@ -126,6 +126,9 @@ cudaError_t launch_quantize(const void* x, int in_dt, const float* gq, int64_t r
 // Block-scaled path (moe_bs.cu): activations split into kSplitTerms NVFP4
 // terms, tcgen05.mma kind::mxf4nvf4 on the packed weights.
 constexpr int kSplitTerms = 4;
+// Bytes after a K-layout scale region: the contiguous scale run of a tile
+// that ends past the last slot (at most 256 slots x 16 bytes) stays inside it.
+constexpr size_t kScaleRunPad = 4096;
 
 struct BsLaunch {
   const void* hidden;

@@ -71,6 +71,13 @@ using namespace ptx;
 constexpr int kBK = 256;              // K elements per pipeline stage
 // Mean routes per expert from which the activation terms go along K.
 constexpr double kKtMinTokens = 96.0;
+// Terms of the K layout. Three residual NVFP4 terms represent a bf16 row to
+// ~8e-4 (normwise; four: ~8e-5), finer than the bf16 rounding of the row
+// itself (~1e-3). At prefill sizes the GEMMs are bound by how many staged
+// bytes each SM keeps in flight, and the term planes are most of them: three
+// planes stage 90 KB per 128-token gate/up step instead of 108 KB and issue a
+// quarter fewer MMAs.
+constexpr int kKtTerms = 3;
 constexpr int kRowBytes = kBK / 2;    // packed bytes per row per stage (128)
 constexpr int kRowScales = kBK / 16;  // scale bytes per row per stage (16)
 constexpr int kM = 128;
@@ -115,6 +122,10 @@ struct BsParams {
   float* const* push_base;
   int64_t push_rows;
   int top_k;
+  // K-layout tiles: the term scales come in as contiguous runs of bsf
+  // ([plane][k stage][slot][16], `plane` rows each)
+  const uint8_t* bsf;
+  int64_t plane;
 };
 
 // BNR: the MMA's N. KT = false: N = BNR term rows (BNR / NT tokens, terms
@@ -338,9 +349,17 @@ __global__ void __launch_bounds__(kThreads, 1)
                              r0 + a * p.a_stride, pol_w);
           }
           if (KT) {
-            // all NT planes of the tile's slots in one box: [plane][slot][bytes]
+            // all NT planes of the tile's slots in one box: [plane][slot][bytes];
+            // their scales are one contiguous run per plane. (The TMA engine
+            // moves a box row at a time, ~2 cycles per row whatever its
+            // width, so 16-byte scale rows cost as much as 128-byte data rows.)
             tma_load_3d_hint(st + C::kOffB, &tmB, &full[s], xa, row_b, 0, pol_x);
-            tma_load_3d_hint(st + C::kOffSB, &tmSB, &full[s], xs, row_b, 0, pol_x);
+#pragma unroll
+            for (int t = 0; t < NT; ++t)
+              bulk_load_hint(st + C::kOffSB + t * BNR * kRowScales,
+                             p.bsf + ((static_cast<int64_t>(t) * p.k_stages + kk) * p.plane +
+                                      row_b) * kRowScales,
+                             BNR * kRowScales, &full[s], pol_x);
           } else {
             tma_load_2d_hint(st + C::kOffB, &tmB, &full[s], xa, row_b, pol_x);
             tma_load_2d_hint(st + C::kOffSB, &tmSB, &full[s], xs, row_b, pol_x);
@@ -720,7 +739,12 @@ __device__ __forceinline__ void split_row_terms(float* v, bool active, int NT, i
       if (d < 0) continue;
       const int64_t orow = plane ? t * plane + d : d * NT + t;
       *reinterpret_cast<uint2*>(q + orow * (K / 2) + blk * 8) = make_uint2(w[0], w[1]);
-      sf[orow * (K / 16) + blk] = s8;
+      // K layout: scales stage-major, [plane][K / 256][slot][16], so a tile's
+      // scales for one stage are one contiguous run
+      const int64_t at = plane ? ((static_cast<int64_t>(t) * (K / 256) + blk / 16) * plane + d) *
+                                         16 + (blk & 15)
+                               : orow * (K / 16) + blk;
+      sf[at] = s8;
     }
     if (!plane) {
       G = __fmul_rn(G, 4.0f);
@@ -1119,17 +1143,17 @@ cudaError_t launch_bnr_nt(int bnr, const CUtensorMap& a, const CUtensorMap& sa,
 }
 
 // nt = 4: bf16/f16/f32 activations as four NVFP4 terms (W4A16 results);
-// nt = 1: activations quantised once (W4A4). kt: term planes run along K
-// (N = bnr tokens), for the four-term split only.
+// nt = 1: activations quantised once (W4A4). kt: kKtTerms term planes run
+// along K (N = bnr tokens), W4A16 at prefill sizes.
 template <int MODE>
 cudaError_t launch_bnr(const BsTile& tile, int nt, const CUtensorMap& a, const CUtensorMap& sa,
                        const CUtensorMap& b, const CUtensorMap& sb, const BsParams& p, int grid,
                        cudaStream_t stream) {
   if (tile.kt) {
-    if (nt != kSplitTerms) return cudaErrorInvalidValue;
+    if (nt != kKtTerms) return cudaErrorInvalidValue;
     switch (tile.bnr) {
-      case 64: return launch_gemm<MODE, 64, kSplitTerms, true>(a, sa, b, sb, p, grid, stream);
-      case 128: return launch_gemm<MODE, 128, kSplitTerms, true>(a, sa, b, sb, p, grid, stream);
+      case 64: return launch_gemm<MODE, 64, kKtTerms, true>(a, sa, b, sb, p, grid, stream);
+      case 128: return launch_gemm<MODE, 128, kKtTerms, true>(a, sa, b, sb, p, grid, stream);
       default: return cudaErrorInvalidValue;
     }
   }
@@ -1227,16 +1251,18 @@ cudaError_t launch_moe_bs(const BsLaunch& a, cudaStream_t stream, const char** s
   const BsTile tile2 = bs_tile(R, a.E, kDown, NT);
   // the exchange split (at most kInlinePlanRoutes routes) writes the rows layout
   if (a.ep && tile1.kt) return cudaErrorInvalidValue;
-  // K layout: NT planes of R rows each (the same workspace as R * NT rows)
+  // K layout: kKtTerms planes of R rows each (inside the workspace's R * NT rows)
   const uint64_t plane_rows = static_cast<uint64_t>(R > 0 ? R : 1);
   const int64_t plane1 = tile1.kt ? static_cast<int64_t>(plane_rows) : 0;
   const int64_t plane2 = tile2.kt ? static_cast<int64_t>(plane_rows) : 0;
+  const int nt1 = tile1.kt ? kKtTerms : NT;
+  const int nt2 = tile2.kt ? kKtTerms : NT;
   auto encode_b = [&](CUtensorMap* m, CUtensorMap* ms, const void* q, const void* sf, int k,
                       const BsTile& t) {
     if (t.kt)
-      return encode_u8_planes(m, q, k / 2, plane_rows, NT, kRowBytes, t.bnr,
+      return encode_u8_planes(m, q, k / 2, plane_rows, kKtTerms, kRowBytes, t.bnr,
                               CU_TENSOR_MAP_SWIZZLE_128B) &&
-             encode_u8_planes(ms, sf, k / 16, plane_rows, NT, kRowScales, t.bnr,
+             encode_u8_planes(ms, sf, k / 16, plane_rows, kKtTerms, kRowScales, t.bnr,
                               CU_TENSOR_MAP_SWIZZLE_NONE);
     return encode_u8(m, q, k / 2, brows, kRowBytes, t.bnr, CU_TENSOR_MAP_SWIZZLE_128B) &&
            encode_u8(ms, sf, k / 16, brows, kRowScales, t.bnr, CU_TENSOR_MAP_SWIZZLE_NONE);
@@ -1271,6 +1297,8 @@ cudaError_t launch_moe_bs(const BsLaunch& a, cudaStream_t stream, const char** s
   // about one token tile per expert: every weight tile is read once
   p1.stream_weights = R <= static_cast<int64_t>(a.E) * (tile1.kt ? tile1.bnr : tile1.bnr / NT);
   p1.wait_ns = g_wait_ns.load(std::memory_order_relaxed);
+  p1.bsf = a.xsf;
+  p1.plane = plane1;
   BsParams p2 = p1;
   p2.gscale = w4a4_static ? a.alpha2 : a.g2;
   p2.bg = a.hg;
@@ -1281,6 +1309,8 @@ cudaError_t launch_moe_bs(const BsLaunch& a, cudaStream_t stream, const char** s
   p2.rows_per_expert = a.K;
   p2.out_ld = a.K;
   p2.stream_weights = R <= static_cast<int64_t>(a.E) * (tile2.kt ? tile2.bnr : tile2.bnr / NT);
+  p2.bsf = a.hsf;
+  p2.plane = plane2;
 
   if (a.push.base) {
     // expert parallel: rows go back to their source ranks, unweighted
@@ -1307,23 +1337,23 @@ cudaError_t launch_moe_bs(const BsLaunch& a, cudaStream_t stream, const char** s
     const InlinePlan plan{a.inline_plan ? a.ids : nullptr, a.E, a.counts, a.offsets, a.sorted,
                           a.slot_of, a.status};
     err = launch_split(a.hidden, a.act_dt, &a.hidden_rows, a.slot_of, a.top_k, nullptr, a.M, a.K,
-                       NT, a.xq, a.xsf, a.xg, a.a13_gscale, a.ids, a.sorted, stream, &plan,
+                       nt1, a.xq, a.xsf, a.xg, a.a13_gscale, a.ids, a.sorted, stream, &plan,
                        plane1);
   }
   if (err != cudaSuccess) return err;
   if (a.stage_mark) a.stage_mark(a.stage_ctx, 1);
   // 2. gate/up + SwiGLU
   *step = "gate/up";
-  err = launch_bnr<kGateUp>(tile1, NT, m1a, m1sa, m1b, m1sb, p1, grid, stream);
+  err = launch_bnr<kGateUp>(tile1, nt1, m1a, m1sa, m1b, m1sb, p1, grid, stream);
   if (err != cudaSuccess) return err;
   if (a.stage_mark) a.stage_mark(a.stage_ctx, 2);
   // 3. split the SwiGLU rows, down projection
   *step = "h split";
-  err = launch_split(a.h, kF32, nullptr, nullptr, 1, a.offsets + a.E, R, a.I, NT, a.hq, a.hsf,
+  err = launch_split(a.h, kF32, nullptr, nullptr, 1, a.offsets + a.E, R, a.I, nt2, a.hq, a.hsf,
                      a.hg, a.a2_gscale, a.ids, a.sorted, stream, nullptr, plane2);
   if (err != cudaSuccess) return err;
   *step = "down";
-  err = launch_bnr<kDown>(tile2, NT, m2a, m2sa, m2b, m2sb, p2, grid, stream);
+  err = launch_bnr<kDown>(tile2, nt2, m2a, m2sa, m2b, m2sb, p2, grid, stream);
   if (err != cudaSuccess) return err;
   if (a.stage_mark) a.stage_mark(a.stage_ctx, 3);
   return cudaSuccess;

@@ -32,10 +32,11 @@ WorkspacePlan plan_workspace(size_t M, size_t E, size_t top_k, size_t K, size_t 
   p.h = take(R * I * sizeof(float));
   const size_t RT = R * kSplitTerms;
   p.xq = take(RT * K / 2);
-  p.xsf = take(RT * K / 16);
+  // + one tile of K-layout scale runs read past the last slot
+  p.xsf = take(RT * K / 16 + kScaleRunPad);
   p.xg = take(RT * sizeof(float));
   p.hq = take(RT * I / 2);
-  p.hsf = take(RT * I / 16);
+  p.hsf = take(RT * I / 16 + kScaleRunPad);
   p.hg = take(RT * sizeof(float));
   p.y = take(R * K * sizeof(float));
   p.total = at;

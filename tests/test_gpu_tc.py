@@ -188,10 +188,11 @@ def _outlier_hidden(oracle, T, K, seed, kind):
 def test_outlier_channels_per_token(sbb, oracle, cuda, kind, T):
     """W4A16 numerics of the 4-term activation split under outliers and
     blocks far below their row maximum, judged token by token rather than
-    over the batch, at the decode shape's K and I. T = 48 runs the terms as
-    interleaved N rows (decode tiles), T = 512 (128 routes per expert) as
-    planes along K with one global per row (prefill tiles); 48 sampled
-    tokens are checked."""
+    over the batch, at the decode shape's K and I. T = 48 runs four terms as
+    interleaved N rows (decode tiles), T = 512 (128 routes per expert) three
+    term planes along K under one global per row (prefill tiles), where a
+    block 2^-14 below its row maximum keeps fewer terms; 48 sampled tokens
+    are checked."""
     E, K, I, top_k = 16, 4096, 1280, 4
     tensors = random_layer(E, K, I, seed=71, device=cuda)
     ids, w = oracle.route_logits(T, E, top_k, seed=72)
