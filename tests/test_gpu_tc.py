@@ -14,37 +14,12 @@ import pytest
 import torch
 
 from conftest import cosine, rel_err
-from gpu_util import dev
+from gpu_util import dev, host_layer, random_layer
 
 pytestmark = pytest.mark.gpu
 
 REL_TOL = 1e-2
 COS_TOL = 0.9999
-
-
-def random_layer(E, K, I, seed, device):
-    g = torch.Generator(device=device)
-    g.manual_seed(seed)
-
-    def plane(rows, cols):
-        q = torch.randint(0, 256, (E, rows, cols // 2), generator=g, device=device,
-                          dtype=torch.int32).to(torch.uint8)
-        ex = torch.randint(4, 11, (E, rows, cols // 16), generator=g, device=device,
-                           dtype=torch.int32)
-        man = torch.randint(0, 8, (E, rows, cols // 16), generator=g, device=device,
-                            dtype=torch.int32)
-        return q, ((ex << 3) | man).to(torch.uint8)
-
-    w13, s13 = plane(2 * I, K)
-    w2, s2 = plane(K, I)
-    g13 = (torch.rand(E, generator=g, device=device) * 0.002 + 0.001).float()
-    g2 = (torch.rand(E, generator=g, device=device) * 0.002 + 0.001).float()
-    return w13, s13, g13, w2, s2, g2
-
-
-def host_layer(oracle, t, E, K, I):
-    w13, s13, g13, w2, s2, g2 = (x.cpu().numpy() for x in t)
-    return oracle.Layer(E, K, I, w13, s13, g13, w2, s2, g2)
 
 
 def run_and_check(sbb, oracle, cuda, E, K, I, ids, w, hidden_bits, tensors, sample=48, seed=0,
