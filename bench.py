@@ -55,6 +55,8 @@ EXPERT_BYTES = 2 * I * D // 2 + 2 * I * D // 16 + D * I // 2 + D * I // 16 + 8
 W13_EXPERT_BYTES = 2 * I * D // 2 + 2 * I * D // 16 + 4
 W2_EXPERT_BYTES = D * I // 2 + D * I // 16 + 4
 METRIC = "routed-expert tokens/s"
+W4A16_DTYPE = ("nvfp4 W4A16: e2m1 weights x e2m1 activation terms (4 interleaved terms at decode "
+               "sizes, 3 term planes along K at prefill sizes), mxf4nvf4 MMA, fp32 accumulate")
 
 
 def parse():
@@ -628,8 +630,7 @@ def run_expert_parallel(args, sbb, rank, world, local):
             "higher_is_better": True, "scaling": "strong", "vs_baseline": None,
             "dtype": ("nvfp4 W4A4: e2m1 weights x e2m1 activations (dynamic per-row globals), "
                       "mxf4nvf4 MMA, fp32 accumulate") if args.w4a4 else
-                     "nvfp4 W4A16: e2m1 weights x 4-term e2m1 activation split, mxf4nvf4 MMA, "
-                     "fp32 accumulate",
+                     W4A16_DTYPE,
             "data": "synthetic",
             "config": ep_config(T, routing, args.w4a4, world),
             "tokens_per_gpu": Tr,
@@ -804,8 +805,7 @@ def run_stack(args, sbb, rank, world, local):
             "higher_is_better": True, "scaling": "strong" if world > 1 else "weak",
             "vs_baseline": None,
             "dtype": "nvfp4 W4A4 (dynamic per-row activation globals)" if args.w4a4 else
-                     "nvfp4 W4A16: e2m1 weights x 4-term e2m1 activation split, mxf4nvf4 MMA, "
-                     "fp32 accumulate",
+                     W4A16_DTYPE,
             "data": "synthetic",
             "config": {"workload": f"config3-stack {Ls} layers E={E} d={D} I={I} top{TOP_K} "
                                    f"T={T} routing={routing}",
@@ -1042,8 +1042,7 @@ def run_single(args, sbb, rank, world, local):
             "higher_is_better": True, "scaling": "weak", "vs_baseline": None,
             "dtype": ("nvfp4 W4A4: e2m1 weights x e2m1 activations (dynamic per-row globals), "
                       "mxf4nvf4 MMA, fp32 accumulate") if args.w4a4 else
-                     "nvfp4 W4A16: e2m1 weights x 4-term e2m1 activation split, mxf4nvf4 MMA, "
-                     "fp32 accumulate",
+                     W4A16_DTYPE,
             "data": "synthetic",
             "config": single_config(T, routing, args.w4a4),
             "tokens_per_gpu": T,

@@ -13,22 +13,22 @@ from pathlib import Path
 ROOT = Path(__file__).resolve().parent.parent
 
 
-def _init(rank: int, world: int, port: int):
+def _init(rank: int, world: int, store_path: str):
+    """gloo process group through a file store at store_path (a fresh path
+    per test): no TCP port to race another process for."""
     sys.path.insert(0, str(ROOT))
     sys.path.insert(0, str(ROOT / "tests"))
-    os.environ["MASTER_ADDR"] = "127.0.0.1"
-    os.environ["MASTER_PORT"] = str(port)
     import torch.distributed as dist
-    dist.init_process_group("gloo", rank=rank, world_size=world,
-                            timeout=datetime.timedelta(seconds=60))
+    dist.init_process_group("gloo", init_method=f"file://{store_path}", rank=rank,
+                            world_size=world, timeout=datetime.timedelta(seconds=60))
     return dist
 
 
-def handles_worker(rank: int, world: int, port: int, q):
+def handles_worker(rank: int, world: int, store: str, q):
     """exchange_handles over gloo: every rank gets all handles in rank order
     (host logic only; the CUDA library is not loaded)."""
     try:
-        dist = _init(rank, world, port)
+        dist = _init(rank, world, store)
         import importlib
         import __graft_entry__ as g
         ep_mod = importlib.import_module(g.load_package().__name__ + ".ep")
@@ -39,10 +39,10 @@ def handles_worker(rank: int, world: int, port: int, q):
         q.put((rank, traceback.format_exc()))
 
 
-def ep_forward_worker(rank: int, world: int, port: int, shape: tuple, steps: list, w4a4: bool, q):
+def ep_forward_worker(rank: int, world: int, store: str, shape: tuple, steps: list, w4a4: bool, q):
     """Expert-parallel forward on GPU `rank` vs the oracle, several steps."""
     try:
-        dist = _init(rank, world, port)
+        dist = _init(rank, world, store)
         import numpy as np
         import torch
         import __graft_entry__ as g
@@ -97,13 +97,13 @@ def ep_forward_worker(rank: int, world: int, port: int, shape: tuple, steps: lis
         q.put((rank, traceback.format_exc()))
 
 
-def ep_skip_worker(rank: int, world: int, port: int, q):
+def ep_skip_worker(rank: int, world: int, store: str, q):
     """One step together, then rank 1 skips a step: rank 0's waits for it
     must give up after their deadline, raise the error bit and return; the
     context stays usable (a host synchronise and a device read follow).
     Rank 1 stays in the group (its memory stays mapped) until rank 0 is done."""
     try:
-        dist = _init(rank, world, port)
+        dist = _init(rank, world, store)
         import time
         import numpy as np
         import torch

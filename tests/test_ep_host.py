@@ -8,7 +8,7 @@ from __future__ import annotations
 
 import importlib
 import multiprocessing as mp
-import socket
+import os
 
 import numpy as np
 import pytest
@@ -16,10 +16,11 @@ import pytest
 from conftest import cosine, rel_err
 
 
-def _free_port() -> int:
-    with socket.socket() as s:
-        s.bind(("127.0.0.1", 0))
-        return s.getsockname()[1]
+def _store_path() -> str:
+    """A fresh file-store path for one group's rendezvous (no TCP port)."""
+    import tempfile
+    d = tempfile.mkdtemp(prefix="sbb200_pg_")
+    return os.path.join(d, "store")
 
 
 @pytest.fixture(scope="module")
@@ -60,8 +61,8 @@ def test_handle_exchange_gloo_world2():
     import ep_worker
     ctx = mp.get_context("spawn")
     q = ctx.Queue()
-    port = _free_port()
-    procs = [ctx.Process(target=ep_worker.handles_worker, args=(r, 2, port, q)) for r in range(2)]
+    store = _store_path()
+    procs = [ctx.Process(target=ep_worker.handles_worker, args=(r, 2, store, q)) for r in range(2)]
     for p in procs:
         p.start()
     got = {}

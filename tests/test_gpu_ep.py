@@ -8,7 +8,7 @@ only; skipped with fewer than two GPUs."""
 from __future__ import annotations
 
 import multiprocessing as mp
-import socket
+import os
 
 import pytest
 import torch
@@ -19,19 +19,20 @@ REL_TOL = 1e-2
 COS_TOL = 0.9999
 
 
-def _free_port() -> int:
-    with socket.socket() as s:
-        s.bind(("127.0.0.1", 0))
-        return s.getsockname()[1]
+def _store_path() -> str:
+    """A fresh file-store path for one group's rendezvous (no TCP port)."""
+    import tempfile
+    d = tempfile.mkdtemp(prefix="sbb200_pg_")
+    return os.path.join(d, "store")
 
 
 def _run(world, shape, steps, w4a4=False):
     import ep_worker
     ctx = mp.get_context("spawn")
     q = ctx.Queue()
-    port = _free_port()
+    store = _store_path()
     procs = [ctx.Process(target=ep_worker.ep_forward_worker,
-                         args=(r, world, port, shape, steps, w4a4, q))
+                         args=(r, world, store, shape, steps, w4a4, q))
              for r in range(world)]
     for p in procs:
         p.start()
@@ -58,7 +59,10 @@ def _steps(world, max_tokens):
 @pytest.mark.parametrize("world", [2, 4, 8])
 @pytest.mark.parametrize("shape,w4a4", [((16, 512, 256, 4, 24), False),
                                         ((34, 1024, 512, 8, 64), False),
-                                        ((34, 1024, 512, 8, 32), True)])
+                                        ((34, 1024, 512, 8, 32), True),
+                                        # more than 1,024 virtual routes with ~100+ per local
+                                        # expert: the publish/gather path and K-layout tiles
+                                        ((16, 1024, 512, 8, 128), False)])
 def test_ep_ranks_match_oracle(cuda, world, shape, w4a4):
     if torch.cuda.device_count() < world:
         pytest.skip(f"needs {world} GPUs")
@@ -86,8 +90,8 @@ def test_wait_gives_up_when_a_rank_skips_a_step(cuda):
     import ep_worker
     ctx = mp.get_context("spawn")
     q = ctx.Queue()
-    port = _free_port()
-    procs = [ctx.Process(target=ep_worker.ep_skip_worker, args=(r, 2, port, q)) for r in range(2)]
+    store = _store_path()
+    procs = [ctx.Process(target=ep_worker.ep_skip_worker, args=(r, 2, store, q)) for r in range(2)]
     for p in procs:
         p.start()
     got = {}
