@@ -126,6 +126,13 @@ struct BsParams {
   // ([plane][k stage][slot][16], `plane` rows each)
   const uint8_t* bsf;
   int64_t plane;
+  // calls whose route plan is computed inside the activation split (at most
+  // kInlinePlanRoutes routes, ids given): the call's route ids. The kernel
+  // then derives the plan's counts and first slots from them itself and
+  // streams its first stages of weights before the previous kernel has
+  // finished (only the term rows wait for it).
+  const int32_t* early_ids;
+  int early_routes;
 };
 
 // BNR: the MMA's N. KT = false: N = BNR term rows (BNR / NT tokens, terms
@@ -276,22 +283,55 @@ __global__ void __launch_bounds__(kThreads, 1)
     tmem_alloc(&tmem_base_s, kTmemCols);
     tmem_relinquish();
   }
-  // everything above is local to the CTA; from here on the kernel reads what
-  // the previous kernel wrote
-  pdl_wait();
-  pdl_trigger();
-  // the wait limit runs from here, so a long predecessor does not eat into it
-  const uint64_t deadline = now_ns() + p.wait_ns;
+  // everything above is local to the CTA. Without early_ids the kernel now
+  // waits for the previous kernel (its results are read from here on); with
+  // them it reads only the call's inputs until each role's own wait below.
+  const bool early = p.early_ids != nullptr;
+  if (!early) {
+    pdl_wait();
+    pdl_trigger();
+  }
   if (warp == 2 || warp == 3) {
-    // every expert's count, first slot and global in one batch of loads
-    // (kMaxExperts / 64 per thread), then warp 2 scans the tile counts
     const int t64 = tid - 64;
-    for (int e = t64; e < p.E; e += 64) {
-      s_cnt[e] = p.counts[e];
-      s_off[e] = p.offsets[e];
-      s_gs[e] = p.gscale[e];
+    if (early) {
+      // the route plan's counts (ids outside [0, E) dropped) and first slots
+      // (exclusive scan), as the activation split computes them
+      for (int e = t64; e < p.E; e += 64) {
+        s_cnt[e] = 0;
+        s_gs[e] = p.gscale[e];
+      }
+      asm volatile("bar.sync 2, 64;" ::: "memory");
+      for (int r = t64; r < p.early_routes; r += 64) {
+        const int32_t e = p.early_ids[r];
+        if (e >= 0 && e < p.E) atomicAdd(&s_cnt[e], 1);
+      }
+      asm volatile("bar.sync 2, 64;" ::: "memory");
+      if (warp == 2) {
+        int carry = 0;
+        for (int e0 = 0; e0 < p.E; e0 += 32) {
+          const int e = e0 + lane;
+          const int v = e < p.E ? s_cnt[e] : 0;
+          int incl = v;
+#pragma unroll
+          for (int d = 1; d < 32; d <<= 1) {
+            const int n = __shfl_up_sync(0xffffffffu, incl, d);
+            if (lane >= d) incl += n;
+          }
+          if (e < p.E) s_off[e] = carry + incl - v;
+          carry += __shfl_sync(0xffffffffu, incl, 31);
+        }
+      }
+    } else {
+      // every expert's count, first slot and global in one batch of loads
+      // (kMaxExperts / 64 per thread)
+      for (int e = t64; e < p.E; e += 64) {
+        s_cnt[e] = p.counts[e];
+        s_off[e] = p.offsets[e];
+        s_gs[e] = p.gscale[e];
+      }
     }
     asm volatile("bar.sync 2, 64;" ::: "memory");
+    // warp 2 scans the tile counts
     if (warp == 2) {
       int carry = 0;
       for (int e0 = 0; e0 < p.E; e0 += 32) {
@@ -313,6 +353,16 @@ __global__ void __launch_bounds__(kThreads, 1)
   tc_fence_after();
   const uint32_t tmem = tmem_base_s;
   const int total_units = prefix[p.E] * p.m_tiles;
+  // early: every role but the producer now waits for the previous kernel
+  // (the producer first issues its first stages of weights)
+  const bool producer = warp == 0 && lane == 0;
+  if (early && !producer) {
+    pdl_wait();
+    pdl_trigger();
+  }
+  // the wait limit runs from the dependency wait, so a long predecessor does
+  // not eat into it (the producer restarts it after its own wait)
+  uint64_t deadline = now_ns() + p.wait_ns;
 
   if (warp == 0) {
     // ---------------- TMA producer ----------------
@@ -326,44 +376,83 @@ __global__ void __launch_bounds__(kThreads, 1)
 #pragma unroll
       for (int i = 0; i < S; ++i) issued[i] = false;
       bool ok = true;
-      for (int u = blockIdx.x; u < total_units && ok; u += gridDim.x) {
+      // the weight half of a stage: packed weight rows and their scales
+      auto load_weights = [&](int st_i, int e, int mt, int kk) {
+        uint8_t* st = smem + st_i * C::kStageBytes;
+        const int r0 = e * p.rows_per_expert + mt * (MODE == kGateUp ? kM : 2 * kM);
+#pragma unroll
+        for (int a = 0; a < C::kNA; ++a) {
+          tma_load_2d_hint(st + a * kM * kRowBytes, &tmA, &full[st_i], kk * kRowBytes,
+                           r0 + a * p.a_stride, pol_w);
+          tma_load_2d_hint(st + C::kOffSA + a * kM * kRowScales, &tmSA, &full[st_i],
+                           kk * kRowScales, r0 + a * p.a_stride, pol_w);
+        }
+      };
+      // the term half of a stage: the activation (or SwiGLU) term rows and
+      // their scales, which the previous kernel wrote
+      auto load_terms = [&](int st_i, int row_b, int kk) {
+        uint8_t* st = smem + st_i * C::kStageBytes;
+        if (KT) {
+          // all NT planes of the tile's slots in one box: [plane][slot][bytes];
+          // their scales are one contiguous run per plane, moved by a plain
+          // bulk copy rather than a box of 16-byte rows
+          tma_load_3d_hint(st + C::kOffB, &tmB, &full[st_i], kk * kRowBytes, row_b, 0, pol_x);
+#pragma unroll
+          for (int t = 0; t < NT; ++t)
+            bulk_load_hint(st + C::kOffSB + t * BNR * kRowScales,
+                           p.bsf + ((static_cast<int64_t>(t) * p.k_stages + kk) * p.plane +
+                                    row_b) * kRowScales,
+                           BNR * kRowScales, &full[st_i], pol_x);
+        } else {
+          tma_load_2d_hint(st + C::kOffB, &tmB, &full[st_i], kk * kRowBytes, row_b, pol_x);
+          tma_load_2d_hint(st + C::kOffSB, &tmSB, &full[st_i], kk * kRowScales, row_b, pol_x);
+        }
+      };
+      // first term row (rows layout) or first slot (KT: the planes' y) of a unit
+      auto term_row = [&](int e, int nt) { return (s_off[e] + nt * C::kTok) * (KT ? 1 : NT); };
+      int u0 = blockIdx.x, kk0 = 0;  // where the main loop starts
+      if (early) {
+        // the first stages' weights before the dependency wait (the ring is
+        // still empty, so nothing to wait for), their term rows after it
+        int n_early = 0, eu[S], ekk[S];
+        while (n_early < S && u0 < total_units) {
+          int e, nt, mt;
+          decode_unit(u0, p.m_tiles, prefix, p.E, e, nt, mt);
+          mbar_expect_tx(&full[n_early], C::kA + C::kB + C::kSA + C::kSB);
+          load_weights(n_early, e, mt, kk0);
+          issued[n_early] = true;
+          issued_phase[n_early] = 0;
+          eu[n_early] = u0;
+          ekk[n_early] = kk0;
+          ++n_early;
+          if (++kk0 == p.k_stages) {
+            kk0 = 0;
+            u0 += gridDim.x;
+          }
+        }
+        pdl_wait();
+        pdl_trigger();
+        deadline = now_ns() + p.wait_ns;
+        for (int i = 0; i < n_early; ++i) {
+          int e, nt, mt;
+          decode_unit(eu[i], p.m_tiles, prefix, p.E, e, nt, mt);
+          load_terms(i, term_row(e, nt), ekk[i]);
+        }
+        s = n_early % S;
+        ph = n_early == S ? 1u : 0u;
+      }
+      for (int u = u0; u < total_units && ok; u += gridDim.x) {
         int e, nt, mt;
         decode_unit(u, p.m_tiles, prefix, p.E, e, nt, mt);
-        // first term row (rows layout) or first slot (KT: the planes' y)
-        const int row_b = (s_off[e] + nt * C::kTok) * (KT ? 1 : NT);
-        const int r0 = e * p.rows_per_expert + mt * (MODE == kGateUp ? kM : 2 * kM);
-        for (int kk = 0; kk < p.k_stages; ++kk) {
+        const int row_b = term_row(e, nt);
+        for (int kk = (u == u0 ? kk0 : 0); kk < p.k_stages; ++kk) {
           if (!mbar_wait(&empty[s], ph ^ 1u, abort, deadline)) {
             ok = false;
             break;
           }
-          uint8_t* st = smem + s * C::kStageBytes;
           mbar_expect_tx(&full[s], C::kA + C::kB + C::kSA + C::kSB);
-          const int xa = kk * kRowBytes;
-          const int xs = kk * kRowScales;
-#pragma unroll
-          for (int a = 0; a < C::kNA; ++a) {
-            tma_load_2d_hint(st + a * kM * kRowBytes, &tmA, &full[s], xa, r0 + a * p.a_stride,
-                             pol_w);
-            tma_load_2d_hint(st + C::kOffSA + a * kM * kRowScales, &tmSA, &full[s], xs,
-                             r0 + a * p.a_stride, pol_w);
-          }
-          if (KT) {
-            // all NT planes of the tile's slots in one box: [plane][slot][bytes];
-            // their scales are one contiguous run per plane. (The TMA engine
-            // moves a box row at a time, ~2 cycles per row whatever its
-            // width, so 16-byte scale rows cost as much as 128-byte data rows.)
-            tma_load_3d_hint(st + C::kOffB, &tmB, &full[s], xa, row_b, 0, pol_x);
-#pragma unroll
-            for (int t = 0; t < NT; ++t)
-              bulk_load_hint(st + C::kOffSB + t * BNR * kRowScales,
-                             p.bsf + ((static_cast<int64_t>(t) * p.k_stages + kk) * p.plane +
-                                      row_b) * kRowScales,
-                             BNR * kRowScales, &full[s], pol_x);
-          } else {
-            tma_load_2d_hint(st + C::kOffB, &tmB, &full[s], xa, row_b, pol_x);
-            tma_load_2d_hint(st + C::kOffSB, &tmSB, &full[s], xs, row_b, pol_x);
-          }
+          load_weights(s, e, mt, kk);
+          load_terms(s, row_b, kk);
           issued[s] = true;
           issued_phase[s] = ph;
           if (++s == S) {
@@ -1153,6 +1242,7 @@ cudaError_t launch_bnr(const BsTile& tile, int nt, const CUtensorMap& a, const C
     if (nt != kKtTerms) return cudaErrorInvalidValue;
     switch (tile.bnr) {
       case 64: return launch_gemm<MODE, 64, kKtTerms, true>(a, sa, b, sb, p, grid, stream);
+      case 80: return launch_gemm<MODE, 80, kKtTerms, true>(a, sa, b, sb, p, grid, stream);
       case 128: return launch_gemm<MODE, 128, kKtTerms, true>(a, sa, b, sb, p, grid, stream);
       default: return cudaErrorInvalidValue;
     }
@@ -1230,7 +1320,7 @@ bool bs_supported(int K, int I) {
 BsTile bs_tile(int64_t routes, int E, int mode, int nt) {
   const double per_expert = static_cast<double>(routes) / E;
   if (nt == kSplitTerms && routes > kInlinePlanRoutes && per_expert >= kKtMinTokens)
-    return {mode == kGateUp ? 128 : 64, true};
+    return {mode == kGateUp ? 128 : 80, true};
   const double want = per_expert * 1.5 * nt;  // term rows
   int rows = 16;
   while (rows < want && rows < 128) rows *= 2;
@@ -1299,6 +1389,10 @@ cudaError_t launch_moe_bs(const BsLaunch& a, cudaStream_t stream, const char** s
   p1.wait_ns = g_wait_ns.load(std::memory_order_relaxed);
   p1.bsf = a.xsf;
   p1.plane = plane1;
+  // a call whose plan the activation split computes: both GEMMs derive it
+  // from the ids themselves and start streaming weights before the split ends
+  p1.early_ids = (a.inline_plan && !a.ep && !a.hidden_rows.base) ? a.ids : nullptr;
+  p1.early_routes = static_cast<int>(R);
   BsParams p2 = p1;
   p2.gscale = w4a4_static ? a.alpha2 : a.g2;
   p2.bg = a.hg;
