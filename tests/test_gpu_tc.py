@@ -44,7 +44,7 @@ def big_layer(cuda):
     return random_layer(170, 4096, 1280, seed=5, device=cuda)
 
 
-@pytest.mark.parametrize("T", [1, 8, 64, 200])
+@pytest.mark.parametrize("T", [1, 2, 8, 64, 200])
 def test_decode_shapes(sbb, oracle, cuda, big_layer, T):
     ids, w = oracle.route_logits(T, 170, 8, seed=T)
     hidden = oracle.make_hidden(T, 4096, seed=T + 1)

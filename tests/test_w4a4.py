@@ -42,7 +42,8 @@ def test_w4a4_oracle_close_to_w4a16(oracle):
 
 @pytest.mark.gpu
 @pytest.mark.parametrize("mode", ["static", "dynamic"])
-@pytest.mark.parametrize("E,K,I,T,k", [(16, 512, 256, 40, 4), (34, 1024, 512, 96, 8)])
+@pytest.mark.parametrize("E,K,I,T,k", [(16, 512, 256, 40, 4), (34, 1024, 512, 96, 8),
+                                       (16, 1024, 512, 2, 4)])
 def test_w4a4_matches_oracle(sbb, oracle, cuda, mode, E, K, I, T, k):
     import torch
     from gpu_util import dev, layer_to
