@@ -81,6 +81,8 @@ def parse():
                          "expert parallelism")
     ap.add_argument("--layers", type=int, default=4,
                     help="independent layers rotated across steps (>= 2 keeps weights out of L2)")
+    ap.add_argument("--no-stack-extras", dest="stack_extras", action="store_false",
+                    help="skip the config-3 46-layer stack in the default one-GPU run")
     ap.add_argument("--no-extras", action="store_true",
                     help="single GPU: measure the headline workload only")
     ap.add_argument("--min-timed-s", type=float, default=1.0,
@@ -685,22 +687,47 @@ def run_stack(args, sbb, rank, world, local):
 
     import torch
     device = torch.device("cuda", local)
-    T, Ls = args.tokens, args.stack
+    T = args.tokens
     if T % world:
         raise SystemExit(f"--tokens {T} must divide evenly over {world} ranks")
-    Tr = T // world
-    routing = args.routing or default_routing(T)
     ep = None
     if world > 1:
         ep_mod = importlib.import_module(sbb.__name__ + ".ep")
-        ep = ep_mod.ExpertParallel(rank=rank, world=world, device=local, max_tokens=Tr,
+        ep = ep_mod.ExpertParallel(rank=rank, world=world, device=local, max_tokens=T // world,
                                    top_k=TOP_K, E=E, K=D, I=I, w4a4=args.w4a4)
+    layers = stack_layers(device, args.stack, ep)
+    line = measure_stack(args, sbb, rank, world, local, T, layers, ep, args.steps, args.warmup)
+    if ep is not None:
+        ep.close()
+    if rank == 0:
+        print(json.dumps(line), flush=True)
+    if world > 1:
+        import torch.distributed as dist
+        dist.barrier()
+        dist.destroy_process_group()
+
+
+def stack_layers(device, Ls, ep=None):
+    """The Ls independent seeded layers of config 3 (this rank's expert shard
+    of each when expert parallel)."""
+    import torch
     layers = []
     for l in range(Ls):
         lw = make_layers(device, 1, seed=5000 + l)[0]
         layers.append(tuple(ep.local_experts(t).contiguous() for t in lw) if ep else lw)
         del lw
     torch.cuda.empty_cache()
+    return layers
+
+
+def measure_stack(args, sbb, rank, world, local, T, layers, ep, steps, warmup):
+    """One config-3 measurement: every layer of `layers` per step on T
+    tokens. Returns the bench line (rank 0's values)."""
+    import torch
+    device = torch.device("cuda", local)
+    Ls = len(layers)
+    Tr = T // world
+    routing = args.routing or default_routing(T)
     routes, gids = [], []
     for l in range(Ls):
         h, ids, w = make_batch(device, T, seed=7000 + l, routing=routing)
@@ -725,7 +752,7 @@ def run_stack(args, sbb, rank, world, local):
         for l in range(Ls):
             layer(l, hidden, out)
 
-    for _ in range(max(args.warmup, 3)):
+    for _ in range(max(warmup, 3)):
         stack_step()
     torch.cuda.synchronize()
     barrier(world)
@@ -745,9 +772,9 @@ def run_stack(args, sbb, rank, world, local):
         graph.replay()
     run = (lambda _i: graph.replay()) if graph is not None else stack_step
     est = timer.loop_ms(run, 1)
-    repeats = timer.repeats_for(est, args.steps, 0.0, lo=3, hi=3)
+    repeats = timer.repeats_for(est, steps, 0.0, lo=3, hi=3)
     clk = ClockSampler(local).start()
-    ms, spread = timer.run(run, args.steps, repeats)
+    ms, spread = timer.run(run, steps, repeats)
     clk.stop()
 
     # end to end: this rank's hidden rows and every layer's routing in from
@@ -774,7 +801,7 @@ def run_stack(args, sbb, rank, world, local):
         host_out.copy_(o, non_blocking=True)
 
     e2e_step()
-    n_e2e = max(1, args.steps // 2)
+    n_e2e = max(1, steps // 2)
     e2e_ms, _ = timer.run(e2e_step, n_e2e, 1)
     errors = (ep.device_errors() if ep is not None else 0) | sbb.device_errors(device)
     errors = int(reduce_over_ranks(float(errors), world, "max"))
@@ -792,16 +819,13 @@ def run_stack(args, sbb, rank, world, local):
                  "frac": tflops / tf_peak})
     roofline.update({"traffic": None, "kernel": f"whole {Ls}-layer stack per GPU",
                      "peak_source": "measured" if peaks else "fallback"})
-    if ep is not None:
-        per_layer = ep.kernels_per_step()
-        ep.close()
-    else:
-        per_layer = sbb.kernels_per_call(T, E, TOP_K, D, I)
+    per_layer = ep.kernels_per_step() if ep is not None else sbb.kernels_per_call(T, E, TOP_K, D, I)
+    line = None
     if rank == 0:
         line = {
             "metric": METRIC, "value": T / (ms * 1e-3) if errors == 0 else None,
             "unit": "tokens/s", "n_gpus": world,
-            "steps": args.steps, "warmup": args.warmup, "ms_per_step": ms,
+            "steps": steps, "warmup": warmup, "ms_per_step": ms,
             "higher_is_better": True, "scaling": "strong" if world > 1 else "weak",
             "vs_baseline": None,
             "dtype": "nvfp4 W4A4 (dynamic per-row activation globals)" if args.w4a4 else
@@ -820,15 +844,11 @@ def run_stack(args, sbb, rank, world, local):
             "e2e": {"value": T / (e2e_ms * 1e-3), "unit": "tokens/s",
                     "h2d_bytes_per_step": Tr * D * 2 + Ls * Tr * TOP_K * 8,
                     "d2h_bytes_per_step": Tr * D * 2, "ms_per_step": e2e_ms},
-            "gpu_launches": per_layer * Ls * args.steps, "device_errors": errors,
+            "gpu_launches": per_layer * Ls * steps, "device_errors": errors,
             "clocks": clk.summary(),
         }
-        print(json.dumps(line), flush=True)
     del graph
-    if world > 1:
-        import torch.distributed as dist
-        dist.barrier()
-        dist.destroy_process_group()
+    return line
 
 
 # --------------------------------------------------------------------------
@@ -999,6 +1019,12 @@ def run_single(args, sbb, rank, world, local):
     h2d = T * D * 2 + T * TOP_K * 4 + T * TOP_K * 4
     d2h = T * D * 2
 
+    # host copies for the CPU baseline (layer 0, batch 0), taken before the
+    # stack measurement below frees the rotating layers
+    cpu_in = None
+    if rank == 0 and world == 1 and not args.no_cpu_baseline:
+        cpu_in = (layer_to_host(layers[0]), host_batch(head.batches[0]))
+
     # ---- the other single-GPU workloads of the configurations -------------
     workloads = {}
     if not args.no_extras and world == 1 and not args.w4a4 and T == 64 and not args.eager:
@@ -1016,6 +1042,24 @@ def run_single(args, sbb, rank, world, local):
                 "gpu_launches": sbb.kernels_per_call(t, E, TOP_K, D, I) * args.steps}
             del lb
             torch.cuda.empty_cache()
+        # config 3 on one GPU: the 46-layer stack (69 GB of weights), decode
+        # T = 64 and a 32,768-token prefill (three timed steps: 0.5 s each)
+        if args.stack_extras:
+            head.batches = []
+            del head
+            layers.clear()
+            torch.cuda.empty_cache()
+            st_layers = stack_layers(device, 46)
+            for t, st_steps in ((64, args.steps), (32768, 3)):
+                sl = measure_stack(args, sbb, rank, world, local, t, st_layers, None, st_steps,
+                                   3)
+                workloads[sl["config"]["workload"]] = {
+                    k: sl[k] for k in ("value", "unit", "ms_per_step", "steps", "warmup",
+                                       "ms_per_layer", "roofline", "e2e", "clocks",
+                                       "gpu_launches", "device_errors", "weights_gb")}
+                torch.cuda.empty_cache()
+            del st_layers
+            torch.cuda.empty_cache()
     errors = sbb.device_errors(device)
 
     cpu_baseline = None
@@ -1024,10 +1068,10 @@ def run_single(args, sbb, rank, world, local):
             from oracle import nvfp4 as O
             if not O.reference_available():
                 O.build(ref=True)
-            if O.reference_available():
-                hb, hids, hw = host_batch(head.batches[0])
+            if O.reference_available() and cpu_in is not None:
+                hb, hids, hw = cpu_in[1]
                 tps, sample, threads, _, _ = cpu_reference_run(
-                    layer_to_host(layers[0]), hb, hids, hw, args.cpu_seconds)
+                    cpu_in[0], hb, hids, hw, args.cpu_seconds)
                 cpu_baseline = {"value": tps, "unit": "tokens/s", "cores": threads,
                                 "kind": "reference", "sample": sample, "isa": cpu_isa()}
         except Exception as exc:  # the baseline is reported, never required
