@@ -21,6 +21,8 @@ from the reference's code, never from this repository's oracle:
   4..10), single-expert FFN outputs of sb_cpu_expert_forward at M in {1, 3, 16}
   and vLLM dequantize_to_dtype of the planes.
 * quant.npz -- vLLM ref_nvfp4_quant codes and scales of a seeded matrix.
+* w4a4.npz -- a W4A4 routed-expert layer through vLLM's NVFP4 linear
+  emulation (run_nvfp4_emulations), static and dynamic activation globals.
 """
 
 from __future__ import annotations
@@ -136,6 +138,60 @@ def quant() -> None:
                         vals=vals.numpy(), scales=scales.numpy())
 
 
+def w4a4() -> None:
+    """A W4A4 routed-expert layer computed with vLLM's own NVFP4 linear
+    emulation (run_nvfp4_emulations: the activations quantised and
+    dequantised by ref_nvfp4_quant with the given global, the weights by
+    dequantize_to_dtype, an fp32 matmul), SwiGLU in fp32 and the routes summed
+    with their weights: the static per-expert a1/a2_gscale convention and the
+    dynamic per-row one (global 448 * 6 / max|row|)."""
+    import torch
+    from vllm.model_executor.layers.quantization.utils.nvfp4_emulation_utils import (
+        run_nvfp4_emulations,
+    )
+
+    E, K, I, T, top_k = 8, 512, 256, 12, 3
+    L = O.make_layer(E, K, I, seed=41)
+    hidden = O.make_hidden(T, K, seed=42)
+    ids, w = O.route_logits(T, E, top_k, seed=43)
+    ids[2, 1] = -1
+    x = O.bf16_bits_to_f32(hidden)
+    amax = np.float32(np.abs(x).max())
+    a13 = np.full(E, np.float32(2688.0) / amax, np.float32)
+    a2 = np.full(E, np.float32(2688.0) / (amax / np.float32(8.0)), np.float32)
+
+    def emu(rows, G, q, sf, g):
+        return run_nvfp4_emulations(
+            torch.from_numpy(rows), torch.tensor([G], dtype=torch.float32),
+            torch.from_numpy(q), torch.from_numpy(sf).view(torch.float8_e4m3fn),
+            torch.tensor(g, dtype=torch.float32), swizzle=False).numpy()
+
+    def dyn(row):
+        m = np.float32(np.abs(row).max())
+        return np.float32(2688.0) / m if m > 0 else np.float32(1.0)
+
+    outs = {}
+    for mode in ("static", "dynamic"):
+        out = np.zeros((T, K), np.float32)
+        for t in range(T):
+            for k in range(top_k):
+                e = int(ids[t, k])
+                if e < 0 or e >= E:
+                    continue
+                xr = x[t:t + 1]
+                G1 = a13[e] if mode == "static" else dyn(xr)
+                gu = emu(xr, G1, L.w13[e], L.s13[e], L.g13[e])
+                g, u = gu[:, :I], gu[:, I:]
+                h = (g / (np.float32(1.0) + np.exp(-g)) * u).astype(np.float32)
+                G2 = a2[e] if mode == "static" else dyn(h)
+                y = emu(h, G2, L.w2[e], L.s2[e], L.g2[e])
+                out[t] += np.float32(w[t, k]) * y[0]
+        outs[mode] = out
+    np.savez_compressed(HERE / "w4a4.npz", out_static=outs["static"], out_dynamic=outs["dynamic"],
+                        ids=ids, weights=w, a13=a13, a2=a2,
+                        digest=digest(hidden, ids, w) + layer_digest(L))
+
+
 if __name__ == "__main__":
     O.build(ref=True)
     if not O.reference_available():
@@ -145,5 +201,6 @@ if __name__ == "__main__":
     c0()
     expert_planes()
     quant()
+    w4a4()
     for p in sorted(HERE.glob("*.npz")):
         print(p.name, p.stat().st_size)
