@@ -624,8 +624,15 @@ def run_expert_parallel(args, sbb, rank, world, local):
     mean_routes = sum(shard_routes) / world
     launches = ep.kernels_per_step()
     del graphs
+    valid = all_errors == 0 and max_rel <= 1e-2 and min_cos >= 0.9999
+    # the other multi-GPU workloads of the configurations, once the headline
+    # step is known good on every rank
+    workloads = None
+    if valid and not args.no_extras and not args.w4a4 and T == 64:
+        layers.clear()
+        torch.cuda.empty_cache()
+        workloads = ep_extras(args, sbb, ep_mod, rank, world, local)
     if rank == 0:
-        valid = all_errors == 0 and max_rel <= 1e-2 and min_cos >= 0.9999
         line = {
             "metric": METRIC, "value": T / (ms * 1e-3) if valid else None, "unit": "tokens/s",
             "n_gpus": world, "steps": args.steps, "warmup": args.warmup, "ms_per_step": ms,
@@ -660,6 +667,7 @@ def run_expert_parallel(args, sbb, rank, world, local):
                        "max_rel": max_rel, "cos": min_cos, "bar": "max_rel <= 1e-2, cos >= 0.9999"},
             "device_errors": all_errors,
             "clocks": clocks,
+            "workloads": workloads,
         }
         if not valid:
             line["invalid"] = "device error bits set or parity outside the bar; no value reported"
@@ -668,6 +676,111 @@ def run_expert_parallel(args, sbb, rank, world, local):
     import torch.distributed as dist
     dist.barrier()
     dist.destroy_process_group()
+
+
+def ep_extras(args, sbb, ep_mod, rank, world, local):
+    """The expert-parallel runs of configurations 4 and 3 at this world size:
+    the Zipf-routed 4,096-token layer (W4A16 and W4A4) with its per-rank
+    load-imbalance tail, then the 46-layer stack at decode T=64 and prefill
+    T=32,768. Each is a fixed sequence of collective steps on every rank;
+    the first one that fails on any rank (agreed over the ranks) ends the
+    list. Returns {workload: result} (rank 0; None elsewhere)."""
+    import torch
+    device = torch.device("cuda", local)
+    stream = torch.cuda.current_stream(device)
+    timer = StepTimer(stream, world)
+    peaks = load_peaks()
+    tf_peak = float(peaks.get("bf16_tflops_sustained", 1400.0))
+    out = {}
+
+    def agreed(ok: bool) -> bool:
+        return reduce_over_ranks(1.0 if ok else 0.0, world, "min") > 0.5
+
+    # config 4: Zipf(1.2) routing, 4,096 tokens split over the ranks
+    try:
+        Tz = 4096
+        Tzr = Tz // world
+        zl = []
+        for lw in make_layers(device, 2, seed=1000):
+            zl.append(lw)
+        ok = True
+        for w4 in (False, True):
+            epz = ep_mod.ExpertParallel(rank=rank, world=world, device=local, max_tokens=Tzr,
+                                        top_k=TOP_K, E=E, K=D, I=I, w4a4=w4)
+            lay = [tuple(epz.local_experts(t).contiguous() for t in lw) for lw in zl]
+            gb = [make_batch(device, Tz, seed=3000 + Tz + 17 * i, routing="zipf")
+                  for i in range(len(lay))]
+            bat = [tuple(x[rank * Tzr:(rank + 1) * Tzr].contiguous() for x in b) for b in gb]
+            o = torch.empty((Tzr, D), dtype=torch.bfloat16, device=device)
+
+            def zstep(i):
+                h, ids, w = bat[i % len(bat)]
+                epz.forward(h, ids, w, *lay[i % len(lay)], out=o)
+
+            for i in range(3):
+                zstep(i)
+            ms, spread = timer.run(zstep, args.steps, 3)
+            err = int(reduce_over_ranks(float(epz.device_errors() | sbb.device_errors(device)),
+                                        world, "max"))
+            ids_all = [b[1].cpu().numpy() for b in gb]
+            per_rank = []
+            for r in range(world):
+                b0, c = ep_mod.expert_shard(E, world, r)
+                per_rank.append(sum(int(((x >= b0) & (x < b0 + c)).sum()) for x in ids_all)
+                                / len(ids_all))
+            mean_r = sum(per_rank) / world
+            routes = sum(int((x >= 0).sum()) for x in ids_all) / len(ids_all)
+            tfl = 2.0 * routes * 3 * I * D / world / (ms * 1e-3) / 1e12
+            peak = tf_peak * (4.0 if w4 else 1.0)
+            out[workload_name(Tz, "zipf", w4) + f", experts sharded over {world} GPUs"] = {
+                "value": Tz / (ms * 1e-3) if err == 0 else None, "unit": "tokens/s",
+                "ms_per_step": ms, "steps": args.steps, "timing": "eager calls, max over ranks",
+                "loop_spread_ms": spread,
+                "load_imbalance": {"routes_per_rank": per_rank,
+                                   "max_over_mean": max(per_rank) / mean_r if mean_r else None},
+                "roofline": {"bound": "tensor", "achieved": tfl, "peak": peak,
+                             "unit": "TFLOP/s", "frac": tfl / peak,
+                             "kernel": "whole expert-parallel step per GPU",
+                             "peak_source": "measured bf16_tflops_sustained" +
+                                            (" x4 (FP4 rate)" if w4 else "")},
+                "device_errors": err}
+            epz.close()
+            del lay, bat, gb, o
+            torch.cuda.empty_cache()
+            ok = ok and err == 0
+        del zl
+        torch.cuda.empty_cache()
+    except Exception as exc:  # recorded, and the stack below is skipped
+        out["error"] = f"config 4: {type(exc).__name__}: {str(exc)[:160]}"
+        ok = False
+    if not agreed(ok):
+        return out if rank == 0 else None
+
+    # config 3: the 46-layer stack, sharded
+    try:
+        ep_dec = ep_mod.ExpertParallel(rank=rank, world=world, device=local,
+                                       max_tokens=64 // world, top_k=TOP_K, E=E, K=D, I=I)
+        st = stack_layers(device, 46, ep_dec)
+        for t, steps, e in ((64, args.steps, ep_dec), (32768, 3, None)):
+            if e is None:
+                e = ep_mod.ExpertParallel(rank=rank, world=world, device=local,
+                                          max_tokens=t // world, top_k=TOP_K, E=E, K=D, I=I)
+            sl = measure_stack(args, sbb, rank, world, local, t, st, e, steps, 3)
+            if rank == 0:
+                out[sl["config"]["workload"]] = {
+                    k: sl[k] for k in ("value", "unit", "ms_per_step", "steps", "warmup",
+                                       "ms_per_layer", "roofline", "e2e", "clocks",
+                                       "gpu_launches", "device_errors", "weights_gb")}
+            e.close()
+            torch.cuda.empty_cache()
+        del st
+        torch.cuda.empty_cache()
+        ok = True
+    except Exception as exc:
+        out["error"] = f"config 3: {type(exc).__name__}: {str(exc)[:160]}"
+        ok = False
+    agreed(ok)
+    return out if rank == 0 else None
 
 
 # --------------------------------------------------------------------------

@@ -624,8 +624,24 @@ __global__ void __launch_bounds__(kThreads, 1)
         uint32_t t0[16], t1[16];
         tmem_ld16(taddr + c0, t0);
         tmem_ld16(taddr + BNR + c0, t1);
-        tmem_wait_ld();
         constexpr int kTokPerChunk = KT ? 16 : 16 / NT;
+        // expert parallel: lane l finds the source row of the chunk's token l
+        // once (route r = v * top_k + k of virtual token v = src * rows + t
+        // goes to row t * top_k + k of the source's buffer); the other lanes
+        // take it by shuffle
+        float* push_row = nullptr;
+        if (MODE == kDown && p.push_base) {
+          const int jl = (KT ? c0 : c0 / NT) + lane;
+          if (lane < kTokPerChunk && jl < valid) {
+            const int32_t rv = p.sorted[slot0 + jl];
+            const int32_t v = rv / p.top_k;
+            const int32_t src = v / static_cast<int32_t>(p.push_rows);
+            push_row = p.push_base[src] +
+                       (static_cast<int64_t>(v - src * static_cast<int32_t>(p.push_rows)) *
+                            p.top_k + (rv - v * p.top_k)) * p.out_ld;
+          }
+        }
+        tmem_wait_ld();
 #pragma unroll
         for (int jj = 0; jj < kTokPerChunk; ++jj) {
           const int j = KT ? c0 + jj : c0 / NT + jj;  // token within the tile
@@ -647,13 +663,8 @@ __global__ void __launch_bounds__(kThreads, 1)
             }
             float* orow = p.out + static_cast<int64_t>(slot) * p.out_ld;
             if (MODE == kDown && p.push_base) {
-              // route r = v * top_k + k of virtual token v = src * rows + t:
-              // row (t * top_k + k) of the source's partial buffer
-              const int32_t rv = p.sorted[slot];
-              const int64_t v = rv / p.top_k;
-              const int64_t src = v / p.push_rows;
-              orow = p.push_base[src] +
-                     ((v - src * p.push_rows) * p.top_k + (rv - v * p.top_k)) * p.out_ld;
+              orow = reinterpret_cast<float*>(__shfl_sync(
+                  0xffffffffu, reinterpret_cast<unsigned long long>(push_row), jj));
             }
             if (MODE == kGateUp) {
               const float gv = v0 * gs, uv = v1 * gs;
