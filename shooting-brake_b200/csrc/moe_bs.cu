@@ -78,6 +78,10 @@ constexpr double kKtMinTokens = 96.0;
 // planes stage 90 KB per 128-token gate/up step instead of 108 KB and issue a
 // quarter fewer MMAs.
 constexpr int kKtTerms = 3;
+// Threads (warps 2-3) that copy the second weight block of every stage with
+// cp.async when the weights are L2-resident (prefill-sized calls): the
+// load/store path adds a second queue of requests in flight to the TMA's.
+constexpr int kLsuThreads = 64;
 constexpr int kRowBytes = kBK / 2;    // packed bytes per row per stage (128)
 constexpr int kRowScales = kBK / 16;  // scale bytes per row per stage (16)
 constexpr int kM = 128;
@@ -133,6 +137,15 @@ struct BsParams {
   // finished (only the term rows wait for it).
   const int32_t* early_ids;
   int early_routes;
+  // the weight plane (w13 or w2) and its row length in bytes. With lsu_half
+  // the second 128-row weight block of each stage is copied by warps 2-3
+  // with cp.async (the load/store path), the rest by TMA: for tiles whose
+  // weights are shared by several token tiles (L2-resident), where one
+  // SM's TMA requests in flight bound the fill rate; streamed weights (decode)
+  // come faster through TMA alone.
+  const uint8_t* wa;
+  int64_t wa_ld;
+  int lsu_half;
 };
 
 // BNR: the MMA's N. KT = false: N = BNR term rows (BNR / NT tokens, terms
@@ -258,7 +271,7 @@ __global__ void __launch_bounds__(kThreads, 1)
 
   if (tid == 0) {
     for (int i = 0; i < S; ++i) {
-      mbar_init(&full[i], 1);
+      mbar_init(&full[i], 1 + (p.lsu_half ? kLsuThreads : 0));  // TMA + the cp.async threads
       mbar_init(&empty[i], 1 + 4);  // MMA commit + the four scale warps
     }
     for (int i = 0; i < NSF; ++i) {
@@ -355,7 +368,7 @@ __global__ void __launch_bounds__(kThreads, 1)
   const int total_units = prefix[p.E] * p.m_tiles;
   // early: every role but the producer now waits for the previous kernel
   // (the producer first issues its first stages of weights)
-  const bool producer = warp == 0 && lane == 0;
+  const bool producer = (warp == 0 && lane == 0) || (p.lsu_half && (warp == 2 || warp == 3));
   if (early && !producer) {
     pdl_wait();
     pdl_trigger();
@@ -382,8 +395,9 @@ __global__ void __launch_bounds__(kThreads, 1)
         const int r0 = e * p.rows_per_expert + mt * (MODE == kGateUp ? kM : 2 * kM);
 #pragma unroll
         for (int a = 0; a < C::kNA; ++a) {
-          tma_load_2d_hint(st + a * kM * kRowBytes, &tmA, &full[st_i], kk * kRowBytes,
-                           r0 + a * p.a_stride, pol_w);
+          if (a == 0 || !p.lsu_half)  // with lsu_half warps 2-3 bring the second block
+            tma_load_2d_hint(st + a * kM * kRowBytes, &tmA, &full[st_i], kk * kRowBytes,
+                             r0 + a * p.a_stride, pol_w);
           tma_load_2d_hint(st + C::kOffSA + a * kM * kRowScales, &tmSA, &full[st_i],
                            kk * kRowScales, r0 + a * p.a_stride, pol_w);
         }
@@ -418,7 +432,7 @@ __global__ void __launch_bounds__(kThreads, 1)
         while (n_early < S && u0 < total_units) {
           int e, nt, mt;
           decode_unit(u0, p.m_tiles, prefix, p.E, e, nt, mt);
-          mbar_expect_tx(&full[n_early], C::kA + C::kB + C::kSA + C::kSB);
+          mbar_expect_tx(&full[n_early], C::kA - (p.lsu_half ? kM * kRowBytes : 0) + C::kB + C::kSA + C::kSB);
           load_weights(n_early, e, mt, kk0);
           issued[n_early] = true;
           issued_phase[n_early] = 0;
@@ -450,7 +464,7 @@ __global__ void __launch_bounds__(kThreads, 1)
             ok = false;
             break;
           }
-          mbar_expect_tx(&full[s], C::kA + C::kB + C::kSA + C::kSB);
+          mbar_expect_tx(&full[s], C::kA - (p.lsu_half ? kM * kRowBytes : 0) + C::kB + C::kSA + C::kSB);
           load_weights(s, e, mt, kk);
           load_terms(s, row_b, kk);
           issued[s] = true;
@@ -468,6 +482,61 @@ __global__ void __launch_bounds__(kThreads, 1)
         }
       }
     }
+  } else if (p.lsu_half && (warp == 2 || warp == 3)) {
+    // ---------------- second weight block by cp.async ----------------
+    const int lt = tid - 64;
+    auto issue = [&](int st_i, int e, int mt, int kk) {
+      uint8_t* dst = smem + st_i * C::kStageBytes + kM * kRowBytes;
+      const int64_t r0 = static_cast<int64_t>(e) * p.rows_per_expert +
+                         mt * (MODE == kGateUp ? kM : 2 * kM) + p.a_stride;
+      const uint8_t* src = p.wa + r0 * p.wa_ld + kk * kRowBytes;
+      // 128 rows x 8 chunks of 16 bytes, in the 128-byte swizzle the MMA's
+      // descriptor expects (chunk c of row r at c ^ (r % 8))
+#pragma unroll 4
+      for (int i = lt; i < kM * 8; i += kLsuThreads) {
+        const int r = i >> 3, c = i & 7;
+        cp_async16(dst + r * kRowBytes + ((c ^ (r & 7)) << 4), src + r * p.wa_ld + c * 16);
+      }
+      cp_async_arrive(&full[st_i]);
+    };
+    int s = 0;
+    uint32_t ph = 0;
+    bool ok = true;
+    int u0 = blockIdx.x, kk0 = 0;
+    if (early) {
+      int n_early = 0;
+      while (n_early < S && u0 < total_units) {
+        int e, nt, mt;
+        decode_unit(u0, p.m_tiles, prefix, p.E, e, nt, mt);
+        issue(n_early, e, mt, kk0);
+        ++n_early;
+        if (++kk0 == p.k_stages) {
+          kk0 = 0;
+          u0 += gridDim.x;
+        }
+      }
+      pdl_wait();
+      pdl_trigger();
+      deadline = now_ns() + p.wait_ns;
+      s = n_early % S;
+      ph = n_early == S ? 1u : 0u;
+    }
+    for (int u = u0; u < total_units && ok; u += gridDim.x) {
+      int e, nt, mt;
+      decode_unit(u, p.m_tiles, prefix, p.E, e, nt, mt);
+      for (int kk = (u == u0 ? kk0 : 0); kk < p.k_stages; ++kk) {
+        if (!warp_wait(&empty[s], ph ^ 1u, abort, deadline)) {
+          ok = false;
+          break;
+        }
+        issue(s, e, mt, kk);
+        if (++s == S) {
+          s = 0;
+          ph ^= 1u;
+        }
+      }
+    }
+    cp_async_wait_all();
   } else if (warp == 1) {
     // ---------------- scale copies + MMA issuer ----------------
     if (lane == 0) {
@@ -1403,6 +1472,9 @@ cudaError_t launch_moe_bs(const BsLaunch& a, cudaStream_t stream, const char** s
   // a call whose plan the activation split computes: both GEMMs derive it
   // from the ids themselves and start streaming weights before the split ends
   p1.early_ids = (a.inline_plan && !a.ep && !a.hidden_rows.base) ? a.ids : nullptr;
+  p1.wa = a.w13;
+  p1.wa_ld = a.K / 2;
+  p1.lsu_half = !p1.stream_weights;
   p1.early_routes = static_cast<int>(R);
   BsParams p2 = p1;
   p2.gscale = w4a4_static ? a.alpha2 : a.g2;
@@ -1416,6 +1488,9 @@ cudaError_t launch_moe_bs(const BsLaunch& a, cudaStream_t stream, const char** s
   p2.stream_weights = R <= static_cast<int64_t>(a.E) * (tile2.kt ? tile2.bnr : tile2.bnr / NT);
   p2.bsf = a.hsf;
   p2.plane = plane2;
+  p2.wa = a.w2;
+  p2.wa_ld = a.I / 2;
+  p2.lsu_half = !p2.stream_weights;
 
   if (a.push.base) {
     // expert parallel: rows go back to their source ranks, unweighted
