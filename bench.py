@@ -354,7 +354,7 @@ class StepTimer:
         self.stream = stream
         self.world = world
 
-    def loop_ms(self, run_one, steps):
+    def loop_ms(self, run_one, steps, finish=None):
         import torch
         torch.cuda.synchronize()
         barrier(self.world)
@@ -365,6 +365,8 @@ class StepTimer:
         ev0.record(self.stream)
         for i in range(steps):
             run_one(i + 1)
+        if finish is not None:  # work on other streams the steps left in flight
+            finish()
         ev1.record(self.stream)
         torch.cuda.synchronize()
         return ev0.elapsed_time(ev1) / steps
@@ -373,11 +375,74 @@ class StepTimer:
         n = math.ceil(seconds * 1e3 / max(est_ms * steps, 1e-3)) if seconds > 0 else lo
         return int(max_over_ranks(float(min(hi, max(lo, n))), self.world))
 
-    def run(self, run_one, steps, repeats):
-        per = [self.loop_ms(run_one, steps) for _ in range(repeats)]
+    def run(self, run_one, steps, repeats, finish=None):
+        per = [self.loop_ms(run_one, steps, finish) for _ in range(repeats)]
         med = statistics.median(per)
         return max_over_ranks(med, self.world), {"repeats": repeats, "min_ms": min(per),
                                                  "max_ms": max(per)}
+
+
+class CopyPipeline:
+    """End-to-end steps as a serving loop runs them: step i's inputs go up
+    from pinned host memory on one copy stream while step i-1's kernels run,
+    and its result comes back to pinned host memory on a second copy stream
+    while step i+1's kernels run. Device inputs are double-buffered (a buffer
+    is refilled once the step that read it has finished). Every step's bytes
+    still cross PCIe; `finish` makes the compute stream wait for the last
+    read-back, so a timed region closed after it contains it.
+
+    host_in: list of tuples of pinned tensors (one tuple per step, cycled);
+    compute(i, device_inputs) -> the step's device result (bf16, out_shape)."""
+
+    DESCRIPTION = ("per step: inputs copied up from pinned host memory on one copy stream while "
+                   "the previous step's kernels run, result copied back to pinned host memory on "
+                   "a second copy stream while the next step's run (double-buffered device "
+                   "inputs); the timed region ends after the last read-back")
+
+    def __init__(self, device, host_in, out_shape, compute):
+        import torch
+        self.comp = torch.cuda.current_stream(device)
+        self.cs_in = torch.cuda.Stream(device)
+        self.cs_out = torch.cuda.Stream(device)
+        self.host_in = host_in
+        self.dev = [tuple(torch.empty(x.shape, dtype=x.dtype, device=device) for x in host_in[0])
+                    for _ in range(2)]
+        self.ready = [torch.cuda.Event() for _ in range(2)]
+        self.free = [None, None]
+        self.host_out = torch.empty(out_shape, dtype=torch.bfloat16).pin_memory()
+        self.compute = compute
+        self.last = None
+
+    def step(self, i):
+        import torch
+        b = i % 2
+        dev = self.dev[b]
+        with torch.cuda.stream(self.cs_in):
+            if self.free[b] is not None:
+                self.cs_in.wait_event(self.free[b])
+            for d, h in zip(dev, self.host_in[i % len(self.host_in)]):
+                d.copy_(h, non_blocking=True)
+            self.ready[b].record(self.cs_in)
+        self.comp.wait_event(self.ready[b])
+        o = self.compute(i, dev)
+        done = torch.cuda.Event()
+        done.record(self.comp)
+        self.free[b] = done
+        with torch.cuda.stream(self.cs_out):
+            self.cs_out.wait_event(done)
+            self.host_out.copy_(o, non_blocking=True)
+            o.record_stream(self.cs_out)
+            back = torch.cuda.Event()
+            back.record(self.cs_out)
+        self.last = back
+
+    def finish(self):
+        if self.last is not None:
+            self.comp.wait_event(self.last)
+
+    def bytes_per_step(self):
+        up = sum(x.numel() * x.element_size() for x in self.host_in[0])
+        return up, self.host_out.numel() * self.host_out.element_size()
 
 
 # --------------------------------------------------------------------------
@@ -573,20 +638,12 @@ def run_expert_parallel(args, sbb, rank, world, local):
     # end to end: this rank's tokens from pinned host memory, result back
     host_in = [(h.cpu().pin_memory(), ids.cpu().pin_memory(), w.cpu().pin_memory())
                for (h, ids, w) in batches]
-    host_out = torch.empty((Tr, D), dtype=torch.bfloat16).pin_memory()
-    dh, di, dw = (torch.empty_like(x) for x in batches[0])
-
-    def e2e_step(i):
-        hh, hi, hw = host_in[i % N_LAYERS]
-        dh.copy_(hh, non_blocking=True)
-        di.copy_(hi, non_blocking=True)
-        dw.copy_(hw, non_blocking=True)
-        o = ep.forward(dh, di, dw, *layers[i % N_LAYERS], out_dtype=torch.bfloat16)
-        host_out.copy_(o, non_blocking=True)
-
+    pipe = CopyPipeline(device, host_in, (Tr, D),
+                        lambda i, x: ep.forward(*x, *layers[i % N_LAYERS],
+                                                out_dtype=torch.bfloat16))
     for i in range(max(args.warmup, 3)):
-        e2e_step(i)
-    e2e_ms, _ = timer.run(e2e_step, args.steps, 3)
+        pipe.step(i)
+    e2e_ms, _ = timer.run(pipe.step, args.steps, 3, finish=pipe.finish)
     errors = ep.device_errors() | sbb.device_errors(device)
 
     # parity: one eager step (layer 0, batch 0) against the single-GPU path
@@ -658,7 +715,8 @@ def run_expert_parallel(args, sbb, rank, world, local):
             "cpu_baseline": None,
             "e2e": {"value": T / (e2e_ms * 1e-3), "unit": "tokens/s",
                     "h2d_bytes_per_step": Tr * D * 2 + Tr * TOP_K * 8,
-                    "d2h_bytes_per_step": Tr * D * 2, "ms_per_step": e2e_ms},
+                    "d2h_bytes_per_step": Tr * D * 2, "ms_per_step": e2e_ms,
+                    "copies": CopyPipeline.DESCRIPTION},
             "gpu_launches": launches * args.steps,
             "load_imbalance": {"routes_per_rank": shard_routes,
                                "max_over_mean": max(shard_routes) / mean_routes if mean_routes else None},
@@ -956,7 +1014,8 @@ def measure_stack(args, sbb, rank, world, local, T, layers, ep, steps, warmup):
             "roofline": roofline, "cpu_baseline": None,
             "e2e": {"value": T / (e2e_ms * 1e-3), "unit": "tokens/s",
                     "h2d_bytes_per_step": Tr * D * 2 + Ls * Tr * TOP_K * 8,
-                    "d2h_bytes_per_step": Tr * D * 2, "ms_per_step": e2e_ms},
+                    "d2h_bytes_per_step": Tr * D * 2, "ms_per_step": e2e_ms,
+                    "copies": "serial, on the compute stream before and after the stack step"},
             "gpu_launches": per_layer * Ls * steps, "device_errors": errors,
             "clocks": clk.summary(),
         }
@@ -1113,24 +1172,12 @@ def run_single(args, sbb, rank, world, local):
     # ---- end-to-end through the public op with host buffers ---------------
     host_in = [(h.cpu().pin_memory(), ids.cpu().pin_memory(), w.cpu().pin_memory())
                for (h, ids, w) in head.batches]
-    host_out = torch.empty((T, D), dtype=torch.bfloat16).pin_memory()
-    dh = torch.empty_like(head.batches[0][0])
-    di = torch.empty_like(head.batches[0][1])
-    dw = torch.empty_like(head.batches[0][2])
-
-    def e2e_step(i):
-        hh, hi, hw = host_in[i % N_LAYERS]
-        dh.copy_(hh, non_blocking=True)
-        di.copy_(hi, non_blocking=True)
-        dw.copy_(hw, non_blocking=True)
-        o = head.forward(dh, di, dw, layers[i % N_LAYERS])
-        host_out.copy_(o, non_blocking=True)
-
+    pipe = CopyPipeline(device, host_in, (T, D),
+                        lambda i, x: head.forward(*x, layers[i % N_LAYERS]))
     for i in range(max(args.warmup, 3)):
-        e2e_step(i)
-    e2e_ms, _ = head.timer.run(e2e_step, args.steps, 3)
-    h2d = T * D * 2 + T * TOP_K * 4 + T * TOP_K * 4
-    d2h = T * D * 2
+        pipe.step(i)
+    e2e_ms, _ = head.timer.run(pipe.step, args.steps, 3, finish=pipe.finish)
+    h2d, d2h = pipe.bytes_per_step()
 
     # host copies for the CPU baseline (layer 0, batch 0), taken before the
     # stack measurement below frees the rotating layers
@@ -1215,7 +1262,7 @@ def run_single(args, sbb, rank, world, local):
             "cpu_baseline": cpu_baseline,
             "e2e": {"value": world * T / (e2e_ms * 1e-3), "unit": "tokens/s",
                     "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": d2h,
-                    "ms_per_step": e2e_ms},
+                    "ms_per_step": e2e_ms, "copies": CopyPipeline.DESCRIPTION},
             "gpu_launches": launches_per_step * args.steps,
             "device_errors": errors,
             "clocks": clocks,
