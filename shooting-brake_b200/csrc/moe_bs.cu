@@ -139,7 +139,7 @@ struct BsParams {
   int early_routes;
   // the weight plane (w13 or w2) and its row length in bytes. With lsu_half
   // the second 128-row weight block of each stage is copied by warps 2-3
-  // with cp.async (the load/store path), the rest by TMA: for tiles whose
+  // with cp.async (the load/store path), the rest by TMA: for down tiles whose
   // weights are shared by several token tiles (L2-resident), where one
   // SM's TMA requests in flight bound the fill rate; streamed weights (decode)
   // come faster through TMA alone.
@@ -1474,7 +1474,9 @@ cudaError_t launch_moe_bs(const BsLaunch& a, cudaStream_t stream, const char** s
   p1.early_ids = (a.inline_plan && !a.ep && !a.hidden_rows.base) ? a.ids : nullptr;
   p1.wa = a.w13;
   p1.wa_ld = a.K / 2;
-  p1.lsu_half = !p1.stream_weights;
+  // gate/up tiles keep the TMA alone: with the split, their prefill launches
+  // measured 2.5 % slower (1.418 against 1.383 ms, T = 8192, same clocks)
+  p1.lsu_half = false;
   p1.early_routes = static_cast<int>(R);
   BsParams p2 = p1;
   p2.gscale = w4a4_static ? a.alpha2 : a.g2;
