@@ -688,7 +688,10 @@ def run_expert_parallel(args, sbb, rank, world, local):
     if valid and not args.no_extras and not args.w4a4 and T == 64:
         layers.clear()
         torch.cuda.empty_cache()
-        workloads = ep_extras(args, sbb, ep_mod, rank, world, local)
+        try:  # the headline line is printed whatever happens to the extras
+            workloads = ep_extras(args, sbb, ep_mod, rank, world, local)
+        except Exception as exc:
+            workloads = {"error": f"{type(exc).__name__}: {str(exc)[:160]}"}
     if rank == 0:
         line = {
             "metric": METRIC, "value": T / (ms * 1e-3) if valid else None, "unit": "tokens/s",
