@@ -306,6 +306,10 @@ class ClockSampler:
 
     def stop(self):
         if self.proc is not None:
+            # a region shorter than the 50 ms period may have no sample yet:
+            # take the one that follows it rather than none
+            import select
+            select.select([self.proc.stdout], [], [], 0.5)
             self.proc.terminate()
             try:
                 out, _ = self.proc.communicate(timeout=5)
