@@ -38,6 +38,10 @@
 //   warp 0       TMA: packed weights (128-byte swizzle), their linear scale
 //                rows, the packed term rows and their scale rows.
 //   warp 1       TMEM allocation; one thread issues the MMAs.
+//   warps 2-3    down tiles of prefill-sized calls only: the second 128-row
+//                weight block of each stage by cp.async, a second queue of
+//                requests beside the TMA (decode calls, with inline plans:
+//                the route histogram in the prologue).
 //   warps 4-7    scale warps: write the stage's e4m3 scales into tensor
 //                memory with tcgen05.st in the layout the block-scaled MMA
 //                reads: for a 128-row operand block and a 64-wide K group the
