@@ -1,7 +1,7 @@
 """Routing extremes on the B200 against the oracle: every route on one expert
 (one expert's token tiles carry the whole call, through the route plan inside
 the activation split and through the separate plan kernels, in both term
-layouts), a call whose routes are all invalid, and top_k = E.
+layouts, W4A16 and W4A4), a call whose routes are all invalid, and top_k = E.
 
 Tolerance as in the other parity tests: max|got - want| / max|want| <= 1e-2
 and cosine >= 0.9999 against the fp32-accumulated oracle."""
@@ -70,3 +70,21 @@ def test_top_k_equals_experts(sbb, oracle, cuda):
     w = np.full((T, E), 1.0 / E, np.float32)
     got = run_moe(sbb, hidden, ids, w, L, cuda)
     check(got, oracle.moe_forward(hidden, ids, w, L))
+
+
+@pytest.mark.parametrize("mode", ["static", "dynamic"])
+@pytest.mark.parametrize("T", [128, 512])
+def test_w4a4_every_route_on_one_expert(sbb, oracle, cuda, mode, T):
+    from test_w4a4 import _static_scales
+    E, K, I, top_k = 16, 1024, 512, 4
+    L = oracle.make_layer(E, K, I, seed=101 + T)
+    hidden = oracle.make_hidden(T, K, seed=102 + T)
+    ids = np.full((T, top_k), 11, np.int32)
+    w = np.random.default_rng(103).random((T, top_k), dtype=np.float32) / top_k
+    scales = _static_scales(oracle, L, hidden, E) if mode == "static" else (None,) * 4
+    want = oracle.moe_forward_w4a4(hidden, ids, w, L, *scales)
+    ts = [None if s is None else torch.from_numpy(s).to(cuda) for s in scales]
+    got = sbb.nvfp4_moe_w4a4(dev(hidden, cuda, torch.bfloat16), dev(ids, cuda), dev(w, cuda),
+                             *layer_to(L, cuda), *ts)
+    torch.cuda.synchronize()
+    check(got.cpu().numpy(), want)
