@@ -1,8 +1,9 @@
 """Generate tests/golden/bank_small.bin (an SBEXP001 expert bank) and
 bank_small_expect.npz with the REFERENCE's own bank writer and reader.
 
-Run where the reference tree exists (its location is the SB_REFERENCE
-environment variable, default the sibling checkout the oracle Makefile uses):
+Run where the reference tree exists (found like the oracle's build finds it:
+the SBB200_REFERENCE_DIR environment variable, else a directory named
+``reference`` beside this repository):
 
     python tests/golden/make_bank.py
 
@@ -18,7 +19,6 @@ pins the library's reader to the reference's format on both sides.
 from __future__ import annotations
 
 import importlib.util
-import os
 import sys
 from pathlib import Path
 
@@ -43,7 +43,9 @@ def _load(path: Path, name: str):
 
 
 def main() -> None:
-    ref = Path(os.environ.get("SB_REFERENCE", "/root/reference"))
+    ref = O.reference_dir()
+    if ref is None:
+        raise SystemExit("reference tree not found: set SBB200_REFERENCE_DIR")
     writer = _load(ref / "src/phase1/extract_experts.py", "sb_ref_extract_experts")
     pkg = ref / "src/phase4/src"
     sys.path.insert(0, str(pkg))
