@@ -1185,6 +1185,18 @@ def run_single(args, sbb, rank, world, local):
         pipe.step(i)
     e2e_ms, _ = head.timer.run(pipe.step, args.steps, 3, finish=pipe.finish)
     h2d, d2h = pipe.bytes_per_step()
+    # the same steps with the copies in line on the compute stream, for
+    # comparison (what the overlap saves)
+    dev_in = pipe.dev[0]
+
+    def serial_step(i):
+        for d, x in zip(dev_in, host_in[i % N_LAYERS]):
+            d.copy_(x, non_blocking=True)
+        o = head.forward(*dev_in, layers[i % N_LAYERS])
+        pipe.host_out.copy_(o, non_blocking=True)
+
+    serial_step(0)
+    serial_ms, _ = head.timer.run(serial_step, args.steps, 3)
 
     # host copies for the CPU baseline (layer 0, batch 0), taken before the
     # stack measurement below frees the rotating layers
@@ -1269,7 +1281,11 @@ def run_single(args, sbb, rank, world, local):
             "cpu_baseline": cpu_baseline,
             "e2e": {"value": world * T / (e2e_ms * 1e-3), "unit": "tokens/s",
                     "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": d2h,
-                    "ms_per_step": e2e_ms, "copies": CopyPipeline.DESCRIPTION},
+                    "ms_per_step": e2e_ms, "copies": CopyPipeline.DESCRIPTION,
+                    "serial_copies": {"value": world * T / (serial_ms * 1e-3),
+                                      "ms_per_step": serial_ms,
+                                      "copies": "in line on the compute stream before and "
+                                                "after each step"}},
             "gpu_launches": launches_per_step * args.steps,
             "device_errors": errors,
             "clocks": clocks,

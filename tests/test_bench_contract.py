@@ -64,6 +64,8 @@ def test_b200_arm_line(cuda):
     assert e["h2d_bytes_per_step"] == T * 4096 * 2 + T * 8 * 4 * 2
     assert e["d2h_bytes_per_step"] == T * 4096 * 2
     assert e["value"] > 0 and e["unit"] == "tokens/s"
+    # the copies overlap the neighbouring steps; the serial form is reported beside them
+    assert e["serial_copies"]["ms_per_step"] > 0
     assert line["gpu_launches"] > 0
     clk = line["clocks"]
     assert clk is not None and clk["sm_max_mhz"] > 0
